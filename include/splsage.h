@@ -1,0 +1,183 @@
+/*
+ * libsplsage: the C ABI of the B200 (sm_100a) SageAttention2 op.
+ *
+ * This is the drop-in boundary for the reference's `spl_nn::sage` Rust API
+ * (platform/spl-nn/src/sage/mod.rs).  Every entry point below names the
+ * reference item it replaces.  Conventions, carried over from the Rust API:
+ *
+ *   - every call that touches the GPU enqueues on the stream given to
+ *     spl_sage_create and returns without synchronising (mod.rs:509-510),
+ *     except spl_sage_status, which reads a device word back;
+ *   - the caller owns Q, K, V and the output (borrowed device pointers);
+ *     a workspace owns the quantised tensors (mod.rs:456-495);
+ *   - errors are checked before any launch and reported as a non-zero
+ *     status plus a thread-local message (spl_sage_last_error), the text of
+ *     the reference's `bail!` where one exists; nothing throws across the ABI;
+ *   - tensors are bf16 with channels contiguous; strides are in elements and
+ *     must be multiples of 8, the data pointer 16-byte aligned
+ *     (Strides::check, mod.rs:251-259).
+ *
+ * Extensions beyond the reference (which has neither): a KV head count for
+ * grouped-query attention and a causal mask.
+ */
+#ifndef SPLSAGE_H
+#define SPLSAGE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SPL_SAGE_OK 0
+#define SPL_SAGE_ERR_INVALID 1     /* bad argument, shape, stride or extent */
+#define SPL_SAGE_ERR_DEVICE 2      /* no usable sm_100 GPU */
+#define SPL_SAGE_ERR_CUDA 3        /* a CUDA runtime / driver call failed */
+#define SPL_SAGE_ERR_STATE 4       /* e.g. workspace not prepared */
+#define SPL_SAGE_ERR_KERNEL 5      /* a kernel reported a device-side error (spl_sage_status) */
+
+typedef struct spl_sage spl_sage;       /* SageAttention (mod.rs:511-520) */
+typedef struct spl_sage_ws spl_sage_ws; /* Workspace (mod.rs:458-477) */
+
+/* PvAccum (mod.rs:172-181). */
+#define SPL_SAGE_PV_F32 0
+#define SPL_SAGE_PV_F16 1
+
+/* Config (mod.rs:188-201) with its Tile (mod.rs:119-124).  The tile fields
+ * are validated as Tile::validate (mod.rs:158-167) does; the sm_100a kernel's
+ * CTA is fixed (128 query rows per CTA, 128-key blocks), so `stages` and
+ * the rest only have to be valid. */
+typedef struct {
+    uint32_t warps;
+    uint32_t m_tiles;
+    uint32_t stages;
+    int32_t pv_accum; /* SPL_SAGE_PV_F32 or SPL_SAGE_PV_F16 */
+} spl_sage_config;
+
+/* Shape (mod.rs:262-268), plus kv_heads (0 = heads) and causal. */
+typedef struct {
+    int64_t batch;
+    int64_t heads;
+    int64_t kv_heads;
+    int64_t tokens;
+    int32_t causal;
+    int32_t reserved;
+} spl_sage_shape;
+
+/* KvMerge + FrameLayout (mod.rs:273-311).  stride 0 or 1: KvMerge::Dense. */
+typedef struct {
+    int32_t stride;
+    int32_t reserved;
+    int64_t frames;
+    int64_t special;
+    int64_t grid_h;
+    int64_t grid_w;
+    int64_t dense_frames;
+} spl_sage_merge;
+
+/* Tensor / TensorMut (mod.rs:497-507) with Strides (mod.rs:203-260):
+ * data + its length in bf16 elements + [batch][token][head] strides. */
+typedef struct {
+    const void* data;
+    int64_t len;
+    int64_t batch;
+    int64_t token;
+    int64_t head;
+} spl_sage_tensor;
+
+typedef struct {
+    void* data;
+    int64_t len;
+    int64_t batch;
+    int64_t token;
+    int64_t head;
+} spl_sage_tensor_mut;
+
+/* Options (mod.rs:313-344).  qk_norm_params (device, f32 [4][head_dim]:
+ * q weight, q bias, k weight, k bias) may be NULL: no QK LayerNorm. */
+typedef struct {
+    float softmax_scale;       /* used when has_softmax_scale */
+    int32_t has_softmax_scale; /* 0: 1 / sqrt(head_dim) */
+    int32_t smooth_k;          /* default 1 */
+    int32_t smooth_v;          /* default 1 */
+    int32_t reserved;
+    const float* qk_norm_params;
+    int64_t qk_norm_len; /* floats available at qk_norm_params */
+    float qk_norm_eps;
+    int32_t reserved2;
+} spl_sage_options;
+
+/* Plan (mod.rs:391-454). */
+typedef struct {
+    int64_t tq_pad; /* queries rounded up to 128 */
+    int64_t tk;     /* keys after merging */
+    int64_t tk_pad; /* tk rounded up to 64 */
+} spl_sage_plan;
+
+/* Config::for_head_dim (mod.rs:195-200) and Options::default (mod.rs:326-335). */
+void spl_sage_default_config(int head_dim, spl_sage_config* out);
+void spl_sage_default_options(spl_sage_options* out);
+
+/* SageAttention::new / with_config (mod.rs:571-626): head_dim 64 or 128;
+ * cfg NULL = spl_sage_default_config.  stream is a cudaStream_t (NULL: the
+ * legacy default stream) on the current device, which must be sm_100. */
+int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_sage** out);
+void spl_sage_destroy(spl_sage* s);
+
+/* SageAttention::workspace (mod.rs:649-670) via Plan::new (mod.rs:405-440):
+ * allocates the quantised buffers (zeroed, on the engine's stream).  merge
+ * NULL = dense.  Causal with merging is rejected. */
+int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
+                              spl_sage_ws** out);
+void spl_sage_ws_destroy(spl_sage_ws* ws);
+/* Workspace::bytes (mod.rs:485-494) and Workspace::plan (mod.rs:480-482). */
+int64_t spl_sage_ws_bytes(const spl_sage_ws* ws);
+int spl_sage_ws_plan(const spl_sage_ws* ws, spl_sage_plan* out);
+
+/* SageAttention::prepare (mod.rs:673-836): quantise (and merge) q, k, v into
+ * ws.  Three launches.  opts NULL = spl_sage_default_options. */
+int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                     const spl_sage_options* opts);
+
+/* SageAttention::attend (mod.rs:840-886): attention over the prepared ws,
+ * bf16 into out. */
+int spl_sage_attend(spl_sage* s, const spl_sage_ws* ws, spl_sage_tensor_mut out);
+
+/* SageAttention::forward (mod.rs:889-900): prepare then attend. */
+int spl_sage_forward(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                     spl_sage_tensor_mut out, const spl_sage_options* opts);
+
+/* The quantised tensors in the reference's byte layout (the public fields
+ * of Workspace, mod.rs:461-474), for the bit-exact gate: device buffers of
+ *   q8 i8 [b][h][tq_pad][D], q_scale f32 [b][h][tq_pad/16],
+ *   k8 i8 [b][g][tk_pad][D], k_scale f32 [b][g][tk_pad/64],
+ *   v8 u8 [b][g][tk_pad/64][D][64] (E4M3, keys permuted within 16),
+ *   stats f32 [b][g][4][D], kbias f32 [tk_pad]   (g = kv heads).
+ * Any pointer may be NULL to skip it.  Stream-ordered copies. */
+int spl_sage_ws_export_reference_layout(spl_sage* s, const spl_sage_ws* ws, void* q8, float* q_scale, void* k8,
+                                        float* k_scale, void* v8, float* stats, float* kbias);
+
+/* Reads and clears the workspace's device error word (bounded-wait
+ * timeouts inside the kernels).  Synchronises the engine's stream.
+ * Returns SPL_SAGE_ERR_KERNEL when the word was non-zero. */
+int spl_sage_status(spl_sage* s, spl_sage_ws* ws, uint32_t* device_error_word);
+
+/* SageAttention::attn_resources (mod.rs:641-646): registers per thread and
+ * local (spill) bytes of the attention kernel. */
+int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes);
+
+/* flops (mod.rs:905-910): 4 * B * H * Tq * Tk * D of the workspace's plan. */
+double spl_sage_flops(const spl_sage_ws* ws);
+
+/* The last error message of this thread ("" when none). */
+const char* spl_sage_last_error(void);
+
+/* Library version string. */
+const char* spl_sage_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,323 @@
+"""ctypes/numpy front end of the CPU oracle (liboracle.so) and of the
+reference's own kernels built as a GPU oracle (oracle/_ref).
+
+TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference arm may use this module, as the checker; the
+product (libsplsage.so and its Python mirror) never imports it.
+
+What each function restates is documented in sage_oracle.h with the
+reference file:line it follows (platform/spl-nn/src/sage/reference.rs,
+platform/spl-nn/cuda/sage_quant.cu).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+QGROUP, QTILE, KBLOCK = 16, 128, 64
+LN_Q, LN_K, SMOOTH_K, SMOOTH_V = 1, 2, 4, 8
+FP8_MAX = 448.0
+PV16_V_RANGE = 2.25
+LOG2_E = np.float32(1.4426950408889634)
+
+
+class Geom(ctypes.Structure):
+    """or_geom of sage_oracle.h."""
+
+    _fields_ = [(n, ctypes.c_int64) for n in
+                ("q_sb", "q_st", "q_sh", "k_sb", "k_st", "k_sh", "v_sb", "v_st", "v_sh")] + [
+        (n, ctypes.c_int32) for n in
+        ("batch", "heads", "kv_heads", "tokens", "tq_pad", "tk", "tk_pad", "d", "merge", "frames",
+         "frame_tokens", "special", "grid_h", "grid_w", "merged_frame", "merged_w", "dense_frames",
+         "q_tiles", "flags", "pad0")] + [(n, ctypes.c_float) for n in ("q_mul", "ln_eps", "v_range", "pad1")]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} missing: run `make -C oracle`")
+        L = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        L.or_bf16_to_f32.restype = ctypes.c_float
+        L.or_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        L.or_f32_to_bf16.restype = ctypes.c_uint16
+        L.or_f32_to_bf16.argtypes = [ctypes.c_float]
+        L.or_e4m3_to_f32.restype = ctypes.c_float
+        L.or_e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        L.or_f32_to_e4m3.restype = ctypes.c_uint8
+        L.or_f32_to_e4m3.argtypes = [ctypes.c_float]
+        L.or_vpos.restype = ctypes.c_int
+        L.or_vpos.argtypes = [ctypes.c_int]
+        L.or_rng_next.restype = ctypes.c_uint64
+        L.or_rng_next.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+        L.or_rng_normal.restype = ctypes.c_float
+        L.or_rng_normal.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+        L.or_rng_normals.argtypes = [ctypes.POINTER(ctypes.c_uint64), P, ctypes.c_int64, ctypes.c_float,
+                                     ctypes.c_float]
+        L.or_synthetic.argtypes = [ctypes.c_int] * 4 + [ctypes.c_uint64, P, P, P]
+        L.or_members.restype = ctypes.c_int
+        L.or_members.argtypes = [ctypes.POINTER(Geom), ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                 ctypes.POINTER(ctypes.c_int)]
+        L.or_prepare.argtypes = [P] * 12 + [ctypes.POINTER(Geom)]
+        L.or_prep.argtypes = [P] * 7 + [ctypes.POINTER(Geom)]
+        L.or_finalize.argtypes = [P, P, ctypes.POINTER(Geom)]
+        L.or_quant_kv.argtypes = [P] * 8 + [ctypes.POINTER(Geom)]
+        L.or_attention_f64.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                       ctypes.c_int, ctypes.c_int, P]
+        L.or_attention_bthd.restype = ctypes.c_int
+        L.or_attention_bthd.argtypes = [P, P, P, ctypes.POINTER(Geom), ctypes.c_float, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+        L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom), ctypes.c_int, ctypes.c_int, P]
+        L.or_layer_norm.argtypes = [P, P, P, ctypes.c_int, ctypes.c_float]
+        L.or_errors.argtypes = [P, P, ctypes.c_int64, P]
+        L.or_flops.restype = ctypes.c_double
+        L.or_flops.argtypes = [ctypes.c_int] * 5
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---------------------------------------------------------------- codecs
+
+def bf16_to_f32(b):
+    b = np.asarray(b, dtype=np.uint16)
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(x):
+    """reference.rs:13-20, vectorised."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    bits = x.view(np.uint32)
+    rnd = np.uint32(0x7FFF) + ((bits >> 16) & 1)
+    out = ((bits + rnd) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = ((bits[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
+
+
+_E4M3_TABLE = None
+
+
+def e4m3_table() -> np.ndarray:
+    global _E4M3_TABLE
+    if _E4M3_TABLE is None:
+        _E4M3_TABLE = np.array([lib().or_e4m3_to_f32(i) for i in range(256)], dtype=np.float32)
+    return _E4M3_TABLE
+
+
+def e4m3_to_f32(b):
+    return e4m3_table()[np.asarray(b, dtype=np.uint8)]
+
+
+def f32_to_e4m3(x: float) -> int:
+    return int(lib().or_f32_to_e4m3(float(x)))
+
+
+def vpos(k: int) -> int:
+    return int(lib().or_vpos(k))
+
+
+# ---------------------------------------------------------------- RNG / data
+
+class Rng:
+    """SplitMix64 + Box-Muller (reference.rs:228-254)."""
+
+    def __init__(self, seed: int):
+        self.s = ctypes.c_uint64(seed)
+
+    def next_u64(self) -> int:
+        return int(lib().or_rng_next(ctypes.byref(self.s)))
+
+    def normal(self) -> float:
+        return float(lib().or_rng_normal(ctypes.byref(self.s)))
+
+    def normals(self, n: int, std: float = 1.0, mean: float = 0.0) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        lib().or_rng_normals(ctypes.byref(self.s), _p(out), n, std, mean)
+        return out
+
+
+def synthetic(batch: int, heads: int, tokens: int, d: int, seed: int):
+    """Data::synthetic (tests.rs:300-329): bf16 bits [b][t][h][d] each."""
+    shape = (batch, tokens, heads, d)
+    q = np.empty(shape, np.uint16)
+    k = np.empty(shape, np.uint16)
+    v = np.empty(shape, np.uint16)
+    lib().or_synthetic(batch, heads, tokens, d, seed, _p(q), _p(k), _p(v))
+    return q, k, v
+
+
+# ---------------------------------------------------------------- geometry
+
+@dataclass
+class Layout:
+    """FrameLayout (mod.rs:273-300)."""
+    frames: int
+    special: int
+    grid_h: int
+    grid_w: int
+    dense_frames: int = 0
+
+    def tokens_per_frame(self) -> int:
+        return self.special + self.grid_h * self.grid_w
+
+    def merged_per_frame(self, s: int) -> int:
+        return self.special + -(-self.grid_h // s) * -(-self.grid_w // s)
+
+    def merged_keys(self, s: int) -> int:
+        d = min(self.dense_frames, self.frames)
+        return d * self.tokens_per_frame() + (self.frames - d) * self.merged_per_frame(s)
+
+
+def make_geom(batch, heads, kv_heads, tokens, d, strides_q, strides_k, strides_v, *, flags=SMOOTH_K | SMOOTH_V,
+              softmax_scale=None, merge: int = 1, layout: Layout | None = None, ln_eps=1e-5,
+              v_range=FP8_MAX) -> Geom:
+    g = Geom()
+    g.q_sb, g.q_st, g.q_sh = strides_q
+    g.k_sb, g.k_st, g.k_sh = strides_k
+    g.v_sb, g.v_st, g.v_sh = strides_v
+    g.batch, g.heads, g.kv_heads, g.tokens, g.d = batch, heads, kv_heads, tokens, d
+    g.tq_pad = -(-tokens // QTILE) * QTILE
+    if merge > 1:
+        lay = layout
+        g.tk = lay.merged_keys(merge)
+        g.frames, g.special, g.grid_h, g.grid_w = lay.frames, lay.special, lay.grid_h, lay.grid_w
+        g.dense_frames = min(lay.dense_frames, lay.frames)
+        g.frame_tokens = lay.tokens_per_frame()
+        g.merged_frame = lay.merged_per_frame(merge)
+        g.merged_w = -(-lay.grid_w // merge)
+    else:
+        g.tk = tokens
+        g.frames = 1
+    g.merge = merge
+    g.tk_pad = -(-g.tk // KBLOCK) * KBLOCK
+    g.q_tiles = g.tq_pad // QTILE
+    g.flags = flags
+    scale = np.float32(1.0) / np.sqrt(np.float32(d)) if softmax_scale is None else np.float32(softmax_scale)
+    g.q_mul = float(np.float32(scale) * LOG2_E)
+    g.ln_eps = ln_eps
+    g.v_range = v_range
+    return g
+
+
+def bthd_strides(tokens, heads, d):
+    return (tokens * heads * d, heads * d, d)
+
+
+def members(g: Geom, j: int):
+    base, nx = ctypes.c_int(), ctypes.c_int()
+    n = lib().or_members(ctypes.byref(g), j, ctypes.byref(base), ctypes.byref(nx))
+    return [base.value + (m // nx.value) * g.grid_w + m % nx.value for m in range(n)]
+
+
+# ---------------------------------------------------------------- quantiser
+
+@dataclass
+class Quant:
+    q8: np.ndarray
+    q_scale: np.ndarray
+    k8: np.ndarray
+    k_scale: np.ndarray
+    v8: np.ndarray  # reference layout [b][hkv][tk_pad/64][d][64], keys permuted
+    stats: np.ndarray
+    kbias: np.ndarray
+    part: np.ndarray
+
+
+def prepare(q, k, v, g: Geom, ln: np.ndarray | None = None) -> Quant:
+    """SageAttention::prepare on the CPU, bit-exact with sage_quant.cu."""
+    b, hq, hkv, d = g.batch, g.heads, g.kv_heads, g.d
+    out = Quant(
+        q8=np.zeros((b, hq, g.tq_pad, d), np.int8),
+        q_scale=np.zeros((b, hq, g.tq_pad // QGROUP), np.float32),
+        k8=np.zeros((b, hkv, g.tk_pad, d), np.int8),
+        k_scale=np.zeros((b, hkv, g.tk_pad // KBLOCK), np.float32),
+        v8=np.zeros((b, hkv, g.tk_pad // KBLOCK, d, KBLOCK), np.uint8),
+        stats=np.zeros((b, hkv, 4, d), np.float32),
+        kbias=np.zeros(g.tk_pad, np.float32),
+        part=np.zeros((b, hkv, g.q_tiles, 4, d), np.float32),
+    )
+    lnp = None if ln is None else np.ascontiguousarray(ln, np.float32)
+    lib().or_prepare(_p(np.ascontiguousarray(q)), _p(np.ascontiguousarray(k)), _p(np.ascontiguousarray(v)),
+                     _p(lnp), _p(out.q8), _p(out.q_scale), _p(out.k8), _p(out.k_scale), _p(out.v8), _p(out.stats),
+                     _p(out.kbias), _p(out.part), ctypes.byref(g))
+    return out
+
+
+def attention_bthd(q, k, v, g: Geom, *, causal=False, rows=None, nthreads=None, scale=None) -> np.ndarray:
+    """f64 exact attention over bf16 [b][t][h][d] inputs (reference.rs:148-184,
+    with the causal mask and GQA head mapping as extensions).  Returns f32
+    [b][t][hq][d]; only `rows` (a (start, stop) range) are computed."""
+    out = np.zeros((g.batch, g.tokens, g.heads, g.d), np.float32)
+    r0, r1 = rows if rows is not None else (0, g.tokens)
+    sc = np.float32(1.0) / np.sqrt(np.float32(g.d)) if scale is None else np.float32(scale)
+    lib().or_attention_bthd(_p(np.ascontiguousarray(q)), _p(np.ascontiguousarray(k)), _p(np.ascontiguousarray(v)),
+                            ctypes.byref(g), float(sc), int(causal), r0, r1, nthreads or os.cpu_count() or 1,
+                            _p(out))
+    return out
+
+
+def sage_emulate(qt: Quant, g: Geom, *, causal=False, nthreads=None) -> np.ndarray:
+    out = np.zeros((g.batch, g.tokens, g.heads, g.d), np.float32)
+    lib().or_sage_emulate(_p(qt.q8), _p(qt.q_scale), _p(qt.k8), _p(qt.k_scale), _p(qt.v8), _p(qt.stats),
+                          _p(qt.kbias), ctypes.byref(g), int(causal), nthreads or os.cpu_count() or 1, _p(out))
+    return out
+
+
+def errors(ours, ref) -> dict:
+    a = np.ascontiguousarray(ours, np.float32).ravel()
+    r = np.ascontiguousarray(ref, np.float32).ravel()
+    o = np.zeros(5, np.float64)
+    lib().or_errors(_p(a), _p(r), a.size, _p(o))
+    return dict(cos=o[0], rel_l1=o[1], rel_l2=o[2], max_abs=o[3], ref_max=o[4])
+
+
+def flops(batch, heads, tq, tk, d) -> float:
+    return 4.0 * batch * heads * tq * tk * d
+
+
+def causal_flops(batch, heads, n, d) -> float:
+    return 4.0 * batch * heads * d * n * (n + 1) / 2
+
+
+# ---------------------------------------------------------------- reference GPU oracle
+
+_ref_libs: dict[int, ctypes.CDLL] = {}
+
+
+def ref_available(d: int) -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", f"libsage_ref_d{d}.so"))
+
+
+def ref_lib(d: int) -> ctypes.CDLL:
+    if d not in _ref_libs:
+        L = ctypes.CDLL(os.path.join(HERE, "_ref", f"libsage_ref_d{d}.so"))
+        P = ctypes.c_void_p
+        L.ref_sage_run.restype = ctypes.c_int
+        L.ref_sage_run.argtypes = [P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float] + [P] * 10
+        L.ref_sage_attend.restype = ctypes.c_int
+        L.ref_sage_attend.argtypes = [P, P, ctypes.c_float, ctypes.c_float] + [P] * 9
+        _ref_libs[d] = L
+    return _ref_libs[d]
+
+
+def ref_dims(g: Geom) -> np.ndarray:
+    return np.array([g.batch, g.heads, g.tokens, g.merge, g.frames, g.special, g.grid_h, g.grid_w,
+                     g.dense_frames, g.flags], np.int32)

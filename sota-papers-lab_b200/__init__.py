@@ -1,0 +1,412 @@
+"""Python mirror of the reference's `spl_nn::sage` API over libsplsage.so.
+
+The reference (platform/spl-nn/src/sage/mod.rs) is a Rust API; this module
+binds the same types and calls to the C ABI in include/splsage.h so the
+tests and the benchmark read like the reference's own tests:
+
+    sage = SageAttention(stream, head_dim=128)            # SageAttention::new
+    ws = sage.workspace(Shape(batch, heads, tokens), KvMerge.dense())
+    sage.prepare(ws, Tensor(q, strides), Tensor(k, strides), Tensor(v, strides), Options())
+    sage.attend(ws, TensorMut(out, Strides.bthd(tokens, heads, d)))
+
+Tensors are torch CUDA tensors (bf16 storage, channels contiguous) viewed
+through element strides, exactly as the Rust `Tensor { data, strides }`.
+There is no CPU fallback: every call goes to the sm_100a kernels, and the
+module refuses to load without the built library.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+
+__all__ = [
+    "QGROUP", "QTILE", "KBLOCK", "FP8_MAX", "PV16_V_RANGE", "SageError", "Tile", "PvAccum", "Config", "Strides",
+    "Shape", "FrameLayout", "KvMerge", "Options", "QkNorm", "Plan", "Tensor", "TensorMut", "Workspace",
+    "SageAttention", "flops", "library_path",
+]
+
+QGROUP = 16      # mod.rs:71
+QTILE = 128      # mod.rs:73
+KBLOCK = 64      # mod.rs:75
+FP8_MAX = 448.0  # mod.rs:77
+PV16_V_RANGE = 2.25  # mod.rs:185
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def library_path() -> str:
+    return os.path.join(_HERE, "libsplsage.so")
+
+
+class SageError(RuntimeError):
+    """A non-zero status from libsplsage, with its message."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+# ---------------------------------------------------------------- C structs
+
+class _Config(ctypes.Structure):
+    _fields_ = [("warps", ctypes.c_uint32), ("m_tiles", ctypes.c_uint32), ("stages", ctypes.c_uint32),
+                ("pv_accum", ctypes.c_int32)]
+
+
+class _Shape(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64),
+                ("tokens", ctypes.c_int64), ("causal", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class _Merge(ctypes.Structure):
+    _fields_ = [("stride", ctypes.c_int32), ("reserved", ctypes.c_int32), ("frames", ctypes.c_int64),
+                ("special", ctypes.c_int64), ("grid_h", ctypes.c_int64), ("grid_w", ctypes.c_int64),
+                ("dense_frames", ctypes.c_int64)]
+
+
+class _Tensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("len", ctypes.c_int64), ("batch", ctypes.c_int64),
+                ("token", ctypes.c_int64), ("head", ctypes.c_int64)]
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [("softmax_scale", ctypes.c_float), ("has_softmax_scale", ctypes.c_int32),
+                ("smooth_k", ctypes.c_int32), ("smooth_v", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("qk_norm_params", ctypes.c_void_p), ("qk_norm_len", ctypes.c_int64),
+                ("qk_norm_eps", ctypes.c_float), ("reserved2", ctypes.c_int32)]
+
+
+class _Plan(ctypes.Structure):
+    _fields_ = [("tq_pad", ctypes.c_int64), ("tk", ctypes.c_int64), ("tk_pad", ctypes.c_int64)]
+
+
+EXPORTS = [
+    "spl_sage_default_config", "spl_sage_default_options", "spl_sage_create", "spl_sage_destroy",
+    "spl_sage_workspace_create", "spl_sage_ws_destroy", "spl_sage_ws_bytes", "spl_sage_ws_plan", "spl_sage_prepare",
+    "spl_sage_attend", "spl_sage_forward", "spl_sage_ws_export_reference_layout", "spl_sage_status",
+    "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version",
+]
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libsplsage.so (fails loudly if it was not built)."""
+    global _lib
+    if _lib is None:
+        path = library_path()
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: build it with `make -C sota-papers-lab_b200/csrc` "
+                               "(or __graft_entry__.build()); there is no fallback implementation")
+        L = ctypes.CDLL(path)
+        P, I = ctypes.c_void_p, ctypes.c_int
+        L.spl_sage_default_config.argtypes = [I, ctypes.POINTER(_Config)]
+        L.spl_sage_default_options.argtypes = [ctypes.POINTER(_Options)]
+        L.spl_sage_create.argtypes = [P, I, ctypes.POINTER(_Config), ctypes.POINTER(P)]
+        L.spl_sage_destroy.argtypes = [P]
+        L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
+        L.spl_sage_ws_destroy.argtypes = [P]
+        L.spl_sage_ws_bytes.restype = ctypes.c_int64
+        L.spl_sage_ws_bytes.argtypes = [P]
+        L.spl_sage_ws_plan.argtypes = [P, ctypes.POINTER(_Plan)]
+        L.spl_sage_prepare.argtypes = [P, P, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options)]
+        L.spl_sage_attend.argtypes = [P, P, _Tensor]
+        L.spl_sage_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options)]
+        L.spl_sage_ws_export_reference_layout.argtypes = [P] * 9
+        L.spl_sage_status.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint32)]
+        L.spl_sage_attn_resources.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.spl_sage_flops.restype = ctypes.c_double
+        L.spl_sage_flops.argtypes = [P]
+        L.spl_sage_last_error.restype = ctypes.c_char_p
+        L.spl_sage_version.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise SageError(rc, lib().spl_sage_last_error().decode())
+
+
+# ---------------------------------------------------------------- types (mod.rs)
+
+@dataclass(frozen=True)
+class Tile:
+    """CTA shape of the reference kernel (mod.rs:119-168); validated, and kept
+    for drop-in compatibility (the sm_100a kernel's CTA is fixed)."""
+    warps: int = 4
+    m_tiles: int = 2
+    stages: int = 3
+
+    @staticmethod
+    def for_head_dim(head_dim: int) -> "Tile":
+        return Tile(4, 1, 3) if head_dim > 64 else Tile(4, 2, 3)
+
+    def rows(self) -> int:
+        return 16 * self.m_tiles * self.warps
+
+
+class PvAccum:
+    """mod.rs:172-181."""
+    F32 = 0
+    F16 = 1
+
+
+@dataclass(frozen=True)
+class Config:
+    tile: Tile
+    pv_accum: int = PvAccum.F32
+
+    @staticmethod
+    def for_head_dim(head_dim: int) -> "Config":
+        return Config(Tile.for_head_dim(head_dim), PvAccum.F32)
+
+
+@dataclass(frozen=True)
+class Strides:
+    """Element strides of a [batch][token][head][dim] bf16 view (mod.rs:203-260)."""
+    batch: int
+    token: int
+    head: int
+
+    @staticmethod
+    def bthd(tokens: int, heads: int, head_dim: int) -> "Strides":
+        return Strides(tokens * heads * head_dim, heads * head_dim, head_dim)
+
+    @staticmethod
+    def bhtd(tokens: int, heads: int, head_dim: int) -> "Strides":
+        return Strides(heads * tokens * head_dim, head_dim, tokens * head_dim)
+
+    @staticmethod
+    def packed_qkv(tokens: int, heads: int, head_dim: int) -> "Strides":
+        return Strides(tokens * 3 * heads * head_dim, 3 * heads * head_dim, head_dim)
+
+    def extent(self, shape: "Shape", head_dim: int, heads: int | None = None) -> int:
+        h = shape.heads if heads is None else heads
+        return (shape.batch - 1) * self.batch + (shape.tokens - 1) * self.token + (h - 1) * self.head + head_dim
+
+
+@dataclass(frozen=True)
+class Shape:
+    """mod.rs:262-268, plus kv_heads (GQA) and causal (extensions)."""
+    batch: int
+    heads: int
+    tokens: int
+    kv_heads: int = 0
+    causal: bool = False
+
+    @property
+    def kv(self) -> int:
+        return self.kv_heads or self.heads
+
+
+@dataclass(frozen=True)
+class FrameLayout:
+    """mod.rs:273-300."""
+    frames: int
+    special: int
+    grid_h: int
+    grid_w: int
+    dense_frames: int = 0
+
+    def tokens_per_frame(self) -> int:
+        return self.special + self.grid_h * self.grid_w
+
+    def merged_per_frame(self, stride: int) -> int:
+        return self.special + -(-self.grid_h // stride) * -(-self.grid_w // stride)
+
+    def merged_keys(self, stride: int) -> int:
+        d = min(self.dense_frames, self.frames)
+        return d * self.tokens_per_frame() + (self.frames - d) * self.merged_per_frame(stride)
+
+
+@dataclass(frozen=True)
+class KvMerge:
+    """KvMerge::Dense or KvMerge::Pool { stride, layout } (mod.rs:302-311)."""
+    stride: int = 1
+    layout: FrameLayout | None = None
+
+    @staticmethod
+    def dense() -> "KvMerge":
+        return KvMerge(1, None)
+
+    @staticmethod
+    def pool(stride: int, layout: FrameLayout) -> "KvMerge":
+        return KvMerge(stride, layout)
+
+
+@dataclass
+class QkNorm:
+    """QK LayerNorm parameters: a CUDA f32 tensor [4][head_dim] (q w, q b, k w, k b)."""
+    params: object
+    eps: float = 1e-5
+
+
+@dataclass
+class Options:
+    """mod.rs:313-335 (smoothing on by default)."""
+    softmax_scale: float | None = None
+    smooth_k: bool = True
+    smooth_v: bool = True
+    qk_norm: QkNorm | None = None
+
+    def _c(self) -> _Options:
+        o = _Options()
+        lib().spl_sage_default_options(ctypes.byref(o))
+        if self.softmax_scale is not None:
+            o.softmax_scale = float(self.softmax_scale)
+            o.has_softmax_scale = 1
+        o.smooth_k = int(bool(self.smooth_k))
+        o.smooth_v = int(bool(self.smooth_v))
+        if self.qk_norm is not None:
+            p = self.qk_norm.params
+            o.qk_norm_params = p.data_ptr()
+            o.qk_norm_len = p.numel()
+            o.qk_norm_eps = float(self.qk_norm.eps)
+        return o
+
+
+@dataclass(frozen=True)
+class Plan:
+    """mod.rs:391-454."""
+    shape: Shape
+    merge: KvMerge
+    tq_pad: int
+    tk: int
+    tk_pad: int
+
+
+@dataclass
+class Tensor:
+    """A bf16 tensor view: torch CUDA tensor (any dtype of 2 bytes) + element strides.
+    The view starts at data's first element."""
+    data: object
+    strides: Strides
+
+    def _c(self) -> _Tensor:
+        t = self.data
+        if t.element_size() != 2:
+            raise SageError(1, "sage tensors hold bf16 (2-byte) elements")
+        return _Tensor(t.data_ptr(), t.numel(), self.strides.batch, self.strides.token, self.strides.head)
+
+
+TensorMut = Tensor
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+class Workspace:
+    """Device buffers of one Plan (mod.rs:456-495); owned by the library."""
+
+    def __init__(self, handle: int, plan: Plan, head_dim: int):
+        self._h = ctypes.c_void_p(handle)
+        self.plan = plan
+        self.head_dim = head_dim
+
+    def bytes(self) -> int:
+        return int(lib().spl_sage_ws_bytes(self._h))
+
+    def close(self):
+        if self._h:
+            lib().spl_sage_ws_destroy(self._h)
+            self._h = ctypes.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SageAttention:
+    """SageAttention (mod.rs:509-901) on one CUDA stream."""
+
+    def __init__(self, stream=None, head_dim: int = 64, config: Config | None = None):
+        cfg = config or Config.for_head_dim(head_dim)
+        c = _Config(cfg.tile.warps, cfg.tile.m_tiles, cfg.tile.stages, cfg.pv_accum)
+        h = ctypes.c_void_p()
+        _check(lib().spl_sage_create(ctypes.c_void_p(_stream_ptr(stream)), head_dim, ctypes.byref(c),
+                                     ctypes.byref(h)))
+        self._h = h
+        self.head_dim = head_dim
+        self.config = cfg
+        self.stream = stream
+
+    @staticmethod
+    def new(stream, head_dim: int) -> "SageAttention":
+        return SageAttention(stream, head_dim)
+
+    @staticmethod
+    def with_config(stream, head_dim: int, config: Config) -> "SageAttention":
+        return SageAttention(stream, head_dim, config)
+
+    def close(self):
+        if self._h:
+            lib().spl_sage_destroy(self._h)
+            self._h = ctypes.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def attn_resources(self) -> tuple[int, int]:
+        r, s = ctypes.c_int(), ctypes.c_int()
+        _check(lib().spl_sage_attn_resources(self._h, ctypes.byref(r), ctypes.byref(s)))
+        return r.value, s.value
+
+    def workspace(self, shape: Shape, merge: KvMerge | None = None) -> Workspace:
+        merge = merge or KvMerge.dense()
+        cs = _Shape(shape.batch, shape.heads, shape.kv_heads, shape.tokens, int(shape.causal), 0)
+        cm = _Merge()
+        if merge.stride > 1:
+            lay = merge.layout
+            cm = _Merge(merge.stride, 0, lay.frames, lay.special, lay.grid_h, lay.grid_w, lay.dense_frames)
+        h = ctypes.c_void_p()
+        _check(lib().spl_sage_workspace_create(self._h, ctypes.byref(cs), ctypes.byref(cm), ctypes.byref(h)))
+        p = _Plan()
+        _check(lib().spl_sage_ws_plan(h, ctypes.byref(p)))
+        return Workspace(h.value, Plan(shape, merge, p.tq_pad, p.tk, p.tk_pad), self.head_dim)
+
+    def prepare(self, ws: Workspace, q: Tensor, k: Tensor, v: Tensor, opts: Options | None = None):
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_prepare(self._h, ws._h, q._c(), k._c(), v._c(), ctypes.byref(o)))
+
+    def attend(self, ws: Workspace, out: Tensor):
+        _check(lib().spl_sage_attend(self._h, ws._h, out._c()))
+
+    def forward(self, ws: Workspace, q: Tensor, k: Tensor, v: Tensor, out: Tensor, opts: Options | None = None):
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_forward(self._h, ws._h, q._c(), k._c(), v._c(), out._c(), ctypes.byref(o)))
+
+    def export_reference_layout(self, ws: Workspace, q8=None, q_scale=None, k8=None, k_scale=None, v8=None,
+                                stats=None, kbias=None):
+        """Copies the quantised tensors, in the reference's byte layout, into
+        the given CUDA tensors (any may be None)."""
+        ptr = (lambda t: None if t is None else ctypes.c_void_p(t.data_ptr()))
+        _check(lib().spl_sage_ws_export_reference_layout(self._h, ws._h, ptr(q8), ptr(q_scale), ptr(k8),
+                                                         ptr(k_scale), ptr(v8), ptr(stats), ptr(kbias)))
+
+    def status(self, ws: Workspace) -> int:
+        """Reads (and clears) the device error word; raises on a kernel error."""
+        w = ctypes.c_uint32()
+        _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
+        return w.value
+
+
+def flops(plan: Plan, head_dim: int) -> float:
+    """mod.rs:905-910: 4 * B * H * Tq * Tk * D."""
+    return 4.0 * plan.shape.batch * plan.shape.heads * plan.shape.tokens * plan.tk * head_dim
+
+
+def causal_flops(batch: int, heads: int, n: int, head_dim: int) -> float:
+    """Algorithmic FLOPs of causal attention: 4 * B * H * D * N (N + 1) / 2."""
+    return 4.0 * batch * heads * head_dim * n * (n + 1) / 2

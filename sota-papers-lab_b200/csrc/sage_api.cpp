@@ -1,0 +1,450 @@
+// C ABI of libsplsage (include/splsage.h): the host side of the spl_nn::sage
+// op (platform/spl-nn/src/sage/mod.rs) for sm_100a.  Validation mirrors the
+// reference's checks and error texts; all GPU work is stream-ordered.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/splsage.h"
+#include "sage_kernels.h"
+
+namespace {
+
+constexpr int QGROUP = 16, QTILE = 128, KBLOCK = 64;
+constexpr float FP8_MAX = 448.0f;       // mod.rs:77
+constexpr float PV16_V_RANGE = 2.25f;   // mod.rs:185
+constexpr int LN_Q = 1, LN_K = 2, SMOOTH_K = 4, SMOOTH_V = 8;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(SPL_SAGE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+// A 3-D UINT8 tensor map {d0, d1, d2} with row pitch p1 and slab pitch p2
+// (bytes), box {b0, b1, 1}, zero fill out of bounds.
+int make_map(CUtensorMap* m, void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t p1, uint64_t p2,
+             uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {p1, p2};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t elem[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, elem,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SPL_SAGE_OK;
+}
+
+bool fits_i32(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
+
+}  // namespace
+
+struct spl_sage {
+    cudaStream_t stream;
+    int head_dim;
+    spl_sage_config config;
+    int device;
+};
+
+struct spl_sage_ws {
+    int head_dim;
+    spl_sage_shape shape;
+    spl_sage_merge merge;
+    int64_t tq_pad, tk, tk_pad;
+    int device;
+    void* mem;
+    size_t bytes;
+    sp::Buffers buf;
+    sp::AttnMaps maps;
+    sp::Geom geom;
+    bool prepared;
+};
+
+extern "C" {
+
+const char* spl_sage_last_error(void) { return g_last_error.c_str(); }
+
+const char* spl_sage_version(void) { return "splsage 0.1 sm_100a"; }
+
+void spl_sage_default_config(int head_dim, spl_sage_config* out) {
+    if (!out) return;
+    // Tile::DEFAULT / Tile::D128 (mod.rs:128-140), FP32 PV.
+    out->warps = 4;
+    out->m_tiles = head_dim > 64 ? 1 : 2;
+    out->stages = 3;
+    out->pv_accum = SPL_SAGE_PV_F32;
+}
+
+void spl_sage_default_options(spl_sage_options* out) {
+    if (!out) return;
+    memset(out, 0, sizeof *out);
+    out->smooth_k = 1;
+    out->smooth_v = 1;
+    out->qk_norm_eps = 1e-5f;
+}
+
+int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_sage** out) {
+    if (!out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_create: out is NULL");
+    *out = nullptr;
+    if (head_dim != 64 && head_dim != 128)
+        return fail(SPL_SAGE_ERR_INVALID, "sage attention supports head dim 64 or 128, got %d", head_dim);
+    spl_sage_config c;
+    if (cfg)
+        c = *cfg;
+    else
+        spl_sage_default_config(head_dim, &c);
+    const uint32_t rows = 16 * c.m_tiles * c.warps;
+    if (!(c.warps == 2 || c.warps == 4 || c.warps == 8) || !(c.m_tiles == 1 || c.m_tiles == 2 || c.m_tiles == 4) ||
+        c.stages < 2 || c.stages > 6 || QTILE % rows != 0)
+        return fail(SPL_SAGE_ERR_INVALID, "unsupported sage tile Tile { warps: %u, m_tiles: %u, stages: %u }",
+                    c.warps, c.m_tiles, c.stages);
+    if (c.pv_accum != SPL_SAGE_PV_F32 && c.pv_accum != SPL_SAGE_PV_F16)
+        return fail(SPL_SAGE_ERR_INVALID, "unknown PV accumulation %d", c.pv_accum);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+        return fail(SPL_SAGE_ERR_DEVICE,
+                    "sage attention needs an sm_100 GPU (B200: tcgen05 tensor cores, compute capability 10.0); "
+                    "this GPU is %d.%d",
+                    major, minor);
+    spl_sage* s = new spl_sage;
+    s->stream = (cudaStream_t)stream;
+    s->head_dim = head_dim;
+    s->config = c;
+    s->device = dev;
+    *out = s;
+    return SPL_SAGE_OK;
+}
+
+void spl_sage_destroy(spl_sage* s) { delete s; }
+
+int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
+                              spl_sage_ws** out) {
+    if (!s || !shape || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_workspace_create: NULL argument");
+    *out = nullptr;
+    spl_sage_shape sh = *shape;
+    if (sh.kv_heads == 0) sh.kv_heads = sh.heads;
+    if (sh.batch <= 0 || sh.heads <= 0 || sh.tokens <= 0 || sh.kv_heads <= 0)
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "empty attention shape Shape { batch: %lld, heads: %lld, kv_heads: %lld, tokens: %lld }",
+                    (long long)sh.batch, (long long)sh.heads, (long long)sh.kv_heads, (long long)sh.tokens);
+    if (sh.heads % sh.kv_heads != 0)
+        return fail(SPL_SAGE_ERR_INVALID, "heads (%lld) must be a multiple of kv_heads (%lld)", (long long)sh.heads,
+                    (long long)sh.kv_heads);
+    spl_sage_merge mg;
+    memset(&mg, 0, sizeof mg);
+    if (merge) mg = *merge;
+    if (mg.stride <= 1) {
+        memset(&mg, 0, sizeof mg);
+        mg.stride = 1;
+    }
+    int64_t tk = sh.tokens;
+    if (mg.stride > 1) {
+        if (mg.stride != 2 && mg.stride != 4)
+            return fail(SPL_SAGE_ERR_INVALID, "KV merge stride must be 2 or 4, got %d", mg.stride);
+        if (mg.grid_h <= 0 || mg.grid_w <= 0)
+            return fail(SPL_SAGE_ERR_INVALID, "KV merge needs a patch grid");
+        if (mg.frames < 0 || mg.special < 0 || mg.dense_frames < 0)
+            return fail(SPL_SAGE_ERR_INVALID, "negative frame layout field");
+        const int64_t per = mg.special + mg.grid_h * mg.grid_w;
+        if (mg.frames * per != sh.tokens)
+            return fail(SPL_SAGE_ERR_INVALID, "frame layout covers %lld tokens, the sequence has %lld",
+                        (long long)(mg.frames * per), (long long)sh.tokens);
+        if (sh.causal) return fail(SPL_SAGE_ERR_INVALID, "causal attention over merged keys is not defined");
+        const int64_t s_ = mg.stride;
+        const int64_t merged = mg.special + ((mg.grid_h + s_ - 1) / s_) * ((mg.grid_w + s_ - 1) / s_);
+        const int64_t d = mg.dense_frames < mg.frames ? mg.dense_frames : mg.frames;
+        tk = d * per + (mg.frames - d) * merged;
+    }
+    const int64_t tq_pad = (sh.tokens + QTILE - 1) / QTILE * QTILE;
+    const int64_t tk_pad = (tk + KBLOCK - 1) / KBLOCK * KBLOCK;
+    if (!fits_i32(tq_pad)) return fail(SPL_SAGE_ERR_INVALID, "padded queries = %lld does not fit in i32", (long long)tq_pad);
+    if (!fits_i32(tk_pad)) return fail(SPL_SAGE_ERR_INVALID, "padded keys = %lld does not fit in i32", (long long)tk_pad);
+    if (!fits_i32(sh.batch * sh.heads))
+        return fail(SPL_SAGE_ERR_INVALID, "batch x heads = %lld does not fit in i32", (long long)(sh.batch * sh.heads));
+    if (tq_pad / 128 > 65535) return fail(SPL_SAGE_ERR_INVALID, "too many query tiles (%lld)", (long long)(tq_pad / 128));
+
+    const int64_t D = s->head_dim, B = sh.batch, H = sh.heads, G = sh.kv_heads;
+    const int64_t q_tiles = tq_pad / QTILE;
+    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t n_q8 = up(B * H * tq_pad * D), n_qs = up(B * H * (tq_pad / QGROUP) * 4);
+    const size_t n_k8 = up(B * G * tk_pad * D), n_ks = up(B * G * (tk_pad / KBLOCK) * 4);
+    const size_t n_v8 = up(B * G * tk_pad * D), n_st = up(B * G * 4 * D * 4);
+    const size_t n_kb = up(tk_pad * 4), n_part = up(B * G * q_tiles * 4 * D * 4), n_err = 256;
+    const size_t total = n_q8 + n_qs + n_k8 + n_ks + n_v8 + n_st + n_kb + n_part + n_err;
+
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != s->device)
+        return fail(SPL_SAGE_ERR_INVALID, "workspace created on device %d, the engine is on device %d", dev, s->device);
+    void* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, total);
+    if (e != cudaSuccess) return cuda_fail(e, "allocate sage workspace");
+    e = cudaMemsetAsync(mem, 0, total, s->stream);
+    if (e != cudaSuccess) {
+        cudaFree(mem);
+        return cuda_fail(e, "zero sage workspace");
+    }
+    spl_sage_ws* ws = new spl_sage_ws;
+    memset(ws, 0, sizeof *ws);
+    ws->head_dim = (int)D;
+    ws->shape = sh;
+    ws->merge = mg;
+    ws->tq_pad = tq_pad;
+    ws->tk = tk;
+    ws->tk_pad = tk_pad;
+    ws->device = dev;
+    ws->mem = mem;
+    ws->bytes = total;
+    uint8_t* p = (uint8_t*)mem;
+    ws->buf.q8 = (int8_t*)p; p += n_q8;
+    ws->buf.q_scale = (float*)p; p += n_qs;
+    ws->buf.k8 = (int8_t*)p; p += n_k8;
+    ws->buf.k_scale = (float*)p; p += n_ks;
+    ws->buf.v8 = (uint8_t*)p; p += n_v8;
+    ws->buf.stats = (float*)p; p += n_st;
+    ws->buf.kbias = (float*)p; p += n_kb;
+    ws->buf.part = (float*)p; p += n_part;
+    ws->buf.err = (uint32_t*)p;
+
+    const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    int rc = make_map(&ws->maps.q, ws->buf.q8, D, tq_pad, B * H, D, tq_pad * D, (uint32_t)D, 128, swz);
+    if (rc == SPL_SAGE_OK)
+        rc = make_map(&ws->maps.k, ws->buf.k8, D, tk_pad, B * G, D, tk_pad * D, (uint32_t)D, 128, swz);
+    if (rc == SPL_SAGE_OK)
+        rc = make_map(&ws->maps.v, ws->buf.v8, tk_pad, D, B * G, tk_pad, tk_pad * D, 128, (uint32_t)D,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SPL_SAGE_OK) {
+        cudaFree(mem);
+        delete ws;
+        return rc;
+    }
+    *out = ws;
+    return SPL_SAGE_OK;
+}
+
+void spl_sage_ws_destroy(spl_sage_ws* ws) {
+    if (!ws) return;
+    cudaFree(ws->mem);
+    delete ws;
+}
+
+int64_t spl_sage_ws_bytes(const spl_sage_ws* ws) { return ws ? (int64_t)ws->bytes : 0; }
+
+int spl_sage_ws_plan(const spl_sage_ws* ws, spl_sage_plan* out) {
+    if (!ws || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ws_plan: NULL argument");
+    out->tq_pad = ws->tq_pad;
+    out->tk = ws->tk;
+    out->tk_pad = ws->tk_pad;
+    return SPL_SAGE_OK;
+}
+
+static int check_tensor(const char* what, const void* data, int64_t len, int64_t sb, int64_t st, int64_t sh,
+                        const spl_sage_shape& shape, int64_t heads, int64_t d) {
+    if (sb < 0 || st < 0 || sh < 0 || sb % 8 || st % 8 || sh % 8)
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "%s strides must be multiples of 8 elements: Strides { batch: %lld, token: %lld, head: %lld }",
+                    what, (long long)sb, (long long)st, (long long)sh);
+    if (!data) return fail(SPL_SAGE_ERR_INVALID, "%s is NULL", what);
+    if ((uintptr_t)data % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "%s must start on a multiple of 8 elements (16 bytes)", what);
+    const int64_t need = (shape.batch - 1) * sb + (shape.tokens - 1) * st + (heads - 1) * sh + d;
+    if (len < need)
+        return fail(SPL_SAGE_ERR_INVALID, "%s holds %lld elements, its shape and strides need %lld", what,
+                    (long long)len, (long long)need);
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                     const spl_sage_options* opts) {
+    if (!s || !ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_prepare: NULL engine or workspace");
+    if (ws->head_dim != s->head_dim)
+        return fail(SPL_SAGE_ERR_INVALID, "workspace was made for head dim %d, kernels are %d", ws->head_dim,
+                    s->head_dim);
+    spl_sage_options o;
+    if (opts)
+        o = *opts;
+    else
+        spl_sage_default_options(&o);
+    const int64_t D = s->head_dim;
+    const spl_sage_shape& sh = ws->shape;
+    int rc;
+    if ((rc = check_tensor("Q", q.data, q.len, q.batch, q.token, q.head, sh, sh.heads, D))) return rc;
+    if ((rc = check_tensor("K", k.data, k.len, k.batch, k.token, k.head, sh, sh.kv_heads, D))) return rc;
+    if ((rc = check_tensor("V", v.data, v.len, v.batch, v.token, v.head, sh, sh.kv_heads, D))) return rc;
+    if (o.qk_norm_params && o.qk_norm_len < 4 * D)
+        return fail(SPL_SAGE_ERR_INVALID, "QK-norm params hold %lld floats, need %lld", (long long)o.qk_norm_len,
+                    (long long)(4 * D));
+    int flags = 0;
+    if (o.qk_norm_params) flags |= LN_Q | LN_K;
+    if (o.smooth_k) flags |= SMOOTH_K;
+    if (o.smooth_v) flags |= SMOOTH_V;
+    // mod.rs:724-726 and :761: scale and q_mul in f32.
+    const float scale = o.has_softmax_scale ? o.softmax_scale : 1.0f / sqrtf((float)D);
+    const float log2e = 1.44269504088896340736f;
+
+    sp::Geom g;
+    memset(&g, 0, sizeof g);
+    g.q_sb = q.batch; g.q_st = q.token; g.q_sh = q.head;
+    g.k_sb = k.batch; g.k_st = k.token; g.k_sh = k.head;
+    g.v_sb = v.batch; g.v_st = v.token; g.v_sh = v.head;
+    g.batch = (int)sh.batch;
+    g.heads = (int)sh.heads;
+    g.kv_heads = (int)sh.kv_heads;
+    g.tokens = (int)sh.tokens;
+    g.tq_pad = (int)ws->tq_pad;
+    g.tk = (int)ws->tk;
+    g.tk_pad = (int)ws->tk_pad;
+    g.q_tiles = (int)(ws->tq_pad / QTILE);
+    const spl_sage_merge& mg = ws->merge;
+    g.merge = mg.stride;
+    if (mg.stride > 1) {
+        const int64_t s_ = mg.stride;
+        g.frames = (int)mg.frames;
+        g.special = (int)mg.special;
+        g.grid_h = (int)mg.grid_h;
+        g.grid_w = (int)mg.grid_w;
+        g.frame_tokens = (int)(mg.special + mg.grid_h * mg.grid_w);
+        g.merged_frame = (int)(mg.special + ((mg.grid_h + s_ - 1) / s_) * ((mg.grid_w + s_ - 1) / s_));
+        g.merged_w = (int)((mg.grid_w + s_ - 1) / s_);
+        g.dense_frames = (int)(mg.dense_frames < mg.frames ? mg.dense_frames : mg.frames);
+    } else {
+        g.frames = 1;
+    }
+    g.flags = flags;
+    g.causal = sh.causal ? 1 : 0;
+    g.q_mul = scale * log2e;
+    g.ln_eps = o.qk_norm_params ? o.qk_norm_eps : 1e-5f;
+    g.v_range = s->config.pv_accum == SPL_SAGE_PV_F16 ? PV16_V_RANGE : FP8_MAX;
+
+    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, o.qk_norm_params, ws->buf, g, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
+    ws->geom = g;
+    ws->prepared = true;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_attend(spl_sage* s, const spl_sage_ws* ws, spl_sage_tensor_mut out) {
+    if (!s || !ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_attend: NULL engine or workspace");
+    if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
+    if (ws->head_dim != s->head_dim)
+        return fail(SPL_SAGE_ERR_INVALID, "workspace was made for head dim %d, kernels are %d", ws->head_dim,
+                    s->head_dim);
+    int rc = check_tensor("output", out.data, out.len, out.batch, out.token, out.head, ws->shape, ws->shape.heads,
+                          s->head_dim);
+    if (rc) return rc;
+    sp::Geom g = ws->geom;
+    g.o_sb = out.batch;
+    g.o_st = out.token;
+    g.o_sh = out.head;
+    cudaError_t e = sp::launch_attend(s->head_dim, ws->maps, ws->buf, g, out.data, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage attention");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_forward(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                     spl_sage_tensor_mut out, const spl_sage_options* opts) {
+    int rc = spl_sage_prepare(s, ws, q, k, v, opts);
+    if (rc) return rc;
+    return spl_sage_attend(s, ws, out);
+}
+
+int spl_sage_ws_export_reference_layout(spl_sage* s, const spl_sage_ws* ws, void* q8, float* q_scale, void* k8,
+                                        float* k_scale, void* v8, float* stats, float* kbias) {
+    if (!s || !ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ws_export_reference_layout: NULL argument");
+    if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
+    const int64_t D = ws->head_dim, B = ws->shape.batch, H = ws->shape.heads, G = ws->shape.kv_heads;
+    struct {
+        void* dst;
+        const void* src;
+        size_t n;
+    } cp[] = {
+        {q8, ws->buf.q8, (size_t)(B * H * ws->tq_pad * D)},
+        {q_scale, ws->buf.q_scale, (size_t)(B * H * (ws->tq_pad / QGROUP) * 4)},
+        {k8, ws->buf.k8, (size_t)(B * G * ws->tk_pad * D)},
+        {k_scale, ws->buf.k_scale, (size_t)(B * G * (ws->tk_pad / KBLOCK) * 4)},
+        {stats, ws->buf.stats, (size_t)(B * G * 4 * D * 4)},
+        {kbias, ws->buf.kbias, (size_t)(ws->tk_pad * 4)},
+    };
+    for (auto& c : cp) {
+        if (!c.dst) continue;
+        cudaError_t e = cudaMemcpyAsync(c.dst, c.src, c.n, cudaMemcpyDeviceToDevice, s->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "export sage workspace");
+    }
+    if (v8) {
+        cudaError_t e = sp::launch_export_v(ws->head_dim, ws->buf, ws->geom, (uint8_t*)v8, s->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "export sage V");
+    }
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_status(spl_sage* s, spl_sage_ws* ws, uint32_t* device_error_word) {
+    if (!s || !ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_status: NULL argument");
+    uint32_t w = 0;
+    cudaError_t e = cudaMemcpyAsync(&w, ws->buf.err, 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "read sage device status");
+    if (device_error_word) *device_error_word = w;
+    if (w) {
+        cudaMemsetAsync(ws->buf.err, 0, 4, s->stream);
+        return fail(SPL_SAGE_ERR_KERNEL, "sage kernel reported device error word 0x%08x (timeout site %u)", w,
+                    (w >> 8) & 0xff);
+    }
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes) {
+    if (!s || !registers || !spill_bytes) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_attn_resources: NULL argument");
+    cudaError_t e = sp::attn_func_attributes(s->head_dim, 0, registers, spill_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "query attention kernel attributes");
+    return SPL_SAGE_OK;
+}
+
+double spl_sage_flops(const spl_sage_ws* ws) {
+    if (!ws) return 0.0;
+    return 4.0 * (double)(ws->shape.batch * ws->shape.heads) * (double)ws->shape.tokens * (double)ws->tk *
+           (double)ws->head_dim;
+}
+
+}  // extern "C"

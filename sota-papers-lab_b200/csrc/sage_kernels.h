@@ -1,0 +1,66 @@
+// Internal interface between the C-ABI host code (sage_api.cpp) and the
+// CUDA translation units.  Not installed; the public ABI is include/splsage.h.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sp {
+
+// Geometry of one prepare/attend call.  Strides are in bf16 elements.
+// Mirrors the reference's SgGeom (platform/spl-nn/cuda/sage_common.cu:39-64)
+// plus kv_heads and the causal flag, which the reference does not have.
+struct Geom {
+    long long q_sb, q_st, q_sh;
+    long long k_sb, k_st, k_sh;
+    long long v_sb, v_st, v_sh;
+    long long o_sb, o_st, o_sh;
+    int batch, heads, kv_heads, tokens;
+    int tq_pad, tk, tk_pad, q_tiles;
+    int merge, frames, frame_tokens, special;
+    int grid_h, grid_w, merged_frame, merged_w;
+    int dense_frames, flags, causal, pad0;
+    float q_mul, ln_eps, v_range, pad1;
+};
+
+// Device buffers of one workspace.  Layouts (b = batch, h = q head,
+// g = kv head):
+//   q8      i8  [b][h][tq_pad][D]         (reference layout)
+//   q_scale f32 [b][h][tq_pad/16]         (reference layout)
+//   k8      i8  [b][g][tk_pad][D]         (reference layout)
+//   k_scale f32 [b][g][tk_pad/64]         (reference layout)
+//   v8      u8  [b][g][D][tk_pad]         E4M3, channel-major, keys in order:
+//                                         the K-major B operand of the PV UMMA
+//   stats   f32 [b][g][4][D]              (reference layout)
+//   kbias   f32 [tk_pad]                  log2(count) or -inf (merge only)
+//   part    f32 [b][g][q_tiles][4][D]     per-tile channel statistics
+//   err     u32 [1]                       device error word
+struct Buffers {
+    int8_t* q8;
+    float* q_scale;
+    int8_t* k8;
+    float* k_scale;
+    uint8_t* v8;
+    float* stats;
+    float* kbias;
+    float* part;
+    uint32_t* err;
+};
+
+// TMA descriptors for the attention kernel (built once per workspace).
+struct AttnMaps {
+    CUtensorMap q;  // q8 as {D, tq_pad, b*h}, box {D, 128, 1}
+    CUtensorMap k;  // k8 as {D, tk_pad, b*g}, box {D, 128, 1}
+    CUtensorMap v;  // v8 as {tk_pad, D, b*g}, box {128, D, 1}
+};
+
+cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                           const Geom& g, cudaStream_t st);
+cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);
+cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
+                          cudaStream_t st);
+cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes);
+int attn_smem_bytes(int d);
+
+}  // namespace sp

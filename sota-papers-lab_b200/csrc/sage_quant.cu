@@ -1,0 +1,405 @@
+// SageAttention2 quantiser for sm_100a: INT8 Q (one scale per 16 rows, the
+// softmax scale and log2(e) folded in), smoothed INT8 K (one scale per 64
+// keys), per-channel FP8 E4M3 V, optional KV merging and QK LayerNorm.
+//
+// The values written are bit-identical to the reference quantiser
+// (platform/spl-nn/cuda/sage_quant.cu:59-326): the K/V channel sums follow
+// its summation tree (per-thread sequential sums over a 128-token tile,
+// an xor butterfly over the lanes that share a channel chunk, a sequential
+// sum over the 8 warps, then two interleaved accumulators over the tiles),
+// and every rounding happens where it happens there.  What differs is the
+// V layout ([b][g][D][tk_pad], keys in order, the K-major operand of the
+// tcgen05 PV MMA; sp_export_v rewrites the reference's layout for the bit
+// gate) and the separate KV head count (GQA: Q and the K/V statistics run
+// as two roles of one launch).
+//
+// Three launches, all HBM-bound:
+//   sp_prep      grid (q_tiles, heads + kv_heads, batch)
+//   sp_finalize  grid (kv_heads, batch)
+//   sp_quant_kv  grid (tk_pad / 64, kv_heads, batch)
+#include "sage_dev.cuh"
+#include "sage_kernels.h"
+
+namespace sp {
+
+__device__ __forceinline__ uint4 load8(const uint16_t* p, bool ok) {
+    return ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+}
+
+// LayerNorm over one head row whose D channels sit on D/8 consecutive lanes,
+// 8 per lane (the reference's sg_layernorm, sage_quant.cu:34-52).  Every lane
+// of the warp calls it.  Uses rsqrtf: tolerance-checked, not bit-checked.
+template <int D>
+__device__ __forceinline__ void layernorm8(float* x, const float* w, const float* bias, int ch, float eps) {
+    constexpr int CH = D / 8;
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) s += x[e];
+#pragma unroll
+    for (int o = 1; o < CH; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * (1.0f / D);
+    float s2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const float t = x[e] - mean;
+        s2 += t * t;
+    }
+#pragma unroll
+    for (int o = 1; o < CH; o <<= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float rstd = rsqrtf(s2 * (1.0f / D) + eps);
+#pragma unroll
+    for (int e = 0; e < 8; e++) x[e] = (x[e] - mean) * rstd * w[ch * 8 + e] + bias[ch * 8 + e];
+}
+
+// Q role: one 128-query tile of one q head.
+template <int D>
+__device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const float* __restrict__ ln,
+                                       int8_t* __restrict__ q8, float* __restrict__ q_scale, const Geom& g, int tile,
+                                       int h, int b) {
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
+    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
+    const long long bh = (long long)b * g.heads + h;
+    __shared__ unsigned gmax[QTILE / QGROUP];
+    if (tid < QTILE / QGROUP) gmax[tid] = 0u;
+    __syncthreads();
+    float qv[NI][8];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tl = tid / CH + i * TPI;
+        const int tok = tile * QTILE + tl;
+        const bool ok = tok < g.tokens;
+        unpack_bf16x8(load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, ok), qv[i]);
+        if (g.flags & LN_Q) layernorm8<D>(qv[i], ln, ln + D, ch, g.ln_eps);
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            if (!ok) qv[i][e] = 0.f;
+            amax = fmaxf(amax, fabsf(qv[i][e]));
+        }
+        // The rows of one warp lie in one 16-row group (32 / CH <= 16 rows).
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) atomicMax(&gmax[tl / QGROUP], __float_as_uint(amax));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tl = tid / CH + i * TPI;
+        const float amax = __uint_as_float(gmax[tl / QGROUP]);
+        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+        const float* f = qv[i];
+        uint2 w;
+        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+        *reinterpret_cast<uint2*>(q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + ch * 8) = w;
+    }
+    if (tid < QTILE / QGROUP) {
+        const float t = __uint_as_float(gmax[tid]) * (1.0f / 127.0f);
+        q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + tid] = t * g.q_mul;
+    }
+}
+
+// Statistics role: per-channel sum of K, sum / min / max of V over one
+// 128-token tile of one kv head, with the reference's reduction tree.
+template <int D>
+__device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                           const float* __restrict__ ln, float* __restrict__ part, const Geom& g,
+                                           int tile, int h, int b) {
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ch = tid % CH;
+    const long long bh = (long long)b * g.kv_heads + h;
+    __shared__ float red[8][4][D];
+    float ks[8], vs[8], vmn[8], vmx[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        ks[e] = 0.f;
+        vs[e] = 0.f;
+        vmn[e] = 3.0e38f;
+        vmx[e] = -3.0e38f;
+    }
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tl = tid / CH + i * TPI;
+        const int tok = tile * QTILE + tl;
+        const bool ok = tok < g.tokens;
+        float fk[8], fv[8];
+        unpack_bf16x8(load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, ok), fk);
+        unpack_bf16x8(load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, ok), fv);
+        if (g.flags & LN_K) layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
+        if (ok) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                ks[e] += fk[e];
+                vs[e] += fv[e];
+                vmn[e] = fminf(vmn[e], fv[e]);
+                vmx[e] = fmaxf(vmx[e], fv[e]);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = CH; o < 32; o <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
+            vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
+            vmn[e] = fminf(vmn[e], __shfl_xor_sync(0xffffffffu, vmn[e], o));
+            vmx[e] = fmaxf(vmx[e], __shfl_xor_sync(0xffffffffu, vmx[e], o));
+        }
+    }
+    if (lane < CH) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            red[warp][0][ch * 8 + e] = ks[e];
+            red[warp][1][ch * 8 + e] = vs[e];
+            red[warp][2][ch * 8 + e] = vmn[e];
+            red[warp][3][ch * 8 + e] = vmx[e];
+        }
+    }
+    __syncthreads();
+    for (int c = tid; c < 4 * D; c += 256) {
+        const int stat = c / D, d = c % D;
+        float r = red[0][stat][d];
+#pragma unroll
+        for (int w = 1; w < 8; w++) {
+            const float x = red[w][stat][d];
+            r = stat < 2 ? r + x : (stat == 2 ? fminf(r, x) : fmaxf(r, x));
+        }
+        part[((bh * g.q_tiles + tile) * 4 + stat) * D + d] = r;
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                                               const uint16_t* __restrict__ v, const float* __restrict__ ln,
+                                               int8_t* __restrict__ q8, float* __restrict__ q_scale,
+                                               float* __restrict__ part, const Geom g) {
+    const int tile = blockIdx.x, y = blockIdx.y, b = blockIdx.z;
+    if (y < g.heads)
+        prep_q<D>(q, ln, q8, q_scale, g, tile, y, b);
+    else
+        prep_stats<D>(k, v, ln, part, g, tile, y - g.heads, b);
+}
+
+// Per (kv head, batch): K mean, V mean, V scale and its reciprocal from the
+// tile partials, the tiles summed as two interleaved accumulators.
+template <int D>
+__global__ void __launch_bounds__(256) sp_finalize(const float* __restrict__ part, float* __restrict__ stats,
+                                                   const Geom g) {
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const long long bh = (long long)b * g.kv_heads + h;
+    __shared__ float st[4][D];
+    for (int c = tid; c < 4 * D; c += 256) {
+        const int stat = c / D, d = c % D;
+        const float* p = part + bh * g.q_tiles * 4 * D + stat * D + d;
+        float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
+        float r1 = r0;
+        int t = 0;
+        for (; t + 1 < g.q_tiles; t += 2) {
+            const float x0 = p[(long long)t * 4 * D], x1 = p[(long long)(t + 1) * 4 * D];
+            if (stat < 2) {
+                r0 += x0;
+                r1 += x1;
+            } else if (stat == 2) {
+                r0 = fminf(r0, x0);
+                r1 = fminf(r1, x1);
+            } else {
+                r0 = fmaxf(r0, x0);
+                r1 = fmaxf(r1, x1);
+            }
+        }
+        if (t < g.q_tiles) {
+            const float x0 = p[(long long)t * 4 * D];
+            r0 = stat < 2 ? r0 + x0 : (stat == 2 ? fminf(r0, x0) : fmaxf(r0, x0));
+        }
+        st[stat][d] = stat < 2 ? r0 + r1 : (stat == 2 ? fminf(r0, r1) : fmaxf(r0, r1));
+    }
+    __syncthreads();
+    for (int d = tid; d < D; d += 256) {
+        const float n = (float)g.tokens;
+        const float mk = (g.flags & SMOOTH_K) ? st[0][d] / n : 0.f;
+        const float mv = (g.flags & SMOOTH_V) ? st[1][d] / n : 0.f;
+        const float amax = fmaxf(st[3][d] - mv, mv - st[2][d]);
+        const float scale = amax > 0.f ? amax / g.v_range : 1.0f;
+        float* o = stats + bh * 4 * D;
+        o[d] = mk;
+        o[D + d] = mv;
+        o[2 * D + d] = scale;
+        o[3 * D + d] = 1.0f / scale;
+    }
+}
+
+// Members of merged key j within one batch item: the count, the first token
+// and the cell's row length (the merge geometry of sage_quant.cu:210-235:
+// special tokens and the first dense_frames frames stay single, patch cells
+// of merge x merge pool what they cover).
+__device__ __forceinline__ int members(const Geom& g, int j, int& base, int& nx) {
+    if (g.merge == 1) {
+        base = j;
+        nx = 1;
+        return 1;
+    }
+    const int dense = g.dense_frames * g.frame_tokens;
+    if (j < dense) {
+        base = j;
+        nx = 1;
+        return 1;
+    }
+    const int f = g.dense_frames + (j - dense) / g.merged_frame, loc = (j - dense) % g.merged_frame;
+    if (loc < g.special) {
+        base = f * g.frame_tokens + loc;
+        nx = 1;
+        return 1;
+    }
+    const int cell = loc - g.special;
+    const int gy = cell / g.merged_w, gx = cell % g.merged_w;
+    const int y0 = gy * g.merge, x0 = gx * g.merge;
+    const int ny = min(g.merge, g.grid_h - y0);
+    nx = min(g.merge, g.grid_w - x0);
+    base = f * g.frame_tokens + g.special + y0 * g.grid_w + x0;
+    return ny * nx;
+}
+
+// One 64-key block of one kv head: pool members, subtract the K mean, INT8 K
+// with one scale per block; V -> (v - mean) / scale -> E4M3, written
+// channel-major ([D][tk_pad]) through a shared-memory transpose.
+template <int D>
+__global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                                   const float* __restrict__ ln, const float* __restrict__ stats,
+                                                   int8_t* __restrict__ k8, float* __restrict__ k_scale,
+                                                   uint8_t* __restrict__ v8, float* __restrict__ kbias,
+                                                   const Geom g) {
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = KBLOCK / TPI;
+    const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
+    const long long bh = (long long)b * g.kv_heads + h;
+    const int nblk = g.tk_pad / KBLOCK;
+    const int cells = g.merge * g.merge;
+
+    __shared__ unsigned kmax;
+    __shared__ __align__(16) uint8_t vt[D][KBLOCK];
+    if (tid == 0) kmax = 0u;
+    __syncthreads();
+
+    const float* st = stats + bh * 4 * D;
+    float kv[NI][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int kl = tid / CH + i * TPI;
+        const int j = blk * KBLOCK + kl;
+        const bool ok = j < g.tk;
+        int base = 0, nx = 1;
+        const int cnt = ok ? members(g, j, base, nx) : 0;
+        float ksum[8], vsum[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) ksum[e] = vsum[e] = 0.f;
+        for (int m = 0; m < cells; m++) {
+            const bool mok = m < cnt;
+            const int tok = base + (mok ? (m / nx) * g.grid_w + m % nx : 0);
+            float fk[8], fv[8];
+            unpack_bf16x8(load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, mok), fk);
+            unpack_bf16x8(load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, mok), fv);
+            if (g.flags & LN_K) layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
+            if (mok) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    ksum[e] += fk[e];
+                    vsum[e] += fv[e];
+                }
+            }
+        }
+        const float rc = cnt > 0 ? 1.0f / (float)cnt : 0.f;
+        float vq[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int d = ch * 8 + e;
+            // fmaf: the contraction nvcc applies to the reference's
+            // `ksum * rc - mean` and `(vsum * rc - mv) * inv`.
+            kv[i][e] = ok ? fmaf(ksum[e], rc, -st[d]) : 0.f;
+            amax = fmaxf(amax, fabsf(kv[i][e]));
+            vq[e] = ok ? fmaf(vsum[e], rc, -st[D + d]) * st[3 * D + d] : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
+            vt[ch * 8 + e][kl] = (uint8_t)(two & 0xff);
+            vt[ch * 8 + e + 1][kl] = (uint8_t)(two >> 8);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) atomicMax(&kmax, __float_as_uint(amax));
+    __syncthreads();
+
+    const float km = __uint_as_float(kmax);
+    const float inv = km > 0.f ? 127.0f / km : 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int kl = tid / CH + i * TPI;
+        const float* f = kv[i];
+        uint2 w;
+        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+        *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + kl) * D + ch * 8) = w;
+    }
+    if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
+    // V: channel d's 64 keys are 64 contiguous bytes of row d.
+    for (int c = tid; c < D * (KBLOCK / 16); c += 256) {
+        const int d = c / (KBLOCK / 16), part16 = c % (KBLOCK / 16);
+        *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + part16 * 16) =
+            *reinterpret_cast<const uint4*>(&vt[d][part16 * 16]);
+    }
+    if (g.merge > 1 && b == 0 && h == 0 && tid < KBLOCK) {
+        const int j = blk * KBLOCK + tid;
+        int base, nx;
+        kbias[j] = j < g.tk ? log2f((float)members(g, j, base, nx)) : __int_as_float(0xff800000);
+    }
+}
+
+// The reference's V layout for the bit gate: [b][g][tk_pad/64][D][64], keys
+// permuted within each 16 by vpos (sage_common.cu:151-155).
+__device__ __forceinline__ int vpos(int k) { return ((k >> 1) & 3) * 4 + ((k >> 3) << 1) + (k & 1); }
+
+template <int D>
+__global__ void __launch_bounds__(256) sp_export_v(const uint8_t* __restrict__ v8, uint8_t* __restrict__ out,
+                                                   const Geom g) {
+    const long long n = (long long)g.batch * g.kv_heads * D * g.tk_pad;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+        const long long key = i % g.tk_pad;
+        const long long rest = i / g.tk_pad;  // bh * D + d
+        const int d = (int)(rest % D);
+        const long long bh = rest / D;
+        const int blk = (int)(key / KBLOCK), kl = (int)(key % KBLOCK);
+        const long long o = ((bh * (g.tk_pad / KBLOCK) + blk) * D + d) * KBLOCK + (kl & ~15) + vpos(kl & 15);
+        out[o] = v8[i];
+    }
+}
+
+template <int D>
+static cudaError_t prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                             const Geom& g, cudaStream_t st) {
+    sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g);
+    sp_finalize<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(buf.part, buf.stats, g);
+    sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
+        (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                           const Geom& g, cudaStream_t st) {
+    return d == 64 ? prepare_d<64>(q, k, v, ln, buf, g, st) : prepare_d<128>(q, k, v, ln, buf, g, st);
+}
+
+cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st) {
+    const long long n = (long long)g.batch * g.kv_heads * d * g.tk_pad;
+    const long long want = (n + 255) / 256;
+    const int blocks = (int)(want < 148ll * 32 ? want : 148ll * 32);
+    if (d == 64)
+        sp_export_v<64><<<blocks, 256, 0, st>>>(buf.v8, v8_ref, g);
+    else
+        sp_export_v<128><<<blocks, 256, 0, st>>>(buf.v8, v8_ref, g);
+    return cudaGetLastError();
+}
+
+}  // namespace sp

@@ -1,0 +1,38 @@
+"""Shared fixtures.  `gpu`-marked tests need a B200; everything else runs on
+the CPU (the driver runs `pytest -m "not gpu"` without a GPU)."""
+import importlib
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a)")
+    config.addinivalue_line("markers", "slow: long-running CPU test")
+
+
+def _ensure_oracle():
+    lib = os.path.join(ROOT, "oracle", "liboracle.so")
+    if not os.path.exists(lib):
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "liboracle.so"], check=True)
+
+
+_ensure_oracle()
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    from oracle import oracle as o
+    return o
+
+
+@pytest.fixture(scope="session")
+def sage():
+    """The product's Python mirror of the spl_nn::sage API (over libsplsage.so)."""
+    return importlib.import_module("sota-papers-lab_b200")

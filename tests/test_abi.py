@@ -1,0 +1,93 @@
+"""CPU tests of the boundary: libsplsage.so loads and exports every symbol
+include/splsage.h declares, the ctypes structs match the C layout, host-side
+validation mirrors the reference's (mod.rs checks), and without a GPU the
+library fails loudly instead of falling back."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "splsage.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(spl_sage_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol(sage):
+    names = declared_functions()
+    assert len(names) >= 17
+    out = subprocess.run(["nm", "-D", "--defined-only", sage.library_path()], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r" T (\w+)", out))
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+    assert set(sage.EXPORTS) == set(names)
+
+
+def test_struct_layouts_match_the_header(sage, tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "splsage.h"\n'
+        'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n",'
+        'sizeof(spl_sage_config), sizeof(spl_sage_shape), sizeof(spl_sage_merge), sizeof(spl_sage_tensor),'
+        'sizeof(spl_sage_options), sizeof(spl_sage_plan), offsetof(spl_sage_options, qk_norm_params),'
+        'offsetof(spl_sage_merge, frames), offsetof(spl_sage_shape, causal), offsetof(spl_sage_options, qk_norm_eps));'
+        'return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    m = sage
+    want = [ctypes.sizeof(m._Config), ctypes.sizeof(m._Shape), ctypes.sizeof(m._Merge), ctypes.sizeof(m._Tensor),
+            ctypes.sizeof(m._Options), ctypes.sizeof(m._Plan), m._Options.qk_norm_params.offset,
+            m._Merge.frames.offset, m._Shape.causal.offset, m._Options.qk_norm_eps.offset]
+    assert got == want
+
+
+def test_defaults_mirror_the_reference(sage):
+    # Config::for_head_dim (mod.rs:195-200), Tile::DEFAULT / D128, Options::default.
+    c = sage._Config()
+    sage.lib().spl_sage_default_config(64, ctypes.byref(c))
+    assert (c.warps, c.m_tiles, c.stages, c.pv_accum) == (4, 2, 3, 0)
+    sage.lib().spl_sage_default_config(128, ctypes.byref(c))
+    assert (c.warps, c.m_tiles, c.stages, c.pv_accum) == (4, 1, 3, 0)
+    o = sage._Options()
+    sage.lib().spl_sage_default_options(ctypes.byref(o))
+    assert (o.smooth_k, o.smooth_v, o.has_softmax_scale, o.qk_norm_params) == (1, 1, 0, None)
+
+
+def test_strides_cover_the_tensor(sage):
+    # tests.rs:246-261
+    shape = sage.Shape(batch=2, heads=3, tokens=5)
+    d = 64
+    assert sage.Strides.bthd(5, 3, d).extent(shape, d) == 2 * 5 * 3 * d
+    assert sage.Strides.bhtd(5, 3, d).extent(shape, d) == 2 * 3 * 5 * d
+    assert sage.Strides.packed_qkv(5, 3, d).extent(shape, d) + 2 * 3 * d == 2 * 5 * 3 * 3 * d
+
+
+def test_create_validates_before_touching_the_gpu(sage):
+    h = ctypes.c_void_p()
+    rc = sage.lib().spl_sage_create(None, 96, None, ctypes.byref(h))
+    assert rc == 1 and b"head dim 64 or 128" in sage.lib().spl_sage_last_error()
+    bad = sage._Config(3, 1, 3, 0)
+    rc = sage.lib().spl_sage_create(None, 64, ctypes.byref(bad), ctypes.byref(h))
+    assert rc == 1 and b"unsupported sage tile" in sage.lib().spl_sage_last_error()
+
+
+def test_no_gpu_fails_loudly(sage):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(sage.SageError) as e:
+        sage.SageAttention(None, 64)
+    assert e.value.code in (2, 3)
+
+
+def test_flops_definition(sage):
+    plan = sage.Plan(sage.Shape(1, 16, 137800), sage.KvMerge.dense(), 137856, 137800, 137856)
+    assert sage.flops(plan, 64) == 4.0 * 16 * 137800 * 137800 * 64
