@@ -168,6 +168,14 @@ int spl_sage_status(spl_sage* s, spl_sage_ws* ws, uint32_t* device_error_word);
  * local (spill) bytes of the attention kernel. */
 int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes);
 
+/* Tensor-core peak probe (the analog of the reference's sage_peak kernels,
+ * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
+ * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n
+ * (64, 128 or 256), 32 bytes of K, kind 0 = i8 -> s32, 1 = f8f6f4 e4m3 -> f32,
+ * 2 = f16 (bf16) -> f32.  Returns the rate over all SMs in tera-ops/s and the
+ * cycles per instruction of SM 0.  Synchronises the engine's stream. */
+int spl_sage_tensor_peak(spl_sage* s, int kind, int n, int iters, double* tops, double* cycles_per_mma);
+
 /* flops (mod.rs:905-910): 4 * B * H * Tq * Tk * D of the workspace's plan. */
 double spl_sage_flops(const spl_sage_ws* ws);
 

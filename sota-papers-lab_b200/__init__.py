@@ -85,7 +85,7 @@ EXPORTS = [
     "spl_sage_default_config", "spl_sage_default_options", "spl_sage_create", "spl_sage_destroy",
     "spl_sage_workspace_create", "spl_sage_ws_destroy", "spl_sage_ws_bytes", "spl_sage_ws_plan", "spl_sage_prepare",
     "spl_sage_attend", "spl_sage_forward", "spl_sage_ws_export_reference_layout", "spl_sage_status",
-    "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version",
+    "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version", "spl_sage_tensor_peak",
 ]
 
 _lib = None
@@ -116,6 +116,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_ws_export_reference_layout.argtypes = [P] * 9
         L.spl_sage_status.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint32)]
         L.spl_sage_attn_resources.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.spl_sage_tensor_peak.argtypes = [P, I, I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         L.spl_sage_flops.restype = ctypes.c_double
         L.spl_sage_flops.argtypes = [P]
         L.spl_sage_last_error.restype = ctypes.c_char_p
@@ -362,6 +363,13 @@ class SageAttention:
         r, s = ctypes.c_int(), ctypes.c_int()
         _check(lib().spl_sage_attn_resources(self._h, ctypes.byref(r), ctypes.byref(s)))
         return r.value, s.value
+
+    def tensor_peak(self, kind: int, n: int = 128, iters: int = 20000) -> tuple[float, float]:
+        """Measured tcgen05 rate: kind 0 INT8, 1 FP8 E4M3, 2 BF16; returns
+        (tera-ops/s over all SMs, cycles per M128 x N x 32-byte instruction)."""
+        t, c = ctypes.c_double(), ctypes.c_double()
+        _check(lib().spl_sage_tensor_peak(self._h, kind, n, iters, ctypes.byref(t), ctypes.byref(c)))
+        return t.value, c.value
 
     def workspace(self, shape: Shape, merge: KvMerge | None = None) -> Workspace:
         merge = merge or KvMerge.dense()

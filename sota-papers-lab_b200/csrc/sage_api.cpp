@@ -441,6 +441,46 @@ int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes) {
     return SPL_SAGE_OK;
 }
 
+int spl_sage_tensor_peak(spl_sage* s, int kind, int n, int iters, double* tops, double* cycles_per_mma) {
+    if (!s || !tops) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_tensor_peak: NULL argument");
+    if (kind < 0 || kind > 2 || !(n == 64 || n == 128 || n == 256) || iters <= 0)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_tensor_peak: kind 0..2, n 64/128/256, iters > 0");
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->device);
+    void* scratch = nullptr;
+    cudaError_t e = cudaMalloc(&scratch, 64);
+    if (e != cudaSuccess) return cuda_fail(e, "allocate peak-probe scratch");
+    cudaMemsetAsync(scratch, 0, 64, s->stream);
+    uint32_t* err = (uint32_t*)scratch;
+    unsigned long long* cyc = (unsigned long long*)((char*)scratch + 32);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    e = sp::launch_peak(kind, n, iters, sms, err, cyc, s->stream);  // warm-up
+    if (e == cudaSuccess) {
+        cudaEventRecord(a, s->stream);
+        e = sp::launch_peak(kind, n, iters, sms, err, cyc, s->stream);
+        cudaEventRecord(b, s->stream);
+    }
+    float ms = 0.f;
+    unsigned long long c = 0;
+    uint32_t w = 0;
+    if (e == cudaSuccess) e = cudaEventSynchronize(b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+    if (e == cudaSuccess) e = cudaMemcpy(&c, cyc, 8, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&w, err, 4, cudaMemcpyDeviceToHost);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaFree(scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor peak probe");
+    if (w) return fail(SPL_SAGE_ERR_KERNEL, "tensor peak probe timed out (0x%08x)", w);
+    const double k_elems = kind == 2 ? 16.0 : 32.0;
+    const double ops = 2.0 * 128.0 * n * k_elems * 4.0 * iters * sms;
+    *tops = ops / (ms * 1e-3) / 1e12;
+    if (cycles_per_mma) *cycles_per_mma = (double)c / (4.0 * iters);
+    return SPL_SAGE_OK;
+}
+
 double spl_sage_flops(const spl_sage_ws* ws) {
     if (!ws) return 0.0;
     return 4.0 * (double)(ws->shape.batch * ws->shape.heads) * (double)ws->shape.tokens * (double)ws->tk *

@@ -5,26 +5,31 @@
 // count bias when keys are merged), q_scale already holding softmax scale *
 // log2(e); online softmax in exp2 with a running max m and sum l;
 // P = 448 * 2^(x - m) rounded to FP8 E4M3; each block's PV starts from zero
-// (FP32) and is folded into the FP32 output O = O * alpha + PV (two-level
-// accumulation); out = O / l * v_scale + v_mean in bf16.  The S accumulator
-// is read as the float 1.5 * 2^23 + S (exact for |S| < 2^22) after one
-// integer add, and the 1.5 * 2^23 offset is folded into the exp2 FFMA, as
-// the reference does.
+// (FP32, in TMEM) and is folded into the FP32 output O = O * alpha + PV held
+// in registers (two-level accumulation); out = O / l * v_scale + v_mean in
+// bf16.  The S accumulator is read as the float 1.5 * 2^23 + S (exact for
+// |S| < 2^22) after one integer add, and the 1.5 * 2^23 offset is folded
+// into the exp2 FFMA, as the reference does.
 //
-// Structure (one CTA = 128 query rows of one (batch, q head); 12 warps):
-//   warp 0     TMA producer: Q once, then a ring of 128-key INT8 K tiles and
-//              a ring of [D][128] FP8 V^T tiles (non-multicast TMA, 128B or
-//              64B swizzle, zero fill past the end)
-//   warp 1     MMA issuer (one thread): QK^T = tcgen05.mma kind::i8 M128 N128
-//              into a double-buffered S in TMEM; PV = tcgen05.mma
-//              kind::f8f6f4 M128 N=D with P from shared memory into a PV
-//              buffer in TMEM
-//   warp 2     TMEM allocation (512 columns)
-//   warps 4-7  softmax: thread = query row (TMEM lane), reads its S row with
-//              tcgen05.ld, computes m, alpha, P8 and l in registers, writes
-//              its P row into the 128B-swizzled K-major P tile
-//   warps 8-11 correction: O (FP32, TMEM) = O * alpha + PV per block, then
-//              the epilogue
+// Structure: one CTA = 128 query rows of one (batch, q head), 10 warps.
+//   warps 0-7  softmax + correction.  Warp w owns the 16 rows
+//              32*(w%4) + 16*(w/4) + (0..15) (its TMEM lane quarter is w%4);
+//              lane t < 16 handles keys 0-63 of every 128-key block and
+//              output columns [0, D/2) of row t, lane t + 16 keys 64-127
+//              and columns [D/2, D) of the same row.  S is read with
+//              tcgen05.ld 16x32bx2, so the two halves of a row meet in one
+//              warp (one shuffle for the row max) and the two warps sharing
+//              an SM sub-partition run independently.  Keys 0-63 and 64-127
+//              are two 64-key k_scale blocks, so each lane has one scale.
+//   warp 8     TMA producer: Q once, then rings of 128-key INT8 K tiles and
+//              [D][128] FP8 V^T tiles (non-multicast TMA, 128B / 64B
+//              swizzle, zero fill past the end)
+//   warp 9     TMEM allocation and the MMA issuer (one thread): QK^T =
+//              tcgen05.mma kind::i8 M128 N128 into a double-buffered S, PV =
+//              tcgen05.mma kind::f8f6f4 M128 N=D with P from shared memory
+//              into a double-buffered PV
+// Per 16 keys, SP_EXP_POLY of the exponentials run on the FMA pipe
+// (exp2_poly2) to take load off the MUFU unit.
 // Extensions not in the reference: causal masking (blocks past the diagonal
 // are skipped, the diagonal block masked) and GQA (q head h reads kv head
 // h / (heads / kv_heads)).
@@ -37,9 +42,29 @@
 
 namespace sp {
 
+// Pipeline timestamps of the first CTA (debug builds with -DSP_TRACE only;
+// compiled out otherwise).  Slot = role * 1024 + block * 8 + event.
+#ifdef SP_TRACE
+__device__ unsigned long long sp_trace_buf[4096];
+#define SP_TR(cond, role, jb, ev)                                      \
+    do {                                                               \
+        if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && (jb) < 128) \
+            sp_trace_buf[(role) * 1024 + (jb) * 8 + (ev)] = clock64(); \
+    } while (0)
+#else
+#define SP_TR(cond, role, jb, ev) \
+    do {                          \
+    } while (0)
+#endif
+
 constexpr int KST = 3;   // K ring depth
 constexpr int VST = 3;   // V ring depth
-constexpr int NTHREADS = 384;
+#ifndef SP_EXP_POLY
+#define SP_EXP_POLY 2
+#endif
+constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
+constexpr int NTHREADS = 320;
+constexpr int PRODUCER_WARP = 8, MMA_WARP = 9, NSOFTMAX_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // bits of 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;       // 1.5 * 2^23
@@ -65,9 +90,7 @@ struct Bars {
     uint64_t v_full[VST], v_empty[VST];
     uint64_t s_full[2];
     uint64_t p_full[2], p_free[2];
-    uint64_t pv_full, pv_free;
-    uint64_t a_full[2], a_free[2];
-    uint64_t l_full;
+    uint64_t pv_full[2], pv_free[2];
     uint64_t mma_done;
 };
 
@@ -90,18 +113,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float* __restrict__ k_scale, const float* __restrict__ stats, const float* __restrict__ kbias,
             uint16_t* __restrict__ out, uint32_t* __restrict__ err, const Geom g) {
     using L = AttnSmem<D>;
+    constexpr int DH = D / 2;
     constexpr uint32_t SWZ = D == 128 ? SWZ_128B : SWZ_64B;
     constexpr uint32_t QK_SBO = 8 * D;  // 8 rows of D bytes
     constexpr uint32_t IDESC_QK = make_idesc(C_S32, F_S8, F_S8, 128, 128);
     constexpr uint32_t IDESC_PV = make_idesc(C_F32, F_E4M3, F_E4M3, 128, D);
-    constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_PV = 256, TM_O = 256 + (D == 128 ? 128 : 64);
+    constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_PV0 = 256, TM_PV1 = 256 + D;
 
     extern __shared__ uint8_t dyn_smem[];
     __shared__ Bars bars;
     __shared__ uint32_t tmem_base_s;
     __shared__ uint32_t abort_s;
-    __shared__ float alpha_s[2][128];
-    __shared__ float l_s[128];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh_q = blockIdx.x;
@@ -131,20 +153,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(bars.s_full[i]), 1);
-            mbar_init(bar(bars.p_full[i]), 128);
+            mbar_init(bar(bars.p_full[i]), NSOFTMAX_WARPS);
             mbar_init(bar(bars.p_free[i]), 1);
-            mbar_init(bar(bars.a_full[i]), 128);
-            mbar_init(bar(bars.a_free[i]), 128);
+            mbar_init(bar(bars.pv_full[i]), 1);
+            mbar_init(bar(bars.pv_free[i]), NSOFTMAX_WARPS);
         }
-        mbar_init(bar(bars.pv_full), 1);
-        mbar_init(bar(bars.pv_free), 128);
-        mbar_init(bar(bars.l_full), 128);
         mbar_init(bar(bars.mma_done), 1);
         fence_barrier_init();
     }
     __syncthreads();
     if (abort_s) return;  // uniform: an earlier CTA already failed
-    if (warp == 2) {
+    if (warp == MMA_WARP) {
         tmem_alloc(smem_u32(&tmem_base_s), TMEM_COLS);
         tmem_relinquish();
     }
@@ -153,7 +172,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
 
-    if (warp == 0) {
+    if (warp == PRODUCER_WARP) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
@@ -165,10 +184,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = 0; j < nb; j++) {
                 const int ks = j % KST, vs = j % VST;
                 if (j >= KST && !mbar_wait(bar(bars.k_empty[ks]), ((j / KST) - 1) & 1, err, 1)) break;
+                SP_TR(true, 0, j, 0);
                 mbar_expect_tx(bar(bars.k_full[ks]), L::K_BYTES);
                 tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, j * BLK, bh_kv);
                 nk++;
                 if (j >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((j / VST) - 1) & 1, err, 2)) break;
+                SP_TR(true, 0, j, 1);
                 mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
                 tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), j * BLK, 0, bh_kv);
                 nv++;
@@ -185,13 +206,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 mbar_wait(bar(bars.v_full[s]), (last / VST) & 1, err, 5, false);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             bool ok = mbar_wait(bar(bars.q_full), 0, err, 10);
             auto issue_qk = [&](int jj) -> bool {
                 const int s = jj % KST;
                 if (!mbar_wait(bar(bars.k_full[s]), (jj / KST) & 1, err, 11)) return false;
+                SP_TR(true, 1, jj, 0);
                 tc_fence_after();
                 const uint32_t d_s = tmem + ((jj & 1) ? TM_S1 : TM_S0);
                 const uint32_t kaddr = sK + s * L::K_BYTES;
@@ -208,209 +230,204 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = 0; j < nb && ok; j++) {
                 const int pb = j & 1, vs = j % VST;
                 ok = mbar_wait(bar(bars.p_full[pb]), (j >> 1) & 1, err, 12);
-                if (ok && j >= 1) ok = mbar_wait(bar(bars.pv_free), (j - 1) & 1, err, 13);
+                if (!ok) break;
+                SP_TR(true, 1, j, 1);
+                // S[pb] has been read: start the QK^T two blocks ahead first.
+                if (j + 2 < nb && !(ok = issue_qk(j + 2))) break;
+                if (j >= 2) ok = mbar_wait(bar(bars.pv_free[pb]), ((j >> 1) - 1) & 1, err, 13);
+                SP_TR(true, 1, j, 2);
                 if (ok) ok = mbar_wait(bar(bars.v_full[vs]), (j / VST) & 1, err, 14);
                 if (!ok) break;
+                SP_TR(true, 1, j, 3);
                 tc_fence_after();
                 const uint32_t paddr = sP + pb * L::P_BYTES, vaddr = sV + vs * L::V_BYTES;
+                const uint32_t d_pv = tmem + (pb ? TM_PV1 : TM_PV0);
 #pragma unroll
                 for (int kk = 0; kk < BLK / 32; kk++)
-                    umma_f8(tmem + TM_PV, smem_desc(paddr + kk * 32, 1024, SWZ_128B),
+                    umma_f8(d_pv, smem_desc(paddr + kk * 32, 1024, SWZ_128B),
                             smem_desc(vaddr + kk * 32, 1024, SWZ_128B), IDESC_PV, kk > 0);
-                tc_commit(bar(bars.pv_full));
+                tc_commit(bar(bars.pv_full[pb]));
                 tc_commit(bar(bars.v_empty[vs]));
                 tc_commit(bar(bars.p_free[pb]));
-                if (j + 2 < nb) ok = issue_qk(j + 2);
             }
             // No MMA may be in flight when TMEM is freed.
             tc_commit(bar(bars.mma_done));
             mbar_wait(bar(bars.mma_done), 0, err, 15, false);
         }
-    } else if (warp >= 4 && warp < 8) {
-        // ------------------------------------------------------------ softmax
-        const int r = tid - 128;                       // query row in the tile = TMEM lane
-        const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+    } else {
+        // ------------------------------------------------------------ softmax + correction
+        const int quarter = warp & 3, sub = warp >> 2;
+        const int half = lane >> 4;                             // 0: keys 0-63, 1: keys 64-127
+        const int r = quarter * 32 + sub * 16 + (lane & 15);    // query row in the tile = TMEM lane
+        const uint32_t lane_base = (uint32_t)(quarter * 32 + sub * 16) << 16;
         const int qrow = qt * 128 + r;
         const float qs = q_scale[(long long)bh_q * (g.tq_pad / QGROUP) + qrow / QGROUP];
         const float* ksc = k_scale + (long long)bh_kv * nkb64;
-        float m = -1.0e30f, l = 0.f;
         const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+        float o[DH];
+#pragma unroll
+        for (int c = 0; c < DH; c++) o[c] = 0.f;
+        float m = -1.0e30f, l = 0.f, alpha_prev = 0.f;
+        auto kscale = [&](int jb) {
+            const int i = 2 * jb + half;
+            return __ldg(ksc + (i < nkb64 ? i : 2 * jb));
+        };
+        float ks = kscale(0);
         bool ok = true;
+        // O = O * a + PV[block jj] for this lane's D/2 columns: the second
+        // level of the FP32 accumulation (each block's PV starts from zero).
+        auto correct = [&](int jj, float a) -> bool {
+            const int pb = jj & 1;
+            if (!warp_wait(bar(bars.pv_full[pb]), (jj >> 1) & 1, err, 31)) return false;
+            SP_TR(lane == 0 && warp == 0, 2, jj, 6);
+            tc_fence_after();
+            const uint64_t a2 = pk2(a, a);
+#pragma unroll
+            for (int c = 0; c < DH; c += 32) {
+                uint32_t pv[32];
+                tmem_ld16x2<DH>(tmem + lane_base + (pb ? TM_PV1 : TM_PV0) + c, pv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    upk2(fma2(pk2(o[c + e], o[c + e + 1]), a2,
+                              pk2(__uint_as_float(pv[e]), __uint_as_float(pv[e + 1]))),
+                         o[c + e], o[c + e + 1]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(bars.pv_free[pb]));  // one arrival per warp
+            return true;
+        };
         for (int j = 0; j < nb; j++) {
             const int sb = j & 1;
-            const float ks0 = ksc[2 * j];
-            const float ks1 = (2 * j + 1 < nkb64) ? ksc[2 * j + 1] : ks0;
-            const float sc0 = qs * ks0, sc1 = qs * ks1;
+            const float sc = qs * ks;
+            if (j + 1 < nb) ks = kscale(j + 1);
+            SP_TR(lane == 0 && warp == 0, 2, j, 0);
             if (!warp_wait(bar(bars.s_full[sb]), (j >> 1) & 1, err, 20)) {
                 ok = false;
                 break;
             }
+            SP_TR(lane == 0 && warp == 0, 2, j, 1);
             tc_fence_after();
-            uint32_t sr[128];
+            uint32_t sr[64];
             {
                 uint32_t (&c0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
                 uint32_t (&c1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
-                uint32_t (&c2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[64]);
-                uint32_t (&c3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[96]);
-                const uint32_t ts = tmem + lane_off + (sb ? TM_S1 : TM_S0);
-                tmem_ld32(ts + 0, c0);
-                tmem_ld32(ts + 32, c1);
-                tmem_ld32(ts + 64, c2);
-                tmem_ld32(ts + 96, c3);
+                const uint32_t ts = tmem + lane_base + (sb ? TM_S1 : TM_S0);
+                tmem_ld16x2<64>(ts, c0);
+                tmem_ld16x2<64>(ts + 32, c1);
                 tmem_wait_ld();
             }
-            // x: the float 1.5 * 2^23 + S, or the log2 logit when merging;
-            // masked keys -inf.
-            float x[128];
-            const int key0 = j * BLK;
-            const bool tail = key0 + BLK > g.tk;
-            const bool diag = CAUSAL && (key0 + BLK > qt * 128);
+            // x: the float 1.5 * 2^23 + S (dense), or the log2 logit with the
+            // merge bias (merged); masked keys -inf.
+            float x[64];
+            const int key0 = j * BLK + half * 64;
             if (MERGE) {
-                const float c0 = -MAGIC_F * sc0, c1 = -MAGIC_F * sc1;
+                const float c0 = -MAGIC_F * sc;
 #pragma unroll
-                for (int c = 0; c < 128; c++) {
+                for (int c = 0; c < 64; c++) {
                     const int key = key0 + c;
                     const float kb = key < g.tk_pad ? __ldg(kbias + key) : __int_as_float(0xff800000);
-                    x[c] = fmaf(__uint_as_float(sr[c] + MAGIC_I), c < 64 ? sc0 : sc1, kb + (c < 64 ? c0 : c1));
+                    x[c] = fmaf(__uint_as_float(sr[c] + MAGIC_I), sc, kb + c0);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < 128; c++) x[c] = __uint_as_float(sr[c] + MAGIC_I);
+                for (int c = 0; c < 64; c++) x[c] = __uint_as_float(sr[c] + MAGIC_I);
             }
-            if (tail || diag) {
+            if (j * BLK + BLK > g.tk || (CAUSAL && j * BLK + BLK > qt * 128)) {
 #pragma unroll
-                for (int c = 0; c < 128; c++) {
+                for (int c = 0; c < 64; c++) {
                     const int key = key0 + c;
                     if (key >= g.tk || (CAUSAL && key > qrow)) x[c] = __int_as_float(0xff800000);
                 }
             }
-            float mnew;
-            if (MERGE) {
-                float mx = x[0];
+            float ma = x[0], mb = x[32];
 #pragma unroll
-                for (int c = 1; c < 127; c += 2) mx = fmax3(mx, x[c], x[c + 1]);
-                mx = fmaxf(mx, x[127]);
-                mnew = fmaxf(m, mx);
-            } else {
-                float m0 = x[0], m1 = x[64];
-#pragma unroll
-                for (int c = 1; c < 63; c += 2) {
-                    m0 = fmax3(m0, x[c], x[c + 1]);
-                    m1 = fmax3(m1, x[64 + c], x[64 + c + 1]);
-                }
-                m0 = fmaxf(m0, x[63]);
-                m1 = fmaxf(m1, x[127]);
-                mnew = fmax3(m, fmaf(m0, sc0, -MAGIC_F * sc0), fmaf(m1, sc1, -MAGIC_F * sc1));
+            for (int c = 1; c < 31; c += 2) {
+                ma = fmax3(ma, x[c], x[c + 1]);
+                mb = fmax3(mb, x[32 + c], x[32 + c + 1]);
             }
+            float pm = fmax3(ma, mb, fmaxf(x[31], x[63]));
+            if (!MERGE) pm = fmaf(pm, sc, -MAGIC_F * sc);  // -inf stays -inf
+            const float mnew = fmax3(m, pm, __shfl_xor_sync(0xffffffffu, pm, 16));
             const float alpha = ex2(m - mnew);
             m = mnew;
-            // P = 448 * 2^(x - m) as E4M3, written to the swizzled P tile.
+            SP_TR(lane == 0 && warp == 0, 2, j, 2);
+            // P = 448 * 2^(x - m) as E4M3 into the swizzled P tile.
             if (j >= 2 && !warp_wait(bar(bars.p_free[sb]), ((j >> 1) - 1) & 1, err, 21)) {
                 ok = false;
                 break;
             }
+            SP_TR(lane == 0 && warp == 0, 2, j, 3);
             const uint32_t prow_addr = sP + sb * L::P_BYTES + prow;
-            float sum = 0.f;
+            const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
+            const uint64_t sc2 = pk2(MERGE ? 1.0f : sc, MERGE ? 1.0f : sc), off2 = pk2(off, off);
+            uint64_t sum2a = pk2(0.f, 0.f), sum2b = sum2a;
 #pragma unroll
-            for (int c16 = 0; c16 < 8; c16++) {
+            for (int c16 = 0; c16 < 4; c16++) {
                 float p[16];
-                const float sc = c16 < 4 ? sc0 : sc1;
-                const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
 #pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    const float y = x[c16 * 16 + e];
-                    p[e] = ex2(MERGE ? y + off : fmaf(y, sc, off));
-                    sum += p[e];
+                for (int e = 0; e < 16; e += 2) {
+                    float y0, y1;
+                    upk2(fma2(pk2(x[c16 * 16 + e], x[c16 * 16 + e + 1]), sc2, off2), y0, y1);
+                    if (e < EXP_POLY) {
+                        exp2_poly2(y0, y1, p[e], p[e + 1]);
+                    } else {
+                        p[e] = ex2(y0);
+                        p[e + 1] = ex2(y1);
+                    }
+                    if ((e >> 1) & 1)
+                        sum2b = add2(sum2b, pk2(p[e], p[e + 1]));
+                    else
+                        sum2a = add2(sum2a, pk2(p[e], p[e + 1]));
                 }
                 uint32_t w[4];
 #pragma unroll
-                for (int q4 = 0; q4 < 4; q4++)
-                    w[q4] = e4m3x2(p[4 * q4], p[4 * q4 + 1]) | (e4m3x2(p[4 * q4 + 2], p[4 * q4 + 3]) << 16);
-                const uint32_t a = prow_addr + (uint32_t)(((c16 ^ (r & 7)) & 7) << 4);
+                for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
+                const int chunk = half * 4 + c16;
+                const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
                 asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
                              "r"(w[3])
                              : "memory");
             }
-            l = fmaf(l, alpha, sum);
+            float s0, s1, s2, s3;
+            upk2(sum2a, s0, s1);
+            upk2(sum2b, s2, s3);
+            l = fmaf(l, alpha, (s0 + s1) + (s2 + s3));
             fence_proxy_async_smem();
             tc_fence_before();
-            if (j >= 2 && !warp_wait(bar(bars.a_free[sb]), ((j >> 1) - 1) & 1, err, 22)) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(bars.p_full[sb]));  // one arrival per warp
+            SP_TR(lane == 0 && warp == 0, 2, j, 4);
+            // fold the previous block's PV into O while this block's PV runs
+            if (j >= 1 && !correct(j - 1, alpha_prev)) {
                 ok = false;
                 break;
             }
-            alpha_s[sb][r] = alpha;
-            mbar_arrive(bar(bars.a_full[sb]));
-            mbar_arrive(bar(bars.p_full[sb]));
+            SP_TR(lane == 0 && warp == 0, 2, j, 5);
+            alpha_prev = alpha;
         }
+        if (ok) ok = correct(nb - 1, alpha_prev);
         if (ok) {
-            l_s[r] = l;
-            mbar_arrive(bar(bars.l_full));
-        }
-    } else if (warp >= 8) {
-        // ------------------------------------------------------------ correction + epilogue
-        const int r = tid - 256;
-        const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
-        const uint32_t t_pv = tmem + lane_off + TM_PV, t_o = tmem + lane_off + TM_O;
-        bool ok = true;
-        for (int j = 0; j < nb; j++) {
-            const int sb = j & 1;
-            if (!warp_wait(bar(bars.a_full[sb]), (j >> 1) & 1, err, 30)) {
-                ok = false;
-                break;
-            }
-            const float alpha = alpha_s[sb][r];
-            mbar_arrive(bar(bars.a_free[sb]));
-            if (!warp_wait(bar(bars.pv_full), j & 1, err, 31)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < D / 32; c++) {
-                uint32_t pv[32], o[32];
-                tmem_ld32(t_pv + c * 32, pv);
-                if (j > 0) {
-                    tmem_ld32(t_o + c * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; e++)
-                        o[e] = __float_as_uint(fmaf(__uint_as_float(o[e]), alpha, __uint_as_float(pv[e])));
-                    tmem_st32(t_o + c * 32, o);
-                } else {
-                    tmem_wait_ld();
-                    tmem_st32(t_o + c * 32, pv);
-                }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bar(bars.pv_free));
-        }
-        if (ok && warp_wait(bar(bars.l_full), 0, err, 32)) {
-            tc_fence_after();
-            const float inv = 1.0f / l_s[r];
-            const int row = qt * 128 + r;
-            const float* vmean = stats + (long long)bh_kv * 4 * D + D;
+            // out = O / l * v_scale + v_mean for this lane's D/2 columns
+            const float inv = 1.0f / (l + __shfl_xor_sync(0xffffffffu, l, 16));
+            const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
             const float* vscale = vmean + D;
-            uint16_t* orow = out + (long long)b * g.o_sb + (long long)row * g.o_st + (long long)h * g.o_sh;
+            uint16_t* orow =
+                out + (long long)b * g.o_sb + (long long)qrow * g.o_st + (long long)h * g.o_sh + half * DH;
+            if (qrow < g.tokens) {
 #pragma unroll
-            for (int c = 0; c < D / 32; c++) {
-                uint32_t o[32];
-                tmem_ld32(t_o + c * 32, o);
-                tmem_wait_ld();
-                if (row < g.tokens) {
+                for (int c = 0; c < DH; c += 8) {
+                    uint32_t w[4];
 #pragma unroll
-                    for (int e8 = 0; e8 < 4; e8++) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e2 = 0; e2 < 4; e2++) {
-                            const int e = e8 * 8 + e2 * 2, d = c * 32 + e;
-                            const float y0 = fmaf(__uint_as_float(o[e]) * inv, __ldg(vscale + d), __ldg(vmean + d));
-                            const float y1 =
-                                fmaf(__uint_as_float(o[e + 1]) * inv, __ldg(vscale + d + 1), __ldg(vmean + d + 1));
-                            w[e2] = pack_bf16x2(y0, y1);
-                        }
-                        *reinterpret_cast<uint4*>(orow + c * 32 + e8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+                    for (int e2 = 0; e2 < 4; e2++) {
+                        const int d = c + 2 * e2;
+                        const float y0 = fmaf(o[d] * inv, __ldg(vscale + d), __ldg(vmean + d));
+                        const float y1 = fmaf(o[d + 1] * inv, __ldg(vscale + d + 1), __ldg(vmean + d + 1));
+                        w[e2] = pack_bf16x2(y0, y1);
                     }
+                    *reinterpret_cast<uint4*>(orow + c) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
         }
@@ -419,7 +436,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == MMA_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 template <int D, bool CAUSAL, bool MERGE>
@@ -451,6 +468,12 @@ cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const
     return causal ? attend_t<128, true, false>(maps, buf, g, out, st)
                   : attend_t<128, false, false>(maps, buf, g, out, st);
 }
+
+#ifdef SP_TRACE
+extern "C" int spl_sage_debug_trace(unsigned long long* host, int n) {
+    return (int)cudaMemcpyFromSymbol(host, sp_trace_buf, sizeof(unsigned long long) * (n < 4096 ? n : 4096));
+}
+#endif
 
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes) {
     cudaFuncAttributes a;

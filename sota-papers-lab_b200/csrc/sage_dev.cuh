@@ -60,10 +60,74 @@ __device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d) {
     return s8(a) | (s8(b) << 8) | (s8(c) << 16) | (s8(d) << 24);
 }
 
+// Four floats -> four E4M3 bytes in one register, a in the lowest byte; the
+// two halves are joined by register pairing rather than shifts.
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+    uint32_t r;
+    asm("{\n .reg .b16 lo, hi;\n"
+        " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
+        " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
+        " mov.b32 %0, {lo, hi};\n}"
+        : "=r"(r)
+        : "f"(a), "f"(b), "f"(c), "f"(d));
+    return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ---------------------------------------------------------------- packed f32x2 (sm_100)
+
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 2^y for two arguments on the FMA pipe instead of the MUFU unit (which
+// delivers only 16 results per clock per SM).  Cody-Waite style split
+// y = n + f with n = rint(y) (by adding and removing the 1.5 * 2^23
+// rounding constant) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
+// whose coefficients minimise the maximum relative error on [-0.5, 0.5]
+// (our own Remez exchange: max relative error 7.5e-5, far below an E4M3
+// step); n is added to the exponent field.  Arguments are clamped at -125 so
+// the exponent never underflows past the sign bit; 2^-125 rounds to 0 in
+// E4M3 anyway.
+__device__ __forceinline__ void exp2_poly2(float y0, float y1, float& p0, float& p1) {
+    constexpr float RND = 12582912.0f;  // 1.5 * 2^23
+    constexpr float C0 = 0.99992806f, C1 = 0.69326097f, C2 = 0.24261113f, C3 = 0.05517167f;
+    const uint64_t y = pk2(fmaxf(y0, -125.0f), fmaxf(y1, -125.0f));
+    const uint64_t t = add2(y, pk2(RND, RND));
+    const uint64_t f = sub2(y, sub2(t, pk2(RND, RND)));
+    uint64_t q = fma2(f, pk2(C3, C3), pk2(C2, C2));
+    q = fma2(q, f, pk2(C1, C1));
+    q = fma2(q, f, pk2(C0, C0));
+    float t0, t1, q0, q1;
+    upk2(t, t0, t1);
+    upk2(q, q0, q1);
+    p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
 // ---------------------------------------------------------------- misc
@@ -247,6 +311,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
           "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
+}
+
+// 16 TMEM lanes x 32 consecutive 32-bit columns, two half-warps: thread t < 16
+// reads lane (base + t), columns col..col+31; thread t >= 16 reads lane
+// (base + t - 16), columns col+SPLIT..col+SPLIT+31.
+template <int SPLIT>
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], %33;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr), "n"(SPLIT));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

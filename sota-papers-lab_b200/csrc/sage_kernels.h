@@ -61,6 +61,8 @@ cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
                           cudaStream_t st);
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes);
+cudaError_t launch_peak(int kind, int n, int iters, int sms, uint32_t* err, unsigned long long* cycles,
+                        cudaStream_t st);
 int attn_smem_bytes(int d);
 
 }  // namespace sp

@@ -1,0 +1,88 @@
+// Tensor-core peak probes for sm_100a (the analog of the reference's
+// cuda/sage_peak.cu, which measures mma.sync chains on Ada): one CTA per SM
+// issues back-to-back tcgen05.mma from shared-memory operands into TMEM
+// accumulators and the host times the launch.  The measured rates are the
+// roofline denominators the benchmark reports beside the datasheet figures.
+//
+// Kinds: 0 = kind::i8 (INT8 x INT8 -> S32), 1 = kind::f8f6f4 (E4M3 x E4M3 ->
+// F32), 2 = kind::f16 (BF16 x BF16 -> F32).  M = 128, N in {64, 128, 256},
+// K = 32 bytes per instruction (32 8-bit / 16 16-bit elements), operands
+// K-major with 128-byte swizzle; the shared memory holds zeros.
+#include "sage_dev.cuh"
+#include "sage_kernels.h"
+
+namespace sp {
+
+template <int KIND, int N>
+__global__ void __launch_bounds__(128, 1) sp_peak(int iters, uint32_t* err, unsigned long long* cycles) {
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ __align__(8) uint64_t done;
+    const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    const uint32_t sA = sbase, sB = sbase + 128 * 128;  // A: 128 rows x 128 B; B: N rows x 128 B
+    for (int i = threadIdx.x; i < (128 + N) * 128 / 16; i += blockDim.x)
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(sbase + i * 16), "r"(0u));
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&done), 1);
+        fence_barrier_init();
+    }
+    if (threadIdx.x < 32) {
+        tmem_alloc(smem_u32(&tmem_base_s), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    if (threadIdx.x == 0) {
+        constexpr uint32_t IDESC = KIND == 0   ? make_idesc(C_S32, F_S8, F_S8, 128, N)
+                                   : KIND == 1 ? make_idesc(C_F32, F_E4M3, F_E4M3, 128, N)
+                                               : make_idesc(C_F32, F_BF16, F_BF16, 128, N);
+        const unsigned long long t0 = clock64();
+        for (int it = 0; it < iters; it++) {
+            const uint32_t d = tmem + (uint32_t)((it & 1) * N);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const uint64_t a = smem_desc(sA + kk * 32, 1024, SWZ_128B), b = smem_desc(sB + kk * 32, 1024, SWZ_128B);
+                if (KIND == 0)
+                    umma_i8(d, a, b, IDESC, kk > 0);
+                else if (KIND == 1)
+                    umma_f8(d, a, b, IDESC, kk > 0);
+                else
+                    umma_bf16(d, a, b, IDESC, kk > 0);
+            }
+        }
+        tc_commit(smem_u32(&done));
+        mbar_wait(smem_u32(&done), 0, err, 60, false);
+        if (blockIdx.x == 0) *cycles = clock64() - t0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x < 32) tmem_dealloc(tmem, 512);
+}
+
+template <int KIND, int N>
+static cudaError_t peak_t(int iters, int sms, uint32_t* err, unsigned long long* cycles, cudaStream_t st) {
+    const int smem = (128 + N) * 128 + 1024;
+    cudaError_t e = cudaFuncSetAttribute(sp_peak<KIND, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    sp_peak<KIND, N><<<sms, 128, smem, st>>>(iters, err, cycles);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_peak(int kind, int n, int iters, int sms, uint32_t* err, unsigned long long* cycles,
+                        cudaStream_t st) {
+    if (kind == 0) return n == 64 ? peak_t<0, 64>(iters, sms, err, cycles, st)
+                          : n == 128 ? peak_t<0, 128>(iters, sms, err, cycles, st)
+                                     : peak_t<0, 256>(iters, sms, err, cycles, st);
+    if (kind == 1) return n == 64 ? peak_t<1, 64>(iters, sms, err, cycles, st)
+                          : n == 128 ? peak_t<1, 128>(iters, sms, err, cycles, st)
+                                     : peak_t<1, 256>(iters, sms, err, cycles, st);
+    return n == 64 ? peak_t<2, 64>(iters, sms, err, cycles, st)
+           : n == 128 ? peak_t<2, 128>(iters, sms, err, cycles, st)
+                      : peak_t<2, 256>(iters, sms, err, cycles, st);
+}
+
+}  // namespace sp
