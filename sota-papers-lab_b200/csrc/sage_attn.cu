@@ -11,7 +11,7 @@
 // |S| < 2^22) after one integer add, and the 1.5 * 2^23 offset is folded
 // into the exp2 FFMA, as the reference does.
 //
-// Structure: one CTA = 128 query rows of one (batch, q head), 10 warps.
+// Structure: one CTA = 128 query rows of one (batch, q head), 12 warps.
 //   warps 0-7  softmax + correction.  Warp w owns the 16 rows
 //              32*(w%4) + 16*(w/4) + (0..15) (its TMEM lane quarter is w%4);
 //              lane t < 16 handles keys 0-63 of every 128-key block and
@@ -21,13 +21,14 @@
 //              warp (one shuffle for the row max) and the two warps sharing
 //              an SM sub-partition run independently.  Keys 0-63 and 64-127
 //              are two 64-key k_scale blocks, so each lane has one scale.
-//   warp 8     TMA producer: Q once, then rings of 128-key INT8 K tiles and
-//              [D][128] FP8 V^T tiles (non-multicast TMA, 128B / 64B
-//              swizzle, zero fill past the end)
-//   warp 9     TMEM allocation and the MMA issuer (one thread): QK^T =
-//              tcgen05.mma kind::i8 M128 N128 into a double-buffered S, PV =
-//              tcgen05.mma kind::f8f6f4 M128 N=D with P from shared memory
-//              into a double-buffered PV
+//   warps 8-11 one service thread each, one per SM sub-partition (issuing
+//              TMA and tcgen05.mma costs the issuing sub-partition cycles):
+//              8: Q once and a ring of 128-key INT8 K tiles, 9: a ring of
+//              [D][128] FP8 V^T tiles (non-multicast TMA, 128B / 64B swizzle,
+//              zero fill past the end); 10: TMEM allocation and QK^T =
+//              tcgen05.mma kind::i8 M128 N128 into a double-buffered S;
+//              11: PV = tcgen05.mma kind::f8f6f4 M128 N=D with P from shared
+//              memory into a double-buffered PV
 // Per 16 keys, SP_EXP_POLY of the exponentials run on the FMA pipe
 // (exp2_poly2) to take load off the MUFU unit.
 // Extensions not in the reference: causal masking (blocks past the diagonal
@@ -60,11 +61,14 @@ __device__ unsigned long long sp_trace_buf[4096];
 constexpr int KST = 3;   // K ring depth
 constexpr int VST = 3;   // V ring depth
 #ifndef SP_EXP_POLY
-#define SP_EXP_POLY 2
+#define SP_EXP_POLY 4
 #endif
 constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
-constexpr int NTHREADS = 320;
-constexpr int PRODUCER_WARP = 8, MMA_WARP = 9, NSOFTMAX_WARPS = 8;
+constexpr int NTHREADS = 384;
+// One service thread per SM sub-partition (warp % 4), so that no pair of
+// softmax warps carries more issue load than another: K loads (and Q),
+// V loads, the QK^T MMAs, the PV MMAs.
+constexpr int K_WARP = 8, V_WARP = 9, QK_WARP = 10, PV_WARP = 11, NSOFTMAX_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // bits of 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;       // 1.5 * 2^23
@@ -90,8 +94,7 @@ struct Bars {
     uint64_t v_full[VST], v_empty[VST];
     uint64_t s_full[2];
     uint64_t p_full[2], p_free[2];
-    uint64_t pv_full[2], pv_free[2];
-    uint64_t mma_done;
+    uint64_t qk_done, pv_done;
 };
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -155,15 +158,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(bar(bars.s_full[i]), 1);
             mbar_init(bar(bars.p_full[i]), NSOFTMAX_WARPS);
             mbar_init(bar(bars.p_free[i]), 1);
-            mbar_init(bar(bars.pv_full[i]), 1);
-            mbar_init(bar(bars.pv_free[i]), NSOFTMAX_WARPS);
         }
-        mbar_init(bar(bars.mma_done), 1);
+        mbar_init(bar(bars.qk_done), 1);
+        mbar_init(bar(bars.pv_done), 1);
         fence_barrier_init();
     }
     __syncthreads();
     if (abort_s) return;  // uniform: an earlier CTA already failed
-    if (warp == MMA_WARP) {
+    if (warp == QK_WARP) {
         tmem_alloc(smem_u32(&tmem_base_s), TMEM_COLS);
         tmem_relinquish();
     }
@@ -172,27 +174,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
 
-    if (warp == PRODUCER_WARP) {
-        // ------------------------------------------------------------ producer
+    if (warp == K_WARP) {
+        // ------------------------------------------------------------ Q and K loads
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
-            tma_prefetch_desc(&map_v);
             mbar_expect_tx(bar(bars.q_full), L::Q_BYTES);
             tma_load_3d(sQ, &map_q, bar(bars.q_full), 0, qt * 128, bh_q);
-            int nk = 0, nv = 0;
+            int nk = 0;
             for (int j = 0; j < nb; j++) {
-                const int ks = j % KST, vs = j % VST;
+                const int ks = j % KST;
                 if (j >= KST && !mbar_wait(bar(bars.k_empty[ks]), ((j / KST) - 1) & 1, err, 1)) break;
                 SP_TR(true, 0, j, 0);
                 mbar_expect_tx(bar(bars.k_full[ks]), L::K_BYTES);
                 tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, j * BLK, bh_kv);
                 nk++;
-                if (j >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((j / VST) - 1) & 1, err, 2)) break;
-                SP_TR(true, 0, j, 1);
-                mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
-                tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), j * BLK, 0, bh_kv);
-                nv++;
             }
             // Drain: every load issued lands before the CTA exits (these
             // waits ignore the error word and stop only at the time limit).
@@ -201,13 +197,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int last = s + ((nk - 1 - s) / KST) * KST;
                 mbar_wait(bar(bars.k_full[s]), (last / KST) & 1, err, 4, false);
             }
+        }
+    } else if (warp == V_WARP) {
+        // ------------------------------------------------------------ V loads
+        if (lane == 0) {
+            tma_prefetch_desc(&map_v);
+            int nv = 0;
+            for (int j = 0; j < nb; j++) {
+                const int vs = j % VST;
+                if (j >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((j / VST) - 1) & 1, err, 2)) break;
+                SP_TR(true, 0, j, 1);
+                mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
+                tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), j * BLK, 0, bh_kv);
+                nv++;
+            }
             for (int s = 0; s < VST && s < nv; s++) {
                 const int last = s + ((nv - 1 - s) / VST) * VST;
                 mbar_wait(bar(bars.v_full[s]), (last / VST) & 1, err, 5, false);
             }
         }
-    } else if (warp == MMA_WARP) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == QK_WARP) {
+        // ------------------------------------------------------------ QK^T issuer
         if (lane == 0) {
             bool ok = mbar_wait(bar(bars.q_full), 0, err, 10);
             auto issue_qk = [&](int jj) -> bool {
@@ -227,15 +237,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             };
             if (ok) ok = issue_qk(0);
             if (ok && nb > 1) ok = issue_qk(1);
+            for (int j = 0; j + 2 < nb && ok; j++) {
+                // S[j % 2] has been read by every softmax warp
+                ok = mbar_wait(bar(bars.p_full[j & 1]), (j >> 1) & 1, err, 12);
+                SP_TR(true, 1, j, 1);
+                if (ok) ok = issue_qk(j + 2);
+            }
+            // No MMA may be in flight when TMEM is freed.
+            tc_commit(bar(bars.qk_done));
+            mbar_wait(bar(bars.qk_done), 0, err, 15, false);
+        }
+    } else if (warp == PV_WARP) {
+        // ------------------------------------------------------------ PV issuer
+        if (lane == 0) {
+            bool ok = true;
             for (int j = 0; j < nb && ok; j++) {
                 const int pb = j & 1, vs = j % VST;
-                ok = mbar_wait(bar(bars.p_full[pb]), (j >> 1) & 1, err, 12);
-                if (!ok) break;
-                SP_TR(true, 1, j, 1);
-                // S[pb] has been read: start the QK^T two blocks ahead first.
-                if (j + 2 < nb && !(ok = issue_qk(j + 2))) break;
-                if (j >= 2) ok = mbar_wait(bar(bars.pv_free[pb]), ((j >> 1) - 1) & 1, err, 13);
-                SP_TR(true, 1, j, 2);
+                // P(j) is written; p_full(j) also means every warp has folded
+                // PV(j - 2) into its O, so PV buffer pb is free.
+                ok = mbar_wait(bar(bars.p_full[pb]), (j >> 1) & 1, err, 13);
                 if (ok) ok = mbar_wait(bar(bars.v_full[vs]), (j / VST) & 1, err, 14);
                 if (!ok) break;
                 SP_TR(true, 1, j, 3);
@@ -246,13 +266,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int kk = 0; kk < BLK / 32; kk++)
                     umma_f8(d_pv, smem_desc(paddr + kk * 32, 1024, SWZ_128B),
                             smem_desc(vaddr + kk * 32, 1024, SWZ_128B), IDESC_PV, kk > 0);
-                tc_commit(bar(bars.pv_full[pb]));
                 tc_commit(bar(bars.v_empty[vs]));
                 tc_commit(bar(bars.p_free[pb]));
             }
-            // No MMA may be in flight when TMEM is freed.
-            tc_commit(bar(bars.mma_done));
-            mbar_wait(bar(bars.mma_done), 0, err, 15, false);
+            tc_commit(bar(bars.pv_done));
+            mbar_wait(bar(bars.pv_done), 0, err, 16, false);
         }
     } else {
         // ------------------------------------------------------------ softmax + correction
@@ -276,9 +294,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         bool ok = true;
         // O = O * a + PV[block jj] for this lane's D/2 columns: the second
         // level of the FP32 accumulation (each block's PV starts from zero).
+        // Waiting for p_free[jj % 2] (committed after PV(jj)) also frees
+        // the P buffer of block jj + 2.
         auto correct = [&](int jj, float a) -> bool {
             const int pb = jj & 1;
-            if (!warp_wait(bar(bars.pv_full[pb]), (jj >> 1) & 1, err, 31)) return false;
+            if (!warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31)) return false;
             SP_TR(lane == 0 && warp == 0, 2, jj, 6);
             tc_fence_after();
             const uint64_t a2 = pk2(a, a);
@@ -294,9 +314,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                          o[c + e], o[c + e + 1]);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(bars.pv_free[pb]));  // one arrival per warp
             return true;
         };
         for (int j = 0; j < nb; j++) {
@@ -354,11 +371,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float alpha = ex2(m - mnew);
             m = mnew;
             SP_TR(lane == 0 && warp == 0, 2, j, 2);
-            // P = 448 * 2^(x - m) as E4M3 into the swizzled P tile.
-            if (j >= 2 && !warp_wait(bar(bars.p_free[sb]), ((j >> 1) - 1) & 1, err, 21)) {
-                ok = false;
-                break;
-            }
+            // P = 448 * 2^(x - m) as E4M3 into the swizzled P tile (buffer
+            // sb is free: PV(j - 2) is done, see correct()).
             SP_TR(lane == 0 && warp == 0, 2, j, 3);
             const uint32_t prow_addr = sP + sb * L::P_BYTES + prow;
             const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
@@ -436,7 +450,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == MMA_WARP) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == QK_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 template <int D, bool CAUSAL, bool MERGE>
