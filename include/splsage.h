@@ -168,6 +168,47 @@ int spl_sage_status(spl_sage* s, spl_sage_ws* ws, uint32_t* device_error_word);
  * local (spill) bytes of the attention kernel. */
 int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes);
 
+/* The QKV side of one transformer block: Gemm::linear_bf16 (gemm.rs:268-292,
+ * y = x w^T + bias, fp32 accumulate, bf16 out) and QkvPrologue::run
+ * (qkv.rs:228-301: split q | k | v, RoPE, head-major bf16) in one tcgen05
+ * GEMM with a fused epilogue.  x bf16 [batch*tokens][hidden]; w bf16
+ * [(heads + 2*kv_heads)*head_dim][hidden] (q rows, then k, then v); bias bf16
+ * [(heads + 2*kv_heads)*head_dim] or NULL; rope NULL or f32
+ * [frame_len][head_dim/2][2] (cos, sin; RopeTable, qkv.rs:65-131) applied to
+ * q and k with pairs (d, d ^ rope_half) (16 or 32 at head dim 64, 64 at 128),
+ * table row = token % frame_len.  Writes q bf16 [batch][tokens][heads][D],
+ * k and v bf16 [batch][tokens][kv_heads][D].  The q, k and v widths must be
+ * multiples of 256 channels. */
+typedef struct {
+    int64_t batch;
+    int64_t tokens;
+    int64_t hidden;
+    int64_t heads;
+    int64_t kv_heads; /* 0 = heads */
+    int32_t rope_half;
+    int32_t frame_len;
+} spl_sage_qkv_shape;
+
+int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const void* bias,
+                      const float* rope, void* q, void* k, void* v);
+
+/* spl_sage_qkv_gemm into q, k, v (bf16 scratch the caller owns), then
+ * spl_sage_prepare of ws from them: the block's whole QKV path up to the
+ * quantised tensors the attention reads. */
+int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_shape* shape, const void* x,
+                            const void* w, const void* bias, const float* rope, void* q, void* k, void* v,
+                            const spl_sage_options* opts);
+
+/* A 1-D RoPE table (Llama-style rotate-half, angle = t * base^(-p / (D/2))
+ * for pair p) in the layout spl_sage_qkv_gemm reads, computed in f64 and
+ * stored f32 like RopeTable::from_angles (qkv.rs:78-96).  Host memory,
+ * positions * head_dim floats. */
+int spl_sage_rope_table_1d(double base, int head_dim, int64_t positions, float* out);
+
+/* Reads and clears the engine's own device error word (kernels launched
+ * without a workspace, e.g. spl_sage_qkv_gemm).  Synchronises the stream. */
+int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word);
+
 /* Tensor-core peak probe (the analog of the reference's sage_peak kernels,
  * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
  * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n

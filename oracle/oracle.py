@@ -79,6 +79,7 @@ def lib():
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
         L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom), ctypes.c_int, ctypes.c_int, P]
         L.or_layer_norm.argtypes = [P, P, P, ctypes.c_int, ctypes.c_float]
+        L.or_qkv_reference.argtypes = [P, P, P, P] + [ctypes.c_int] * 10 + [P, P, P]
         L.or_errors.argtypes = [P, P, ctypes.c_int64, P]
         L.or_flops.restype = ctypes.c_double
         L.or_flops.argtypes = [ctypes.c_int] * 5
@@ -279,6 +280,22 @@ def sage_emulate(qt: Quant, g: Geom, *, causal=False, nthreads=None) -> np.ndarr
     lib().or_sage_emulate(_p(qt.q8), _p(qt.q_scale), _p(qt.k8), _p(qt.k_scale), _p(qt.v8), _p(qt.stats),
                           _p(qt.kbias), ctypes.byref(g), int(causal), nthreads or os.cpu_count() or 1, _p(out))
     return out
+
+
+def qkv_reference(x, w, bias, rope, *, tokens, hq, hkv, d, rope_half=0, frame_len=1, nthreads=None):
+    """f64 QKV GEMM + prologue (host::linear + qkv::reference): x bf16 bits
+    [m][k], w [n][k], bias [n] or None, rope f32 [frame_len][d/2][2] or None.
+    Returns f32 q [m][hq][d], k [m][hkv][d], v [m][hkv][d]."""
+    m, k = x.shape
+    n = w.shape[0]
+    q = np.zeros((m, hq, d), np.float32)
+    kk = np.zeros((m, hkv, d), np.float32)
+    v = np.zeros((m, hkv, d), np.float32)
+    lib().or_qkv_reference(_p(np.ascontiguousarray(x)), _p(np.ascontiguousarray(w)),
+                           _p(None if bias is None else np.ascontiguousarray(bias)),
+                           _p(None if rope is None else np.ascontiguousarray(rope, np.float32)), rope_half, frame_len,
+                           m, n, k, tokens, hq, hkv, d, nthreads or os.cpu_count() or 1, _p(q), _p(kk), _p(v))
+    return q, kk, v
 
 
 def errors(ours, ref) -> dict:

@@ -720,3 +720,70 @@ void or_errors(const float* ours, const float* ref, int64_t n, double* out) {
 double or_flops(int batch, int heads, int tq, int tk, int d) {
     return 4.0 * (double)batch * heads * (double)tq * (double)tk * (double)d;
 }
+
+/* ------------------------------------------------------------------ QKV path */
+
+typedef struct {
+    const uint16_t *x, *w, *bias;
+    const float* rope;
+    int rope_half, frame_len, m, n, k, tokens, hq, hkv, d;
+    float *q, *kk, *v;
+    int64_t next;
+    pthread_mutex_t mu;
+} qkv_job;
+
+static void* qkv_worker(void* arg) {
+    qkv_job* J = (qkv_job*)arg;
+    double* y = (double*)malloc(sizeof(double) * (size_t)J->n);
+    double* xr = (double*)malloc(sizeof(double) * (size_t)J->k);
+    for (;;) {
+        pthread_mutex_lock(&J->mu);
+        int64_t r = J->next++;
+        pthread_mutex_unlock(&J->mu);
+        if (r >= J->m) break;
+        for (int i = 0; i < J->k; i++) xr[i] = (double)or_bf16_to_f32(J->x[r * J->k + i]);
+        for (int c = 0; c < J->n; c++) {
+            const uint16_t* wc = J->w + (int64_t)c * J->k;
+            double acc = 0.0;
+            for (int i = 0; i < J->k; i++) acc += xr[i] * (double)or_bf16_to_f32(wc[i]);
+            y[c] = acc + (J->bias ? (double)or_bf16_to_f32(J->bias[c]) : 0.0);
+        }
+        const int d = J->d, tok = (int)(r % J->tokens), half = J->rope_half;
+        for (int part = 0; part < 3; part++) {
+            const int heads = part == 0 ? J->hq : J->hkv;
+            const int c0 = part == 0 ? 0 : (part == 1 ? J->hq * d : (J->hq + J->hkv) * d);
+            float* out = part == 0 ? J->q : (part == 1 ? J->kk : J->v);
+            for (int h = 0; h < heads; h++) {
+                const double* src = y + c0 + h * d;
+                float* dst = out + (r * heads + h) * (int64_t)d;
+                for (int e = 0; e < d; e++) {
+                    double val = src[e];
+                    if (J->rope && part < 2) {
+                        const int pair = (e / (2 * half)) * half + (e & (half - 1));
+                        const float* cs = J->rope + ((int64_t)(tok % J->frame_len) * (d / 2) + pair) * 2;
+                        const double p = src[e ^ half];
+                        val = (e & half) ? src[e] * (double)cs[0] + p * (double)cs[1]
+                                         : src[e] * (double)cs[0] - p * (double)cs[1];
+                    }
+                    dst[e] = (float)val;
+                }
+            }
+        }
+    }
+    free(y);
+    free(xr);
+    return NULL;
+}
+
+void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias, const float* rope, int rope_half,
+                      int frame_len, int m, int n, int k, int tokens, int hq, int hkv, int d, int nthreads, float* q,
+                      float* kk, float* v) {
+    qkv_job J = {x, w, bias, rope, rope_half, frame_len, m, n, k, tokens, hq, hkv, d, q, kk, v, 0};
+    pthread_mutex_init(&J.mu, NULL);
+    if (nthreads < 1) nthreads = 1;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * nthreads);
+    for (int i = 0; i < nthreads; i++) pthread_create(&th[i], NULL, qkv_worker, &J);
+    for (int i = 0; i < nthreads; i++) pthread_join(th[i], NULL);
+    free(th);
+    pthread_mutex_destroy(&J.mu);
+}

@@ -128,6 +128,17 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
                      const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
                      int nthreads, float* out);
 
+/* The QKV path of one block in f64: y = x w^T + bias (host::linear,
+ * platform/spl-nn/src/host.rs) then the QKV prologue (qkv::reference,
+ * platform/spl-nn/src/qkv.rs:306-372, generalised to head dim 128 and any
+ * RoPE pair distance): split q | k | v, RoPE x*cos -+ partner*sin on q and k
+ * with partner d ^ rope_half and table row token % frame_len.  x bf16
+ * [m][k], w bf16 [n][k], bias bf16 [n] or NULL, rope f32 [frame_len][d/2][2]
+ * or NULL.  Outputs f32 q [m][hq][d], k and v [m][hkv][d]. */
+void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias, const float* rope, int rope_half,
+                      int frame_len, int m, int n, int k, int tokens, int hq, int hkv, int d, int nthreads, float* q,
+                      float* kk, float* v);
+
 /* LayerNorm of one row in f64 (reference.rs:110-118). */
 void or_layer_norm(float* x, const float* w, const float* b, int n, float eps);
 

@@ -77,6 +77,12 @@ class _Options(ctypes.Structure):
                 ("qk_norm_eps", ctypes.c_float), ("reserved2", ctypes.c_int32)]
 
 
+class _QkvShape(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("tokens", ctypes.c_int64), ("hidden", ctypes.c_int64),
+                ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64), ("rope_half", ctypes.c_int32),
+                ("frame_len", ctypes.c_int32)]
+
+
 class _Plan(ctypes.Structure):
     _fields_ = [("tq_pad", ctypes.c_int64), ("tk", ctypes.c_int64), ("tk_pad", ctypes.c_int64)]
 
@@ -86,6 +92,7 @@ EXPORTS = [
     "spl_sage_workspace_create", "spl_sage_ws_destroy", "spl_sage_ws_bytes", "spl_sage_ws_plan", "spl_sage_prepare",
     "spl_sage_attend", "spl_sage_forward", "spl_sage_ws_export_reference_layout", "spl_sage_status",
     "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version", "spl_sage_tensor_peak",
+    "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
 ]
 
 _lib = None
@@ -117,6 +124,10 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_status.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint32)]
         L.spl_sage_attn_resources.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
         L.spl_sage_tensor_peak.argtypes = [P, I, I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+        L.spl_sage_qkv_gemm.argtypes = [P, ctypes.POINTER(_QkvShape)] + [P] * 7
+        L.spl_sage_qkv_gemm_quant.argtypes = [P, P, ctypes.POINTER(_QkvShape)] + [P] * 7 + [ctypes.POINTER(_Options)]
+        L.spl_sage_rope_table_1d.argtypes = [ctypes.c_double, I, ctypes.c_int64, P]
+        L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
         L.spl_sage_flops.restype = ctypes.c_double
         L.spl_sage_flops.argtypes = [P]
         L.spl_sage_last_error.restype = ctypes.c_char_p
@@ -371,6 +382,29 @@ class SageAttention:
         _check(lib().spl_sage_tensor_peak(self._h, kind, n, iters, ctypes.byref(t), ctypes.byref(c)))
         return t.value, c.value
 
+    def qkv_gemm(self, x, w, bias, rope, q, k, v, *, batch: int, tokens: int, heads: int, kv_heads: int = 0,
+                 rope_half: int = 0, frame_len: int = 0):
+        """Gemm::linear_bf16 + QkvPrologue::run fused (spl_sage_qkv_gemm): x
+        [batch*tokens][hidden], w [(heads+2*kv)*D][hidden], bias or None,
+        rope (f32 [frame_len][D/2][2]) or None; writes q/k/v bf16 [B][T][H][D]."""
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        sh = _QkvShape(batch, tokens, x.shape[-1], heads, kv_heads, rope_half, frame_len)
+        _check(lib().spl_sage_qkv_gemm(self._h, ctypes.byref(sh), p(x), p(w), p(bias), p(rope), p(q), p(k), p(v)))
+
+    def qkv_gemm_quant(self, ws: Workspace, x, w, bias, rope, q, k, v, opts: Options | None = None, *,
+                       rope_half: int = 0, frame_len: int = 0):
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        s = ws.plan.shape
+        sh = _QkvShape(s.batch, s.tokens, x.shape[-1], s.heads, s.kv_heads, rope_half, frame_len)
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_qkv_gemm_quant(self._h, ws._h, ctypes.byref(sh), p(x), p(w), p(bias), p(rope), p(q),
+                                             p(k), p(v), ctypes.byref(o)))
+
+    def engine_status(self) -> int:
+        w = ctypes.c_uint32()
+        _check(lib().spl_sage_engine_status(self._h, ctypes.byref(w)))
+        return w.value
+
     def workspace(self, shape: Shape, merge: KvMerge | None = None) -> Workspace:
         merge = merge or KvMerge.dense()
         cs = _Shape(shape.batch, shape.heads, shape.kv_heads, shape.tokens, int(shape.causal), 0)
@@ -408,6 +442,14 @@ class SageAttention:
         w = ctypes.c_uint32()
         _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
         return w.value
+
+
+def rope_table_1d(base: float, head_dim: int, positions: int):
+    """A Llama-style 1-D RoPE table (f32 numpy [positions][D/2][2])."""
+    import numpy as np
+    out = np.empty((positions, head_dim // 2, 2), np.float32)
+    _check(lib().spl_sage_rope_table_1d(base, head_dim, positions, out.ctypes.data_as(ctypes.c_void_p)))
+    return out
 
 
 def flops(plan: Plan, head_dim: int) -> float:

@@ -1,0 +1,209 @@
+// Fused QKV projection for sm_100a: y = x W^T (+ bias) on the tcgen05 tensor
+// cores (kind::f16, BF16 x BF16 -> FP32 in TMEM), with the QKV prologue in the
+// epilogue: split q | k | v, bias, round to bf16 (the reference's GEMM writes
+// bf16: platform/spl-nn/src/gemm.rs:408-416), RoPE on q and k from a
+// (cos, sin) table with the reference's pairing rule
+// (platform/spl-nn/cuda/qkv.cu:102-119: the partner of channel d is d ^ half,
+// pair (d / 2half) * half + d % half), round to bf16 again (qkv.cu:121-133),
+// and write Q, K, V in [B][T][H][D] for the quantiser.
+//
+// Tile: 128 rows x 256 output channels (two heads of 128 or four of 64), K in
+// 64-element (128-byte) blocks through a 4-stage TMA ring.  Warp 0 loads,
+// warp 1 issues the MMAs (4 x M128 N256 K16 per block) and owns the 256 TMEM
+// columns, warps 4-7 run the epilogue, one thread per row.
+#include "sage_dev.cuh"
+#include "sage_kernels.h"
+
+namespace sp {
+
+namespace gemm {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+constexpr int NTHREADS = 256;
+}  // namespace gemm
+
+// HALF: distance between the two channels of a RoPE pair (0: no RoPE).
+template <int D, int HALF>
+__global__ void __launch_bounds__(gemm::NTHREADS, 1)
+    sp_qkv_gemm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                const uint16_t* __restrict__ bias, const float2* __restrict__ rope, uint16_t* __restrict__ q_out,
+                uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, uint32_t* __restrict__ err,
+                const QkvGeom g) {
+    using namespace gemm;
+    constexpr uint32_t IDESC = make_idesc(C_F32, F_BF16, F_BF16, BM, BN);
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full;
+    __shared__ uint32_t tmem_base_s;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kblocks = (g.k + BK - 1) / BK;
+    const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    auto bar = [](uint64_t& x) { return smem_u32(&x); };
+
+    if (tid == 0) {
+        for (int i = 0; i < STAGES; i++) {
+            mbar_init(bar(full[i]), 1);
+            mbar_init(bar(empty[i]), 1);
+        }
+        mbar_init(bar(acc_full), 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&tmem_base_s), BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&map_x);
+            tma_prefetch_desc(&map_w);
+            int issued = 0;
+            for (int kb = 0; kb < kblocks; kb++) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !mbar_wait(bar(empty[s]), ((kb / STAGES) - 1) & 1, err, 40)) break;
+                const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+                mbar_expect_tx(bar(full[s]), STAGE_BYTES);
+                tma_load_2d(sa, &map_x, bar(full[s]), kb * BK, m0);
+                tma_load_2d(sb, &map_w, bar(full[s]), kb * BK, n0);
+                issued++;
+            }
+            for (int s = 0; s < STAGES && s < issued; s++) {
+                const int last = s + ((issued - 1 - s) / STAGES) * STAGES;
+                mbar_wait(bar(full[s]), (last / STAGES) & 1, err, 41, false);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int kb = 0; kb < kblocks && ok; kb++) {
+                const int s = kb % STAGES;
+                ok = mbar_wait(bar(full[s]), (kb / STAGES) & 1, err, 42);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)
+                    umma_bf16(tmem, smem_desc(sa + kk * 32, 1024, SWZ_128B), smem_desc(sb + kk * 32, 1024, SWZ_128B),
+                              IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(bar(empty[s]));
+            }
+            tc_commit(bar(acc_full));
+            mbar_wait(bar(acc_full), 0, err, 43, false);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ epilogue, one thread per row
+        const int r = tid - 128;
+        const int row = m0 + r;
+        const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+        const bool ok = warp_all_wait(bar(acc_full), 0, err, 44);
+        if (ok) {
+            tc_fence_after();
+            const int bb = row / g.tokens, tok = row % g.tokens;
+            // the row's position inside its frame selects the RoPE table row
+            const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
+#pragma unroll 1
+            for (int hh = 0; hh < BN / D; hh++) {
+                const int c0 = n0 + hh * D;  // first output channel of this head
+                // which part and head (q | k | v, each part a whole number of heads)
+                int part, head;
+                if (c0 < g.hq * D) {
+                    part = 0;
+                    head = c0 / D;
+                } else if (c0 < (g.hq + g.hkv) * D) {
+                    part = 1;
+                    head = (c0 - g.hq * D) / D;
+                } else {
+                    part = 2;
+                    head = (c0 - (g.hq + g.hkv) * D) / D;
+                }
+                float x[D];
+#pragma unroll
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + lane_off + hh * D + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        float y = __uint_as_float(v[e]);
+                        if (bias) y += __uint_as_float((uint32_t)bias[c0 + c + e] << 16);
+                        x[c + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);  // the GEMM's bf16 output
+                    }
+                }
+                if (HALF && part < 2) {
+                    // each (d, d + HALF) pair shares one table entry
+#pragma unroll
+                    for (int d = 0; d < D; d++) {
+                        if (d & HALF) continue;
+                        const int pair = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
+                        const float2 cs = __ldg(rt + pair);
+                        const float a = x[d], b = x[d | HALF];
+                        x[d] = a * cs.x - b * cs.y;
+                        x[d | HALF] = b * cs.x + a * cs.y;
+                    }
+                }
+                if (row < g.m) {
+                    uint16_t* dst = (part == 0 ? q_out : part == 1 ? k_out : v_out) +
+                                    ((long long)bb * g.tokens + tok) * (long long)(part == 0 ? g.hq : g.hkv) * D +
+                                    (long long)head * D;
+#pragma unroll
+                    for (int c = 0; c < D; c += 8) {
+                        uint4 w;
+                        w.x = pack_bf16x2(x[c], x[c + 1]);
+                        w.y = pack_bf16x2(x[c + 2], x[c + 3]);
+                        w.z = pack_bf16x2(x[c + 4], x[c + 5]);
+                        w.w = pack_bf16x2(x[c + 6], x[c + 7]);
+                        *reinterpret_cast<uint4*>(dst + c) = w;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, BN);
+}
+
+template <int D, int HALF>
+static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q, uint16_t* k,
+                         uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    static unsigned attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !(attr_set & (1u << dev))) {
+        cudaError_t e =
+            cudaFuncSetAttribute(sp_qkv_gemm<D, HALF>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) attr_set |= 1u << dev;
+    }
+    dim3 grid(g.n / gemm::BN, (g.m + gemm::BM - 1) / gemm::BM);
+    sp_qkv_gemm<D, HALF><<<grid, gemm::NTHREADS, gemm::SMEM, st>>>(maps.x, maps.w, bias, (const float2*)rope, q, k,
+                                                                   v, err, g);
+    return cudaGetLastError();
+}
+
+// RoPE pairings: none; D=64 with pairs (i, i+16) in each 32-wide half (VGGT
+// 2-D) or (i, i+32) (DINOv3); D=128 with (i, i+64) (rotate-half, Llama).
+cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q,
+                            uint16_t* k, uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    const int half = rope ? g.rope_half : 0;
+    if (d == 64) {
+        if (half == 0) return qkv_t<64, 0>(maps, bias, rope, q, k, v, err, g, st);
+        if (half == 16) return qkv_t<64, 16>(maps, bias, rope, q, k, v, err, g, st);
+        if (half == 32) return qkv_t<64, 32>(maps, bias, rope, q, k, v, err, g, st);
+        return cudaErrorInvalidValue;
+    }
+    if (half == 0) return qkv_t<128, 0>(maps, bias, rope, q, k, v, err, g, st);
+    if (half == 64) return qkv_t<128, 64>(maps, bias, rope, q, k, v, err, g, st);
+    return cudaErrorInvalidValue;
+}
+
+int qkv_smem_bytes() { return gemm::SMEM; }
+
+}  // namespace sp

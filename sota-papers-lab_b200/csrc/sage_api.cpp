@@ -72,6 +72,23 @@ int make_map(CUtensorMap* m, void* base, uint64_t d0, uint64_t d1, uint64_t d2, 
     return SPL_SAGE_OK;
 }
 
+// A 2-D BF16 tensor map {d0, d1} with row pitch p1 (bytes), box {b0, b1},
+// 128-byte swizzle, zero fill out of bounds.
+int make_map_bf16_2d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t p1, uint32_t b0,
+                     uint32_t b1) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = {d0, d1};
+    cuuint64_t strides[1] = {p1};
+    cuuint32_t box[2] = {b0, b1};
+    cuuint32_t elem[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return SPL_SAGE_OK;
+}
+
 bool fits_i32(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
 
 }  // namespace
@@ -81,6 +98,7 @@ struct spl_sage {
     int head_dim;
     spl_sage_config config;
     int device;
+    uint32_t* err;  // device error word of the calls that run without a workspace
 };
 
 struct spl_sage_ws {
@@ -148,16 +166,29 @@ int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_
                     "sage attention needs an sm_100 GPU (B200: tcgen05 tensor cores, compute capability 10.0); "
                     "this GPU is %d.%d",
                     major, minor);
+    uint32_t* errw = nullptr;
+    e = cudaMalloc(&errw, 256);
+    if (e != cudaSuccess) return cuda_fail(e, "allocate the engine's error word");
+    e = cudaMemsetAsync(errw, 0, 256, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        cudaFree(errw);
+        return cuda_fail(e, "zero the engine's error word");
+    }
     spl_sage* s = new spl_sage;
     s->stream = (cudaStream_t)stream;
     s->head_dim = head_dim;
     s->config = c;
     s->device = dev;
+    s->err = errw;
     *out = s;
     return SPL_SAGE_OK;
 }
 
-void spl_sage_destroy(spl_sage* s) { delete s; }
+void spl_sage_destroy(spl_sage* s) {
+    if (!s) return;
+    cudaFree(s->err);
+    delete s;
+}
 
 int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
                               spl_sage_ws** out) {
@@ -478,6 +509,98 @@ int spl_sage_tensor_peak(spl_sage* s, int kind, int n, int iters, double* tops, 
     const double ops = 2.0 * 128.0 * n * k_elems * 4.0 * iters * sms;
     *tops = ops / (ms * 1e-3) / 1e12;
     if (cycles_per_mma) *cycles_per_mma = (double)c / (4.0 * iters);
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_rope_table_1d(double base, int head_dim, int64_t positions, float* out) {
+    if (!out || positions <= 0 || (head_dim != 64 && head_dim != 128) || !(base > 1.0))
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_rope_table_1d: bad arguments");
+    const int pairs = head_dim / 2;
+    for (int64_t t = 0; t < positions; t++)
+        for (int p = 0; p < pairs; p++) {
+            // RopeTable::from_angles (qkv.rs:78-96): cos / sin in f64, stored f32
+            const double a = (double)t * pow(base, -(double)p / (double)pairs);
+            out[(t * pairs + p) * 2] = (float)cos(a);
+            out[(t * pairs + p) * 2 + 1] = (float)sin(a);
+        }
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const void* bias,
+                      const float* rope, void* q, void* k, void* v) {
+    if (!s || !shape || !x || !w || !q || !k || !v)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm: NULL argument");
+    const spl_sage_qkv_shape& sh = *shape;
+    const int64_t D = s->head_dim;
+    const int64_t G = sh.kv_heads ? sh.kv_heads : sh.heads;
+    const int64_t m = sh.batch * sh.tokens, n = (sh.heads + 2 * G) * D, kd = sh.hidden;
+    if (sh.batch <= 0 || sh.tokens <= 0 || sh.heads <= 0 || kd <= 0)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: empty shape");
+    if (n % 256 != 0 || (sh.heads * D) % 256 != 0 || (G * D) % 256 != 0)
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "qkv: q and k/v widths (%lld, %lld channels) must be multiples of 256 (the GEMM tile)",
+                    (long long)(sh.heads * D), (long long)(G * D));
+    if (kd % 8 != 0) return fail(SPL_SAGE_ERR_INVALID, "qkv: hidden size %lld must be a multiple of 8", (long long)kd);
+    if (!fits_i32(m) || !fits_i32(n) || !fits_i32(kd)) return fail(SPL_SAGE_ERR_INVALID, "qkv: size does not fit i32");
+    if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: buffers must be 16-byte aligned");
+    int half = 0;
+    if (rope) {
+        half = sh.rope_half;
+        const bool okh = D == 64 ? (half == 16 || half == 32) : half == 64;
+        if (!okh) return fail(SPL_SAGE_ERR_INVALID, "qkv: RoPE pair distance %d unsupported for head dim %lld", half,
+                              (long long)D);
+        if (sh.frame_len <= 0) return fail(SPL_SAGE_ERR_INVALID, "qkv: RoPE frame length is 0");
+    }
+    sp::QkvMaps maps;
+    int rc = make_map_bf16_2d(&maps.x, x, kd, m, kd * 2, 64, 128);
+    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, kd, n, kd * 2, 64, 256);
+    if (rc != SPL_SAGE_OK) return rc;
+    sp::QkvGeom g;
+    g.m = (int)m;
+    g.n = (int)n;
+    g.k = (int)kd;
+    g.tokens = (int)sh.tokens;
+    g.hq = (int)sh.heads;
+    g.hkv = (int)G;
+    g.frame_len = rope ? (int)sh.frame_len : 1;
+    g.rope_half = half;
+    cudaError_t e = sp::launch_qkv_gemm((int)D, maps, (const uint16_t*)bias, rope, (uint16_t*)q, (uint16_t*)k,
+                                        (uint16_t*)v, s->err, g, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_shape* shape, const void* x,
+                            const void* w, const void* bias, const float* rope, void* q, void* k, void* v,
+                            const spl_sage_options* opts) {
+    if (!s || !ws || !shape) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm_quant: NULL argument");
+    const spl_sage_qkv_shape& sh = *shape;
+    const int64_t G = sh.kv_heads ? sh.kv_heads : sh.heads;
+    if (ws->shape.batch != sh.batch || ws->shape.tokens != sh.tokens || ws->shape.heads != sh.heads ||
+        ws->shape.kv_heads != G)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: the workspace was made for another shape");
+    int rc = spl_sage_qkv_gemm(s, shape, x, w, bias, rope, q, k, v);
+    if (rc) return rc;
+    const int64_t D = s->head_dim;
+    spl_sage_tensor tq = {q, sh.batch * sh.tokens * sh.heads * D, sh.tokens * sh.heads * D, sh.heads * D, D};
+    spl_sage_tensor tk = {k, sh.batch * sh.tokens * G * D, sh.tokens * G * D, G * D, D};
+    spl_sage_tensor tv = {v, sh.batch * sh.tokens * G * D, sh.tokens * G * D, G * D, D};
+    return spl_sage_prepare(s, ws, tq, tk, tv, opts);
+}
+
+int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word) {
+    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_engine_status: NULL argument");
+    uint32_t w = 0;
+    cudaError_t e = cudaMemcpyAsync(&w, s->err, 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "read engine status");
+    if (device_error_word) *device_error_word = w;
+    if (w) {
+        cudaMemsetAsync(s->err, 0, 4, s->stream);
+        return fail(SPL_SAGE_ERR_KERNEL, "kernel reported device error word 0x%08x (timeout site %u)", w,
+                    (w >> 8) & 0xff);
+    }
     return SPL_SAGE_OK;
 }
 

@@ -103,10 +103,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return r;
 }
 
-// All 32 lanes wait; the warp gives up together if any lane gave up.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t site) {
-    const bool ok = mbar_wait(bar, parity, err, site);
-    return __all_sync(0xffffffffu, ok);
+    return warp_all_wait(bar, parity, err, site);
 }
 
 template <int D, bool CAUSAL, bool MERGE>

@@ -201,6 +201,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     }
 }
 
+// All 32 lanes wait; the warp gives up together if any lane gave up.
+__device__ __forceinline__ bool warp_all_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t site) {
+    const bool ok = mbar_wait(bar, parity, err, site);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
@@ -211,6 +217,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
         ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
 }
 

@@ -55,6 +55,23 @@ struct AttnMaps {
     CUtensorMap v;  // v8 as {tk_pad, D, b*g}, box {128, D, 1}
 };
 
+// Fused QKV projection: y[m][n] = x[m][k] w[n][k]^T (+ bias[n]); columns
+// [0, hq*D) are q heads, then hkv k heads, then hkv v heads.  Rows are
+// (batch item, token) with `tokens` tokens per batch item.
+struct QkvGeom {
+    int m, n, k, tokens;
+    int hq, hkv, frame_len, rope_half;
+};
+
+struct QkvMaps {
+    CUtensorMap x;  // bf16 {k, m}, box {64, 128}
+    CUtensorMap w;  // bf16 {k, n}, box {64, 256}
+};
+
+cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q,
+                            uint16_t* k, uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st);
+int qkv_smem_bytes();
+
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                            const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);
