@@ -209,6 +209,33 @@ int spl_sage_rope_table_1d(double base, int head_dim, int64_t positions, float* 
  * without a workspace, e.g. spl_sage_qkv_gemm).  Synchronises the stream. */
 int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word);
 
+/* Quantises q, k and v exactly like spl_sage_prepare (same bytes), for
+ * callers that cannot allocate device memory: a library embedded in a host
+ * application that owns all device memory through its own pool and forbids
+ * raw cudaMalloc, or a hot path that must not take the allocator lock (or
+ * risk the device synchronisation cudaMalloc and cudaFree can cause).  It
+ * has no counterpart in the reference.  No engine, no workspace, and no
+ * cudaMalloc, cudaFree or other allocating call: the caller passes the
+ * inputs and every output, and the one piece of scratch (the per-tile
+ * channel statistics) is a fixed 4 MiB device array inside the library,
+ * which every GPU that loads the library keeps until the process exits.
+ *   - Dense keys only (no KV merging).  Limit: batch * kv_heads *
+ *     ceil(tokens / 128) * 4 * head_dim <= 1,048,576; larger calls are
+ *     rejected with SPL_SAGE_ERR_INVALID (use spl_sage_prepare).
+ *   - The first call on a device looks the array's device address up (and
+ *     caches it); make that first call before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents
+ *     (each call overwrites what it reads), so calls that overlap on the
+ *     GPU, on different streams, race.
+ * Outputs (device buffers, the workspace's own layouts): q8 i8
+ * [b][h][tq_pad][D], q_scale f32 [b][h][tq_pad/16], k8 i8 [b][g][tk_pad][D],
+ * k_scale f32 [b][g][tk_pad/64], v8 u8 [b][g][D][tk_pad] (E4M3, one row per
+ * channel, keys in order), stats f32 [b][g][4][D]; tq_pad = tokens rounded
+ * up to 128, tk_pad to 64, g = kv heads.  Stream-ordered on `stream`. */
+int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const spl_sage_shape* shape,
+                              spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v, const spl_sage_options* opts,
+                              void* q8, float* q_scale, void* k8, float* k_scale, void* v8, float* stats);
+
 /* Tensor-core peak probe (the analog of the reference's sage_peak kernels,
  * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
  * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n

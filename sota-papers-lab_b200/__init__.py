@@ -93,6 +93,7 @@ EXPORTS = [
     "spl_sage_attend", "spl_sage_forward", "spl_sage_ws_export_reference_layout", "spl_sage_status",
     "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version", "spl_sage_tensor_peak",
     "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
+    "spl_sage_quantize_noalloc",
 ]
 
 _lib = None
@@ -128,6 +129,8 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_qkv_gemm_quant.argtypes = [P, P, ctypes.POINTER(_QkvShape)] + [P] * 7 + [ctypes.POINTER(_Options)]
         L.spl_sage_rope_table_1d.argtypes = [ctypes.c_double, I, ctypes.c_int64, P]
         L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
+        L.spl_sage_quantize_noalloc.argtypes = ([P, I, I, ctypes.POINTER(_Shape), _Tensor, _Tensor, _Tensor,
+                                                 ctypes.POINTER(_Options)] + [P] * 6)
         L.spl_sage_flops.restype = ctypes.c_double
         L.spl_sage_flops.argtypes = [P]
         L.spl_sage_last_error.restype = ctypes.c_char_p
@@ -442,6 +445,23 @@ class SageAttention:
         w = ctypes.c_uint32()
         _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
         return w.value
+
+
+def quantize_noalloc(head_dim: int, shape: Shape, q: Tensor, k: Tensor, v: Tensor, q8, q_scale, k8, k_scale, v8,
+                     stats, opts: Options | None = None, pv_accum: int = PvAccum.F32, stream=None):
+    """Quantises q, k, v into caller-owned CUDA tensors without any device
+    allocation (spl_sage_quantize_noalloc; no counterpart in the reference).
+    Outputs use the workspace layouts: q8 [b][h][tq_pad][D] i8, q_scale
+    [b][h][tq_pad/16] f32, k8 [b][g][tk_pad][D] i8, k_scale [b][g][tk_pad/64]
+    f32, v8 [b][g][D][tk_pad] E4M3 bytes, stats [b][g][4][D] f32.  Dense keys
+    only; the library's fixed scratch bounds batch * kv_heads *
+    ceil(tokens/128) * 4 * D to 1,048,576."""
+    sh = _Shape(shape.batch, shape.heads, shape.kv, shape.tokens, int(shape.causal), 0)
+    o = (opts or Options())._c()
+    ptr = (lambda t: ctypes.c_void_p(t.data_ptr()))
+    _check(lib().spl_sage_quantize_noalloc(_stream_ptr(stream), head_dim, pv_accum, ctypes.byref(sh), q._c(), k._c(),
+                                           v._c(), ctypes.byref(o), ptr(q8), ptr(q_scale), ptr(k8), ptr(k_scale),
+                                           ptr(v8), ptr(stats)))
 
 
 def rope_table_1d(base: float, head_dim: int, positions: int):

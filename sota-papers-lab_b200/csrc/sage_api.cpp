@@ -589,6 +589,89 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     return spl_sage_prepare(s, ws, tq, tk, tv, opts);
 }
 
+int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const spl_sage_shape* shape,
+                              spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v, const spl_sage_options* opts,
+                              void* q8, float* q_scale, void* k8, float* k_scale, void* v8, float* stats) {
+    // Everything this call needs besides the caller's inputs and outputs is
+    // the fixed device array in sage_quant.cu: no cudaMalloc, no cudaFree.
+    if (!shape || !q8 || !q_scale || !k8 || !k_scale || !v8 || !stats)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: NULL argument");
+    if (head_dim != 64 && head_dim != 128)
+        return fail(SPL_SAGE_ERR_INVALID, "sage attention supports head dim 64 or 128, got %d", head_dim);
+    if (pv_accum != SPL_SAGE_PV_F32 && pv_accum != SPL_SAGE_PV_F16)
+        return fail(SPL_SAGE_ERR_INVALID, "unknown PV accumulation %d", pv_accum);
+    int dev = 0, major = 0, minor = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+        return fail(SPL_SAGE_ERR_DEVICE, "sage attention needs an sm_100 GPU; this GPU is %d.%d", major, minor);
+    spl_sage_shape sh = *shape;
+    if (sh.kv_heads == 0) sh.kv_heads = sh.heads;
+    if (sh.batch <= 0 || sh.heads <= 0 || sh.tokens <= 0 || sh.kv_heads <= 0 || sh.heads % sh.kv_heads)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: bad shape");
+    const int64_t D = head_dim;
+    const int64_t tq_pad = (sh.tokens + QTILE - 1) / QTILE * QTILE, tk_pad = (sh.tokens + KBLOCK - 1) / KBLOCK * KBLOCK;
+    if (!fits_i32(tq_pad) || !fits_i32(sh.batch * sh.heads))
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: size does not fit i32");
+    const int64_t part_floats = sh.batch * sh.kv_heads * (tq_pad / QTILE) * 4 * D;
+    if (part_floats > (int64_t)sp::noalloc_part_capacity())
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "spl_sage_quantize_noalloc: batch x kv_heads x ceil(tokens/128) x 4 x head_dim = %lld floats "
+                    "exceeds its fixed scratch of %lld floats; use a workspace (spl_sage_prepare)",
+                    (long long)part_floats, (long long)sp::noalloc_part_capacity());
+    spl_sage_options o;
+    if (opts)
+        o = *opts;
+    else
+        spl_sage_default_options(&o);
+    if (o.qk_norm_params && o.qk_norm_len < 4 * D)
+        return fail(SPL_SAGE_ERR_INVALID, "QK-norm params hold %lld floats, need %lld", (long long)o.qk_norm_len,
+                    (long long)(4 * D));
+    int rc;
+    if ((rc = check_tensor("Q", q.data, q.len, q.batch, q.token, q.head, sh, sh.heads, D))) return rc;
+    if ((rc = check_tensor("K", k.data, k.len, k.batch, k.token, k.head, sh, sh.kv_heads, D))) return rc;
+    if ((rc = check_tensor("V", v.data, v.len, v.batch, v.token, v.head, sh, sh.kv_heads, D))) return rc;
+    float* part = nullptr;
+    e = sp::noalloc_part_buffer(&part);
+    if (e != cudaSuccess) return cuda_fail(e, "look up the fixed quantiser scratch");
+
+    sp::Geom g;
+    memset(&g, 0, sizeof g);
+    g.q_sb = q.batch; g.q_st = q.token; g.q_sh = q.head;
+    g.k_sb = k.batch; g.k_st = k.token; g.k_sh = k.head;
+    g.v_sb = v.batch; g.v_st = v.token; g.v_sh = v.head;
+    g.batch = (int)sh.batch;
+    g.heads = (int)sh.heads;
+    g.kv_heads = (int)sh.kv_heads;
+    g.tokens = (int)sh.tokens;
+    g.tq_pad = (int)tq_pad;
+    g.tk = (int)sh.tokens;
+    g.tk_pad = (int)tk_pad;
+    g.q_tiles = (int)(tq_pad / QTILE);
+    g.merge = 1;
+    g.frames = 1;
+    g.flags = (o.qk_norm_params ? (LN_Q | LN_K) : 0) | (o.smooth_k ? SMOOTH_K : 0) | (o.smooth_v ? SMOOTH_V : 0);
+    const float scale = o.has_softmax_scale ? o.softmax_scale : 1.0f / sqrtf((float)D);
+    g.q_mul = scale * 1.44269504088896340736f;
+    g.ln_eps = o.qk_norm_params ? o.qk_norm_eps : 1e-5f;
+    g.v_range = pv_accum == SPL_SAGE_PV_F16 ? PV16_V_RANGE : FP8_MAX;
+    sp::Buffers buf;
+    memset(&buf, 0, sizeof buf);
+    buf.q8 = (int8_t*)q8;
+    buf.q_scale = q_scale;
+    buf.k8 = (int8_t*)k8;
+    buf.k_scale = k_scale;
+    buf.v8 = (uint8_t*)v8;
+    buf.stats = stats;
+    buf.kbias = nullptr;  // dense keys: the quantiser never writes kbias
+    buf.part = part;      // fully rewritten by every call before it is read
+    e = sp::launch_prepare(head_dim, q.data, k.data, v.data, o.qk_norm_params, buf, g, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage quantiser");
+    return SPL_SAGE_OK;
+}
+
 int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word) {
     if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_engine_status: NULL argument");
     uint32_t w = 0;

@@ -72,6 +72,10 @@ cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, co
                             uint16_t* k, uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st);
 int qkv_smem_bytes();
 
+// Fixed device scratch of spl_sage_quantize_noalloc (sage_quant.cu).
+cudaError_t noalloc_part_buffer(float** out);
+size_t noalloc_part_capacity();
+
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                            const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);

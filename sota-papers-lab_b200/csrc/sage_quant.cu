@@ -17,6 +17,8 @@
 //   sp_prep      grid (q_tiles, heads + kv_heads, batch)
 //   sp_finalize  grid (kv_heads, batch)
 //   sp_quant_kv  grid (tk_pad / 64, kv_heads, batch)
+#include <mutex>
+
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
@@ -401,5 +403,45 @@ cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v
         sp_export_v<128><<<blocks, 256, 0, st>>>(buf.v8, v8_ref, g);
     return cudaGetLastError();
 }
+
+}  // namespace sp
+
+// ---------------------------------------------------------------- fixed scratch for spl_sage_quantize_noalloc
+//
+// Some callers cannot allocate device memory themselves: a library embedded
+// in a host application that owns every byte of device memory through its
+// own pool (and forbids raw cudaMalloc, which can also synchronise the
+// device and fragment that pool), or code that must not take the allocator
+// lock on its hot path.  For them the quantiser's only scratch, the per-tile
+// channel statistics, lives in this fixed device array instead of a
+// workspace.  It is part of the module image, so every GPU that loads the
+// library holds it until the process exits.
+namespace sp {
+
+constexpr size_t NOALLOC_PART_FLOATS = size_t(1) << 20;  // 4 MiB of per-tile statistics
+static __device__ __align__(256) float g_noalloc_part[NOALLOC_PART_FLOATS];
+
+// Device address of g_noalloc_part on the current device.  In host code the
+// array's name is only a host-side stand-in, so its device address is asked
+// for once per device (with that device current) and cached.
+cudaError_t noalloc_part_buffer(float** out) {
+    static std::mutex mu;
+    static float* addr[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_part);
+        if (e != cudaSuccess) return e;
+        addr[dev] = (float*)p;
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
+size_t noalloc_part_capacity() { return NOALLOC_PART_FLOATS; }
 
 }  // namespace sp
