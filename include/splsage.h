@@ -236,6 +236,46 @@ int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const sp
                               spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v, const spl_sage_options* opts,
                               void* q8, float* q_scale, void* k8, float* k_scale, void* v8, float* stats);
 
+/* ---- Context parallelism (ring attention over GPUs) ----
+ * No counterpart in the reference, which runs one sequence on one GPU.
+ * Each rank holds part of a long sequence (e.g. the zig-zag chunks r and
+ * 2P-1-r of 2P) in its own workspace; the host exchanges quantised K/V
+ * between ranks (NCCL send/recv) and combines statistics (all-reduce):
+ *   1. spl_sage_cp_prepare: quantise this rank's Q; write its raw K/V channel
+ *      statistics raw f32 [b][g][4][D] = {sum K, sum V, -min V, max V}.
+ *   2. combine raw over all ranks: entries 0-1 summed, 2-3 maxed.
+ *   3. spl_sage_cp_quantize_kv: this rank's K/V quantised with the global
+ *      statistics (total_tokens = the whole sequence) into a K/V buffer.
+ *   4. for every (query chunk, key chunk) pair that is not wholly masked,
+ *      spl_sage_cp_attend against the K/V buffer holding those keys
+ *      (received from their owner), merged into acc / lse.
+ *   5. spl_sage_cp_finish: acc to bf16.
+ * The quantised K/V are not bit-identical to a single-GPU prepare (the
+ * channel sums are added in another order); results are tolerance-equal. */
+typedef struct spl_sage_kv spl_sage_kv; /* one rank's quantised K/V over caller memory */
+
+/* Bytes of the three K/V buffers of ws's plan: k8 i8 [b][g][tk_pad][D],
+ * k_scale f32 [b][g][tk_pad/64], v8 E4M3 [b][g][D][tk_pad]. */
+int spl_sage_kv_bytes(const spl_sage_ws* ws, int64_t* k8_bytes, int64_t* k_scale_bytes, int64_t* v8_bytes);
+/* TMA descriptors over caller-owned buffers (k8 and v8 128-byte aligned,
+ * k_scale 16-byte aligned) of ws's plan; dense keys only. */
+int spl_sage_kv_create(spl_sage* s, const spl_sage_ws* ws, void* k8, float* k_scale, void* v8, spl_sage_kv** out);
+void spl_sage_kv_destroy(spl_sage_kv* kv);
+int spl_sage_cp_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                        const spl_sage_options* opts, float* raw);
+int spl_sage_cp_quantize_kv(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor k, spl_sage_tensor v,
+                            const spl_sage_options* opts, const float* raw_global, int64_t total_tokens,
+                            spl_sage_kv* kv);
+/* Queries [q_begin, q_begin + q_len) of this rank (whole 128-row tiles)
+ * against keys [k_begin, k_begin + k_len) of kv (k_begin a multiple of 128).
+ * causal: the two segments cover the same positions (key i is seen by query
+ * i and later); otherwise every key is seen.  Merged into acc f32
+ * [b][t][h][D] and lse f32 [b][h][t] (t = this rank's tokens), which start
+ * at 0 and -inf, by log-sum-exp. */
+int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
+                       int64_t k_begin, int64_t k_len, int causal, float* acc, float* lse);
+int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out);
+
 /* Tensor-core peak probe (the analog of the reference's sage_peak kernels,
  * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
  * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n

@@ -93,7 +93,8 @@ EXPORTS = [
     "spl_sage_attend", "spl_sage_forward", "spl_sage_ws_export_reference_layout", "spl_sage_status",
     "spl_sage_attn_resources", "spl_sage_flops", "spl_sage_last_error", "spl_sage_version", "spl_sage_tensor_peak",
     "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
-    "spl_sage_quantize_noalloc",
+    "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
+    "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
 ]
 
 _lib = None
@@ -131,6 +132,14 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
         L.spl_sage_quantize_noalloc.argtypes = ([P, I, I, ctypes.POINTER(_Shape), _Tensor, _Tensor, _Tensor,
                                                  ctypes.POINTER(_Options)] + [P] * 6)
+        I64P = ctypes.POINTER(ctypes.c_int64)
+        L.spl_sage_kv_bytes.argtypes = [P, I64P, I64P, I64P]
+        L.spl_sage_kv_create.argtypes = [P, P, P, P, P, ctypes.POINTER(P)]
+        L.spl_sage_kv_destroy.argtypes = [P]
+        L.spl_sage_cp_prepare.argtypes = [P, P, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
+        L.spl_sage_cp_quantize_kv.argtypes = [P, P, _Tensor, _Tensor, ctypes.POINTER(_Options), P, ctypes.c_int64, P]
+        L.spl_sage_cp_attend.argtypes = [P, P, P] + [ctypes.c_int64] * 4 + [I, P, P]
+        L.spl_sage_cp_finish.argtypes = [P, P, P, _Tensor]
         L.spl_sage_flops.restype = ctypes.c_double
         L.spl_sage_flops.argtypes = [P]
         L.spl_sage_last_error.restype = ctypes.c_char_p
@@ -440,11 +449,72 @@ class SageAttention:
         _check(lib().spl_sage_ws_export_reference_layout(self._h, ws._h, ptr(q8), ptr(q_scale), ptr(k8),
                                                          ptr(k_scale), ptr(v8), ptr(stats), ptr(kbias)))
 
+    # ------------------------------------------------------------ context parallelism
+    # (no counterpart in the reference; see ring.py for the schedule)
+
+    def cp_prepare(self, ws: Workspace, q: Tensor, k: Tensor, v: Tensor, raw, opts: Options | None = None):
+        """Quantise this rank's Q into ws; raw (f32 CUDA, b*g*4*D) receives
+        its K/V channel statistics {sum K, sum V, -min V, max V}."""
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_cp_prepare(self._h, ws._h, q._c(), k._c(), v._c(), ctypes.byref(o),
+                                         ctypes.c_void_p(raw.data_ptr())))
+
+    def cp_quantize_kv(self, ws: Workspace, k: Tensor, v: Tensor, raw_global, total_tokens: int, kv: "KvBuffer",
+                       opts: Options | None = None):
+        """This rank's K/V quantised with the statistics combined over all
+        ranks (raw entries 0-1 summed, 2-3 maxed) into kv."""
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_cp_quantize_kv(self._h, ws._h, k._c(), v._c(), ctypes.byref(o),
+                                             ctypes.c_void_p(raw_global.data_ptr()), total_tokens, kv._h))
+
+    def cp_attend(self, ws: Workspace, kv: "KvBuffer", q_begin: int, q_len: int, k_begin: int, k_len: int,
+                  causal: bool, acc, lse):
+        """Segment attention merged into acc (f32 [b][t][h][D]) and lse (f32
+        [b][h][t]) by log-sum-exp."""
+        _check(lib().spl_sage_cp_attend(self._h, ws._h, kv._h, q_begin, q_len, k_begin, k_len, int(causal),
+                                        ctypes.c_void_p(acc.data_ptr()), ctypes.c_void_p(lse.data_ptr())))
+
+    def cp_finish(self, ws: Workspace, acc, out: Tensor):
+        _check(lib().spl_sage_cp_finish(self._h, ws._h, ctypes.c_void_p(acc.data_ptr()), out._c()))
+
     def status(self, ws: Workspace) -> int:
         """Reads (and clears) the device error word; raises on a kernel error."""
         w = ctypes.c_uint32()
         _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
         return w.value
+
+
+class KvBuffer:
+    """One rank's quantised K/V (k8, k_scale, v8 as torch CUDA tensors that
+    NCCL can send and receive) with the TMA descriptors the attention kernel
+    reads them through (spl_sage_kv_create)."""
+
+    def __init__(self, eng: "SageAttention", ws: Workspace):
+        import torch
+        n = [ctypes.c_int64() for _ in range(3)]
+        _check(lib().spl_sage_kv_bytes(ws._h, *[ctypes.byref(x) for x in n]))
+        self.k8 = torch.empty(n[0].value, dtype=torch.uint8, device="cuda")
+        self.k_scale = torch.empty(n[1].value // 4, dtype=torch.float32, device="cuda")
+        self.v8 = torch.empty(n[2].value, dtype=torch.uint8, device="cuda")
+        h = ctypes.c_void_p()
+        _check(lib().spl_sage_kv_create(eng._h, ws._h, ctypes.c_void_p(self.k8.data_ptr()),
+                                        ctypes.c_void_p(self.k_scale.data_ptr()), ctypes.c_void_p(self.v8.data_ptr()),
+                                        ctypes.byref(h)))
+        self._h = h
+
+    def tensors(self):
+        return [self.k8, self.k_scale, self.v8]
+
+    def close(self):
+        if self._h:
+            lib().spl_sage_kv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def quantize_noalloc(head_dim: int, shape: Shape, q: Tensor, k: Tensor, v: Tensor, q8, q_scale, k8, k_scale, v8,

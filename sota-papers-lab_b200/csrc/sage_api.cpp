@@ -16,7 +16,7 @@
 
 namespace {
 
-constexpr int QGROUP = 16, QTILE = 128, KBLOCK = 64;
+constexpr int QGROUP = 16, QTILE = 128, KBLOCK = 64, BLK = 128;
 constexpr float FP8_MAX = 448.0f;       // mod.rs:77
 constexpr float PV16_V_RANGE = 2.25f;   // mod.rs:185
 constexpr int LN_Q = 1, LN_K = 2, SMOOTH_K = 4, SMOOTH_V = 8;
@@ -327,8 +327,12 @@ static int check_tensor(const char* what, const void* data, int64_t len, int64_t
     return SPL_SAGE_OK;
 }
 
-int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
-                     const spl_sage_options* opts) {
+}  // extern "C"
+
+// The geometry of a quantiser call on ws (mod.rs:673-768): checks the
+// tensors and options, then fills g; *ln receives the QK-norm parameters.
+static int build_geom(spl_sage* s, const spl_sage_ws* ws, const spl_sage_tensor& q, const spl_sage_tensor& k,
+                      const spl_sage_tensor& v, const spl_sage_options* opts, sp::Geom* out, const float** ln) {
     if (!s || !ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_prepare: NULL engine or workspace");
     if (ws->head_dim != s->head_dim)
         return fail(SPL_SAGE_ERR_INVALID, "workspace was made for head dim %d, kernels are %d", ws->head_dim,
@@ -355,7 +359,7 @@ int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_t
     const float scale = o.has_softmax_scale ? o.softmax_scale : 1.0f / sqrtf((float)D);
     const float log2e = 1.44269504088896340736f;
 
-    sp::Geom g;
+    sp::Geom& g = *out;
     memset(&g, 0, sizeof g);
     g.q_sb = q.batch; g.q_st = q.token; g.q_sh = q.head;
     g.k_sb = k.batch; g.k_st = k.token; g.k_sh = k.head;
@@ -388,8 +392,19 @@ int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_t
     g.q_mul = scale * log2e;
     g.ln_eps = o.qk_norm_params ? o.qk_norm_eps : 1e-5f;
     g.v_range = s->config.pv_accum == SPL_SAGE_PV_F16 ? PV16_V_RANGE : FP8_MAX;
+    *ln = o.qk_norm_params;
+    return SPL_SAGE_OK;
+}
 
-    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, o.qk_norm_params, ws->buf, g, s->stream);
+extern "C" {
+
+int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                     const spl_sage_options* opts) {
+    sp::Geom g;
+    const float* ln = nullptr;
+    int rc = build_geom(s, ws, q, k, v, opts, &g, &ln);
+    if (rc) return rc;
+    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = g;
     ws->prepared = true;
@@ -691,6 +706,162 @@ double spl_sage_flops(const spl_sage_ws* ws) {
     if (!ws) return 0.0;
     return 4.0 * (double)(ws->shape.batch * ws->shape.heads) * (double)ws->shape.tokens * (double)ws->tk *
            (double)ws->head_dim;
+}
+
+// ---------------------------------------------------------------- context parallelism
+
+int spl_sage_kv_bytes(const spl_sage_ws* ws, int64_t* k8_bytes, int64_t* k_scale_bytes, int64_t* v8_bytes) {
+    if (!ws) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_kv_bytes: NULL workspace");
+    const int64_t B = ws->shape.batch, G = ws->shape.kv_heads, D = ws->head_dim;
+    if (k8_bytes) *k8_bytes = B * G * ws->tk_pad * D;
+    if (k_scale_bytes) *k_scale_bytes = B * G * (ws->tk_pad / KBLOCK) * 4;
+    if (v8_bytes) *v8_bytes = B * G * ws->tk_pad * D;
+    return SPL_SAGE_OK;
+}
+
+}  // extern "C"
+
+struct spl_sage_kv {
+    int head_dim;
+    int64_t batch, kv_heads, tk_pad;
+    int8_t* k8;
+    float* k_scale;
+    uint8_t* v8;
+    CUtensorMap map_k, map_v;
+};
+
+extern "C" {
+
+int spl_sage_kv_create(spl_sage* s, const spl_sage_ws* ws, void* k8, float* k_scale, void* v8, spl_sage_kv** out) {
+    if (!s || !ws || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_kv_create: NULL argument");
+    if (!k8 || !k_scale || !v8) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_kv_create: NULL buffer");
+    if ((uintptr_t)k8 % 128 || (uintptr_t)v8 % 128 || (uintptr_t)k_scale % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "K/V buffers must be 128-byte aligned, k_scale 16-byte aligned");
+    if (ws->head_dim != s->head_dim)
+        return fail(SPL_SAGE_ERR_INVALID, "workspace was made for head dim %d, kernels are %d", ws->head_dim,
+                    s->head_dim);
+    if (ws->merge.stride > 1) return fail(SPL_SAGE_ERR_INVALID, "context parallelism takes dense keys only");
+    const int64_t D = ws->head_dim, B = ws->shape.batch, G = ws->shape.kv_heads, T = ws->tk_pad;
+    spl_sage_kv* kv = new spl_sage_kv;
+    memset(kv, 0, sizeof *kv);
+    kv->head_dim = (int)D;
+    kv->batch = B;
+    kv->kv_heads = G;
+    kv->tk_pad = T;
+    kv->k8 = (int8_t*)k8;
+    kv->k_scale = k_scale;
+    kv->v8 = (uint8_t*)v8;
+    const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    int rc = make_map(&kv->map_k, k8, D, T, B * G, D, T * D, (uint32_t)D, 128, swz);
+    if (rc == SPL_SAGE_OK)
+        rc = make_map(&kv->map_v, v8, T, D, B * G, T, T * D, 128, (uint32_t)D, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SPL_SAGE_OK) {
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return SPL_SAGE_OK;
+}
+
+void spl_sage_kv_destroy(spl_sage_kv* kv) { delete kv; }
+
+int spl_sage_cp_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                        const spl_sage_options* opts, float* raw) {
+    if (!raw) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_prepare: NULL raw statistics buffer");
+    sp::Geom g;
+    const float* ln = nullptr;
+    int rc = build_geom(s, ws, q, k, v, opts, &g, &ln);
+    if (rc) return rc;
+    if (ws->merge.stride > 1) return fail(SPL_SAGE_ERR_INVALID, "context parallelism takes dense keys only");
+    cudaError_t e = sp::launch_cp_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, g, raw, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage context-parallel prepare");
+    ws->geom = g;
+    ws->prepared = false;  // K/V not quantised yet
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_cp_quantize_kv(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor k, spl_sage_tensor v,
+                            const spl_sage_options* opts, const float* raw_global, int64_t total_tokens,
+                            spl_sage_kv* kv) {
+    if (!raw_global || !kv) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_quantize_kv: NULL argument");
+    if (total_tokens < ws->shape.tokens)
+        return fail(SPL_SAGE_ERR_INVALID, "total tokens %lld is less than this rank's %lld", (long long)total_tokens,
+                    (long long)ws->shape.tokens);
+    if (kv->head_dim != ws->head_dim || kv->tk_pad != ws->tk_pad || kv->batch != ws->shape.batch ||
+        kv->kv_heads != ws->shape.kv_heads)
+        return fail(SPL_SAGE_ERR_INVALID, "the K/V buffer was made for another workspace plan");
+    sp::Geom g;
+    const float* ln = nullptr;
+    // the query operand only has to pass the checks: K stands in for it
+    spl_sage_tensor qdummy = k;
+    spl_sage_ws tmp = *ws;
+    tmp.shape.heads = ws->shape.kv_heads;
+    int rc = build_geom(s, &tmp, qdummy, k, v, opts, &g, &ln);
+    if (rc) return rc;
+    g.heads = (int)ws->shape.heads;
+    sp::Buffers buf = ws->buf;
+    buf.k8 = kv->k8;
+    buf.k_scale = kv->k_scale;
+    buf.v8 = kv->v8;
+    buf.kbias = nullptr;
+    cudaError_t e = sp::launch_cp_quant_kv(s->head_dim, k.data, v.data, ln, buf, g, raw_global,
+                                           (float)total_tokens, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage context-parallel K/V quantiser");
+    ws->prepared = true;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
+                       int64_t k_begin, int64_t k_len, int causal, float* acc, float* lse) {
+    if (!s || !ws || !kv || !acc || !lse) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend: NULL argument");
+    if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
+    if (kv->head_dim != ws->head_dim || kv->tk_pad != ws->tk_pad || kv->batch != ws->shape.batch ||
+        kv->kv_heads != ws->shape.kv_heads)
+        return fail(SPL_SAGE_ERR_INVALID, "the K/V buffer was made for another workspace plan");
+    if (q_begin < 0 || q_len <= 0 || q_begin % QTILE || q_len % QTILE || q_begin + q_len > ws->tq_pad)
+        return fail(SPL_SAGE_ERR_INVALID, "query segment [%lld, +%lld) must be whole 128-row tiles within %lld rows",
+                    (long long)q_begin, (long long)q_len, (long long)ws->tq_pad);
+    if (k_begin < 0 || k_len <= 0 || k_begin % BLK || k_begin + k_len > ws->tk)
+        return fail(SPL_SAGE_ERR_INVALID, "key segment [%lld, +%lld) must start on a 128-key block within %lld keys",
+                    (long long)k_begin, (long long)k_len, (long long)ws->tk);
+    if (causal && k_len < q_len)
+        return fail(SPL_SAGE_ERR_INVALID, "a causal segment needs at least as many keys as queries");
+    if (q_len / QTILE > 65535) return fail(SPL_SAGE_ERR_INVALID, "too many query tiles");
+    sp::Geom g = ws->geom;
+    const int64_t H = ws->shape.heads, D = ws->head_dim, T = ws->shape.tokens;
+    g.o_sb = T * H * D;
+    g.o_st = H * D;
+    g.o_sh = D;
+    g.q_tile0 = (int)(q_begin / QTILE);
+    g.q_tiles = (int)(q_len / QTILE);
+    g.k_key0 = (int)k_begin;
+    g.tk = (int)k_len;
+    g.tk_pad = (int)kv->tk_pad;
+    g.causal = causal ? 1 : 0;
+    g.merge = 1;
+    sp::AttnMaps maps;
+    maps.q = ws->maps.q;
+    maps.k = kv->map_k;
+    maps.v = kv->map_v;
+    sp::Buffers buf = ws->buf;
+    buf.k_scale = kv->k_scale;
+    cudaError_t e = sp::launch_attend_partial(s->head_dim, maps, buf, g, acc, lse, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage segment attention");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out) {
+    if (!s || !ws || !acc) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_finish: NULL argument");
+    int rc = check_tensor("output", out.data, out.len, out.batch, out.token, out.head, ws->shape, ws->shape.heads,
+                          s->head_dim);
+    if (rc) return rc;
+    sp::Geom g = ws->geom;
+    g.o_sb = out.batch;
+    g.o_st = out.token;
+    g.o_sh = out.head;
+    cudaError_t e = sp::launch_cp_finish(s->head_dim, acc, g, out.data, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage context-parallel finish");
+    return SPL_SAGE_OK;
 }
 
 }  // extern "C"

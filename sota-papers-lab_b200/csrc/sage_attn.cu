@@ -107,12 +107,18 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_
     return warp_all_wait(bar, parity, err, site);
 }
 
-template <int D, bool CAUSAL, bool MERGE>
+// PARTIAL (context parallelism): the CTA's query tiles are tiles
+// q_tile0 + blockIdx.y of the workspace, its keys keys k_key0 .. k_key0 + tk
+// of the K/V buffer (CAUSAL then means key i is seen by query i and later of
+// the segment); the result is merged into the fp32 accumulator acc and the
+// per-row log2 softmax denominator lse by log-sum-exp instead of written.
+template <int D, bool CAUSAL, bool MERGE, bool PARTIAL>
 __global__ void __launch_bounds__(NTHREADS, 1)
     sp_attn(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
             const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q_scale,
             const float* __restrict__ k_scale, const float* __restrict__ stats, const float* __restrict__ kbias,
-            uint16_t* __restrict__ out, uint32_t* __restrict__ err, const Geom g) {
+            uint16_t* __restrict__ out, float* __restrict__ acc, float* __restrict__ lse, uint32_t* __restrict__ err,
+            const Geom g) {
     using L = AttnSmem<D>;
     constexpr int DH = D / 2;
     constexpr uint32_t SWZ = D == 128 ? SWZ_128B : SWZ_64B;
@@ -128,12 +134,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh_q = blockIdx.x;
-    const int n_qt = g.tq_pad / 128;
-    const int qt = CAUSAL ? n_qt - 1 - (int)blockIdx.y : (int)blockIdx.y;
+    const int n_qt = (int)gridDim.y;
+    const int qt = CAUSAL ? n_qt - 1 - (int)blockIdx.y : (int)blockIdx.y;  // tile within the segment
     const int b = bh_q / g.heads, h = bh_q % g.heads;
     const int group = g.heads / g.kv_heads;
     const int bh_kv = b * g.kv_heads + h / group;
-    const int nkb64 = g.tk_pad / KBLOCK;
+    const int nkb64 = g.tk_pad / KBLOCK;  // k_scale row length of the K/V buffer
+    // segment offsets (context parallelism only; compile-time zero otherwise)
+    const int q_tile0 = PARTIAL ? g.q_tile0 : 0, k_key0 = PARTIAL ? g.k_key0 : 0;
+    const int nkb64_seg = PARTIAL ? (g.tk + KBLOCK - 1) / KBLOCK : nkb64;  // 64-key blocks attended
     const int nkb = (g.tk + BLK - 1) / BLK;
     const int nb = CAUSAL ? min(nkb, qt + 1) : nkb;
 
@@ -178,14 +187,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
             mbar_expect_tx(bar(bars.q_full), L::Q_BYTES);
-            tma_load_3d(sQ, &map_q, bar(bars.q_full), 0, qt * 128, bh_q);
+            tma_load_3d(sQ, &map_q, bar(bars.q_full), 0, (q_tile0 + qt) * 128, bh_q);
             int nk = 0;
             for (int j = 0; j < nb; j++) {
                 const int ks = j % KST;
                 if (j >= KST && !mbar_wait(bar(bars.k_empty[ks]), ((j / KST) - 1) & 1, err, 1)) break;
                 SP_TR(true, 0, j, 0);
                 mbar_expect_tx(bar(bars.k_full[ks]), L::K_BYTES);
-                tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, j * BLK, bh_kv);
+                tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, k_key0 + j * BLK, bh_kv);
                 nk++;
             }
             // Drain: every load issued lands before the CTA exits (these
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (j >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((j / VST) - 1) & 1, err, 2)) break;
                 SP_TR(true, 0, j, 1);
                 mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
-                tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), j * BLK, 0, bh_kv);
+                tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), k_key0 + j * BLK, 0, bh_kv);
                 nv++;
             }
             for (int s = 0; s < VST && s < nv; s++) {
@@ -276,9 +285,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int half = lane >> 4;                             // 0: keys 0-63, 1: keys 64-127
         const int r = quarter * 32 + sub * 16 + (lane & 15);    // query row in the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)(quarter * 32 + sub * 16) << 16;
-        const int qrow = qt * 128 + r;
-        const float qs = q_scale[(long long)bh_q * (g.tq_pad / QGROUP) + qrow / QGROUP];
-        const float* ksc = k_scale + (long long)bh_kv * nkb64;
+        const int qrow = qt * 128 + r;                          // within the segment (masking)
+        const int qrow_ws = PARTIAL ? (q_tile0 + qt) * 128 + r : qrow;  // within the workspace
+        const float qs = q_scale[(long long)bh_q * (g.tq_pad / QGROUP) + qrow_ws / QGROUP];
+        const float* ksc = k_scale + (long long)bh_kv * nkb64 + k_key0 / KBLOCK;
         const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
         float o[DH];
 #pragma unroll
@@ -286,7 +296,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float m = -1.0e30f, l = 0.f, alpha_prev = 0.f;
         auto kscale = [&](int jb) {
             const int i = 2 * jb + half;
-            return __ldg(ksc + (i < nkb64 ? i : 2 * jb));
+            return __ldg(ksc + (i < nkb64_seg ? i : 2 * jb));
         };
         float ks = kscale(0);
         bool ok = true;
@@ -421,14 +431,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             alpha_prev = alpha;
         }
         if (ok) ok = correct(nb - 1, alpha_prev);
-        if (ok) {
+        if (ok && !PARTIAL) {
             // out = O / l * v_scale + v_mean for this lane's D/2 columns
             const float inv = 1.0f / (l + __shfl_xor_sync(0xffffffffu, l, 16));
             const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
             const float* vscale = vmean + D;
             uint16_t* orow =
-                out + (long long)b * g.o_sb + (long long)qrow * g.o_st + (long long)h * g.o_sh + half * DH;
-            if (qrow < g.tokens) {
+                out + (long long)b * g.o_sb + (long long)qrow_ws * g.o_st + (long long)h * g.o_sh + half * DH;
+            if (qrow_ws < g.tokens) {
 #pragma unroll
                 for (int c = 0; c < DH; c += 8) {
                     uint32_t w[4];
@@ -443,6 +453,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
+        if (ok && PARTIAL) {
+            // this segment's y = O / l * v_scale + v_mean and its log2
+            // denominator, merged into (acc, lse): acc = (acc w_old + y w_new)
+            // / (w_old + w_new) with w = 2^(lse - max), lse = log2 of the sum
+            const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
+            const float inv = 1.0f / lt;
+            const float lse_new = m + log2f(lt) - LOG2_448;
+            float* lrow = lse + ((long long)b * g.heads + h) * g.tokens + qrow_ws;
+            const float lse_old = *lrow;
+            const float mx = fmaxf(lse_old, lse_new);
+            const float w_old = lse_old == __int_as_float(0xff800000) ? 0.f : exp2f(lse_old - mx);
+            const float w_new = exp2f(lse_new - mx);
+            const float s_inv = 1.0f / (w_old + w_new);
+            const float a_old = w_old * s_inv, a_new = w_new * inv * s_inv;
+            const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
+            const float* vscale = vmean + D;
+            float* arow = acc + (long long)b * g.o_sb + (long long)qrow_ws * g.o_st + (long long)h * g.o_sh + half * DH;
+            if (qrow_ws < g.tokens) {
+#pragma unroll
+                for (int c = 0; c < DH; c += 4) {
+                    float4 x = w_old > 0.f ? *reinterpret_cast<const float4*>(arow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x.x = fmaf(x.x, a_old, fmaf(o[c] * a_new, __ldg(vscale + c), __ldg(vmean + c) * w_new * s_inv));
+                    x.y = fmaf(x.y, a_old, fmaf(o[c + 1] * a_new, __ldg(vscale + c + 1), __ldg(vmean + c + 1) * w_new * s_inv));
+                    x.z = fmaf(x.z, a_old, fmaf(o[c + 2] * a_new, __ldg(vscale + c + 2), __ldg(vmean + c + 2) * w_new * s_inv));
+                    x.w = fmaf(x.w, a_old, fmaf(o[c + 3] * a_new, __ldg(vscale + c + 3), __ldg(vmean + c + 3) * w_new * s_inv));
+                    *reinterpret_cast<float4*>(arow + c) = x;
+                }
+            }
+            __syncwarp();
+            if (half == 0 && qrow_ws < g.tokens) *lrow = mx + log2f(w_old + w_new);
+        }
     }
 
     tc_fence_before();
@@ -451,10 +492,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp == QK_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-template <int D, bool CAUSAL, bool MERGE>
-static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out, cudaStream_t st) {
+template <int D, bool CAUSAL, bool MERGE, bool PARTIAL>
+static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out, float* acc, float* lse,
+                            int q_tiles, cudaStream_t st) {
     static unsigned attr_set = 0;  // one bit per device ordinal
-    auto kern = sp_attn<D, CAUSAL, MERGE>;
+    auto kern = sp_attn<D, CAUSAL, MERGE, PARTIAL>;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 32 || !(attr_set & (1u << dev))) {
@@ -462,37 +504,43 @@ static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom
         if (e != cudaSuccess) return e;
         if (dev < 32) attr_set |= 1u << dev;
     }
-    dim3 grid(g.batch * g.heads, g.tq_pad / 128);
+    dim3 grid(g.batch * g.heads, q_tiles);
     kern<<<grid, NTHREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,
-                                                   buf.kbias, (uint16_t*)out, buf.err, g);
+                                                   buf.kbias, (uint16_t*)out, acc, lse, buf.err, g);
     return cudaGetLastError();
 }
 
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
                           cudaStream_t st) {
     const bool merge = g.merge > 1, causal = g.causal != 0;
+    const int qt = g.tq_pad / 128;
     if (d == 64) {
-        if (merge) return attend_t<64, false, true>(maps, buf, g, out, st);
-        return causal ? attend_t<64, true, false>(maps, buf, g, out, st)
-                      : attend_t<64, false, false>(maps, buf, g, out, st);
+        if (merge) return attend_t<64, false, true, false>(maps, buf, g, out, nullptr, nullptr, qt, st);
+        return causal ? attend_t<64, true, false, false>(maps, buf, g, out, nullptr, nullptr, qt, st)
+                      : attend_t<64, false, false, false>(maps, buf, g, out, nullptr, nullptr, qt, st);
     }
-    if (merge) return attend_t<128, false, true>(maps, buf, g, out, st);
-    return causal ? attend_t<128, true, false>(maps, buf, g, out, st)
-                  : attend_t<128, false, false>(maps, buf, g, out, st);
+    if (merge) return attend_t<128, false, true, false>(maps, buf, g, out, nullptr, nullptr, qt, st);
+    return causal ? attend_t<128, true, false, false>(maps, buf, g, out, nullptr, nullptr, qt, st)
+                  : attend_t<128, false, false, false>(maps, buf, g, out, nullptr, nullptr, qt, st);
 }
 
-#ifdef SP_TRACE
-extern "C" int spl_sage_debug_trace(unsigned long long* host, int n) {
-    return (int)cudaMemcpyFromSymbol(host, sp_trace_buf, sizeof(unsigned long long) * (n < 4096 ? n : 4096));
+cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, float* acc,
+                                  float* lse, cudaStream_t st) {
+    const bool causal = g.causal != 0;
+    const int qt = g.q_tiles;  // the segment's query tiles
+    if (d == 64)
+        return causal ? attend_t<64, true, false, true>(maps, buf, g, nullptr, acc, lse, qt, st)
+                      : attend_t<64, false, false, true>(maps, buf, g, nullptr, acc, lse, qt, st);
+    return causal ? attend_t<128, true, false, true>(maps, buf, g, nullptr, acc, lse, qt, st)
+                  : attend_t<128, false, false, true>(maps, buf, g, nullptr, acc, lse, qt, st);
 }
-#endif
 
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes) {
     cudaFuncAttributes a;
-    cudaError_t e = d == 64 ? (merge ? cudaFuncGetAttributes(&a, sp_attn<64, false, true>)
-                                     : cudaFuncGetAttributes(&a, sp_attn<64, false, false>))
-                            : (merge ? cudaFuncGetAttributes(&a, sp_attn<128, false, true>)
-                                     : cudaFuncGetAttributes(&a, sp_attn<128, false, false>));
+    cudaError_t e = d == 64 ? (merge ? cudaFuncGetAttributes(&a, sp_attn<64, false, true, false>)
+                                     : cudaFuncGetAttributes(&a, sp_attn<64, false, false, false>))
+                            : (merge ? cudaFuncGetAttributes(&a, sp_attn<128, false, true, false>)
+                                     : cudaFuncGetAttributes(&a, sp_attn<128, false, false, false>));
     if (e != cudaSuccess) return e;
     *regs = a.numRegs;
     *local_bytes = (int)a.localSizeBytes;

@@ -22,6 +22,10 @@ struct Geom {
     int grid_h, grid_w, merged_frame, merged_w;
     int dense_frames, flags, causal, pad0;
     float q_mul, ln_eps, v_range, pad1;
+    // Segment attention (context parallelism): the query tiles start at
+    // tile q_tile0 of the workspace's Q, the keys at key k_key0 of the K/V
+    // buffer; tk is then the segment's key count.  Both 0 otherwise.
+    int q_tile0, k_key0;
 };
 
 // Device buffers of one workspace.  Layouts (b = batch, h = q head,
@@ -79,6 +83,22 @@ size_t noalloc_part_capacity();
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                            const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);
+// Context parallelism (sage_quant.cu): Q quantised and this rank's raw K/V
+// channel statistics raw [b][g][4][D] = {sum K, sum V, -min V, max V};
+// then, from the raw statistics combined over all ranks (sums added, the
+// other two maxed), the workspace stats for `total` tokens and this rank's
+// K/V quantised into buf.k8 / k_scale / v8; and the fp32 accumulator of
+// segment attention converted to bf16.
+cudaError_t launch_cp_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                              const Geom& g, float* raw, cudaStream_t st);
+cudaError_t launch_cp_quant_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
+                               const Geom& g, const float* raw, float total, cudaStream_t st);
+cudaError_t launch_cp_finish(int d, const float* acc, const Geom& g, void* out, cudaStream_t st);
+// Segment attention merged into acc f32 (strides g.o_*) and lse f32
+// [b][h][tokens] (log2 of the row's softmax denominator) by log-sum-exp.
+cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, float* acc,
+                                  float* lse, cudaStream_t st);
+
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
                           cudaStream_t st);
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes);

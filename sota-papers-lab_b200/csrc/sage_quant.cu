@@ -393,6 +393,111 @@ cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, c
     return d == 64 ? prepare_d<64>(q, k, v, ln, buf, g, st) : prepare_d<128>(q, k, v, ln, buf, g, st);
 }
 
+// ---------------------------------------------------------------- context parallelism
+// (No counterpart in the reference, which runs on one GPU.)  Each rank holds
+// part of the sequence; the K/V smoothing statistics must be those of the
+// whole sequence, so every rank reduces its tiles' partials to raw sums,
+// the ranks combine them, and each finalises the same stats from the result.
+
+// raw[b][g][4][D] = {sum K, sum V, -min V, max V} over this rank's tiles.
+template <int D>
+__global__ void __launch_bounds__(256) sp_cp_partial(const float* __restrict__ part, float* __restrict__ raw,
+                                                     const Geom g) {
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const long long bh = (long long)b * g.kv_heads + h;
+    for (int c = tid; c < 4 * D; c += 256) {
+        const int stat = c / D, d = c % D;
+        const float* p = part + bh * g.q_tiles * 4 * D + stat * D + d;
+        float r = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
+        for (int t = 0; t < g.q_tiles; t++) {
+            const float x = p[(long long)t * 4 * D];
+            r = stat < 2 ? r + x : (stat == 2 ? fminf(r, x) : fmaxf(r, x));
+        }
+        raw[(bh * 4 + stat) * D + d] = stat == 2 ? -r : r;
+    }
+}
+
+// The workspace stats from the combined raw statistics of `total` tokens
+// (the formulas of sp_finalize).
+template <int D>
+__global__ void __launch_bounds__(256) sp_cp_finalize(const float* __restrict__ raw, float* __restrict__ stats,
+                                                      const Geom g, float total) {
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const long long bh = (long long)b * g.kv_heads + h;
+    const float* r = raw + bh * 4 * D;
+    for (int d = tid; d < D; d += 256) {
+        const float mk = (g.flags & SMOOTH_K) ? r[d] / total : 0.f;
+        const float mv = (g.flags & SMOOTH_V) ? r[D + d] / total : 0.f;
+        const float amax = fmaxf(r[3 * D + d] - mv, mv + r[2 * D + d]);
+        const float scale = amax > 0.f ? amax / g.v_range : 1.0f;
+        float* o = stats + bh * 4 * D;
+        o[d] = mk;
+        o[D + d] = mv;
+        o[2 * D + d] = scale;
+        o[3 * D + d] = 1.0f / scale;
+    }
+}
+
+// bf16 out [b][t][h][D] (strides g.o_*) from the fp32 accumulator (dense
+// [b][t][h][D]).
+template <int D>
+__global__ void __launch_bounds__(256) sp_cp_finish(const float* __restrict__ acc, uint16_t* __restrict__ out,
+                                                    const Geom g) {
+    const long long n8 = (long long)g.batch * g.tokens * g.heads * (D / 8);
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
+        const int c8 = (int)(i % (D / 8));
+        const long long row = i / (D / 8);  // (b * tokens + t) * heads + h
+        const int h = (int)(row % g.heads);
+        const long long bt = row / g.heads;
+        const int t = (int)(bt % g.tokens), b = (int)(bt / g.tokens);
+        const float4 x0 = *reinterpret_cast<const float4*>(acc + i * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(acc + i * 8 + 4);
+        const uint4 w = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                                   pack_bf16x2(x1.z, x1.w));
+        *reinterpret_cast<uint4*>(out + b * g.o_sb + (long long)t * g.o_st + (long long)h * g.o_sh + c8 * 8) = w;
+    }
+}
+
+template <int D>
+static cudaError_t cp_prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                                const Geom& g, float* raw, cudaStream_t st) {
+    sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g);
+    sp_cp_partial<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(buf.part, raw, g);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cp_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
+                              const Geom& g, float* raw, cudaStream_t st) {
+    return d == 64 ? cp_prepare_d<64>(q, k, v, ln, buf, g, raw, st) : cp_prepare_d<128>(q, k, v, ln, buf, g, raw, st);
+}
+
+template <int D>
+static cudaError_t cp_quant_kv_d(const void* k, const void* v, const float* ln, const Buffers& buf, const Geom& g,
+                                 const float* raw, float total, cudaStream_t st) {
+    sp_cp_finalize<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(raw, buf.stats, g, total);
+    sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
+        (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cp_quant_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
+                               const Geom& g, const float* raw, float total, cudaStream_t st) {
+    return d == 64 ? cp_quant_kv_d<64>(k, v, ln, buf, g, raw, total, st)
+                   : cp_quant_kv_d<128>(k, v, ln, buf, g, raw, total, st);
+}
+
+cudaError_t launch_cp_finish(int d, const float* acc, const Geom& g, void* out, cudaStream_t st) {
+    const long long n8 = (long long)g.batch * g.tokens * g.heads * (d / 8);
+    const long long want = (n8 + 255) / 256;
+    const int blocks = (int)(want < 148ll * 16 ? want : 148ll * 16);
+    if (d == 64)
+        sp_cp_finish<64><<<blocks, 256, 0, st>>>(acc, (uint16_t*)out, g);
+    else
+        sp_cp_finish<128><<<blocks, 256, 0, st>>>(acc, (uint16_t*)out, g);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st) {
     const long long n = (long long)g.batch * g.kv_heads * d * g.tk_pad;
     const long long want = (n + 255) / 256;

@@ -1,0 +1,199 @@
+"""Context-parallel (ring) SageAttention over several GPUs, one process per
+GPU.  No counterpart in the reference, which runs a sequence on one GPU.
+
+The sequence of N tokens is cut into 2P chunks of C = N / (2P) tokens; rank r
+holds chunks r and 2P-1-r ("zig-zag", so that every rank has the same causal
+work).  Its Q, K and V are those 2C tokens, chunk r first.
+
+1. Every rank quantises its Q and reduces its K/V channel statistics; the
+   statistics are combined over all ranks (one all-reduce of sums, one of
+   maxima), so every rank smooths and scales K/V with the whole sequence's
+   mean and range; then each rank quantises its own K/V.
+2. P steps: at step s rank r holds the quantised K/V of rank (r - s) mod P,
+   attends its two query chunks to that rank's two key chunks (a pair of
+   chunks is skipped when the key chunk lies after the query chunk, causal
+   when they are the same chunk, full otherwise) and merges the result into
+   an fp32 accumulator by log-sum-exp.  Meanwhile the K/V it holds travels
+   to rank r + 1 and the next arrives from rank r - 1 (NCCL send/recv, on
+   NCCL's own stream, double-buffered): the transfer of ~2 * C * Hkv * D
+   bytes overlaps the attention of the step.
+3. The accumulator is converted to bf16.
+
+With P = 1 this is one GPU attending the whole sequence in two chunks.
+"""
+from __future__ import annotations
+
+import importlib
+from dataclasses import dataclass
+from typing import Callable, List, Sequence, Tuple
+
+
+def zigzag_chunks(rank: int, world: int) -> Tuple[int, int]:
+    """The two global chunk indices (of 2 * world) rank holds, in local order."""
+    return rank, 2 * world - 1 - rank
+
+
+@dataclass(frozen=True)
+class Pair:
+    q_local: int   # 0 or 1: which of this rank's chunks is the query
+    k_local: int   # 0 or 1: which of the source rank's chunks is the key
+    causal: bool   # same global chunk: causal mask within it
+
+
+def ring_schedule(rank: int, world: int) -> List[Tuple[int, List[Pair]]]:
+    """For each step: the rank whose K/V this rank holds, and the chunk
+    pairs to attend.  Across the steps every (query chunk, key chunk) pair
+    with the key chunk at or before the query chunk appears exactly once."""
+    steps = []
+    for s in range(world):
+        src = (rank - s) % world
+        pairs = []
+        for qi, cq in enumerate(zigzag_chunks(rank, world)):
+            for ki, ck in enumerate(zigzag_chunks(src, world)):
+                if ck > cq:
+                    continue
+                pairs.append(Pair(qi, ki, ck == cq))
+        steps.append((src, pairs))
+    return steps
+
+
+def shard_zigzag(x, rank: int, world: int, dim: int = 1):
+    """This rank's two chunks of a full-sequence tensor, concatenated."""
+    import torch
+    n = x.shape[dim]
+    c = n // (2 * world)
+    a, b = zigzag_chunks(rank, world)
+    return torch.cat([x.narrow(dim, a * c, c), x.narrow(dim, b * c, c)], dim=dim).contiguous()
+
+
+def unshard_zigzag(parts: Sequence, world: int, dim: int = 1):
+    """Inverse of shard_zigzag over all ranks' outputs."""
+    import torch
+    c = parts[0].shape[dim] // 2
+    chunks = [None] * (2 * world)
+    for r, p in enumerate(parts):
+        a, b = zigzag_chunks(r, world)
+        chunks[a] = p.narrow(dim, 0, c)
+        chunks[b] = p.narrow(dim, c, c)
+    return torch.cat(chunks, dim=dim)
+
+
+def nccl_exchange(group=None):
+    """send(bufs) to rank + 1 and recv(into) from rank - 1 with torch.distributed
+    P2P ops; returns a function (send_bufs, recv_bufs) -> a wait() callable."""
+    import torch.distributed as dist
+
+    def exchange(send_bufs, recv_bufs):
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        nxt, prv = (rank + 1) % world, (rank - 1) % world
+        if group is not None:
+            nxt = dist.get_global_rank(group, nxt)
+            prv = dist.get_global_rank(group, prv)
+        ops = []
+        for t in send_bufs:
+            ops.append(dist.P2POp(dist.isend, t, nxt, group))
+        for t in recv_bufs:
+            ops.append(dist.P2POp(dist.irecv, t, prv, group))
+        works = dist.batch_isend_irecv(ops)
+
+        def wait():
+            for w in works:
+                w.wait()
+        return wait
+    return exchange
+
+
+def combine_stats(raw, world: int, group=None):
+    """raw [b*g, 4, D] summed (entries 0-1) and maxed (2-3) over the ranks."""
+    if world == 1:
+        return raw
+    import torch.distributed as dist
+    sums = raw[:, :2].contiguous()
+    maxs = raw[:, 2:].contiguous()
+    dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(maxs, op=dist.ReduceOp.MAX, group=group)
+    raw[:, :2].copy_(sums)
+    raw[:, 2:].copy_(maxs)
+    return raw
+
+
+class RingAttention:
+    """Ring attention of one rank.  Holds the workspace (this rank's tokens),
+    two K/V buffers (the one being attended, the one being received) and the
+    fp32 accumulator; reuse it for every call of the same shape."""
+
+    def __init__(self, eng, batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int, world: int,
+                 head_dim: int):
+        import torch
+        sage = importlib.import_module("sota-papers-lab_b200")
+        if local_tokens % 256:
+            raise sage.SageError(1, "each rank's tokens must be two chunks of whole 128-token tiles")
+        self.sage, self.eng = sage, eng
+        self.rank, self.world = rank, world
+        self.B, self.H, self.G, self.T, self.D = batch, heads, kv_heads, local_tokens, head_dim
+        self.C = local_tokens // 2
+        self.ws = eng.workspace(sage.Shape(batch, heads, local_tokens, kv_heads, False))
+        self.kv = [sage.KvBuffer(eng, self.ws), sage.KvBuffer(eng, self.ws)]
+        self.raw = torch.empty(batch * kv_heads, 4, head_dim, dtype=torch.float32, device="cuda")
+        self.acc = torch.empty(batch, local_tokens, heads, head_dim, dtype=torch.float32, device="cuda")
+        self.lse = torch.empty(batch, heads, local_tokens, dtype=torch.float32, device="cuda")
+
+    def forward(self, q, k, v, out, *, exchange: Callable | None = None, group=None, opts=None,
+                combine: Callable | None = None):
+        """q, k, v, out: this rank's tokens (sage.Tensor views); exchange: the
+        K/V transfer (default NCCL P2P over `group`); combine: the statistics
+        reduction (default all-reduce over `group`)."""
+        sage = self.sage
+        P, r = self.world, self.rank
+        self.eng.cp_prepare(self.ws, q, k, v, self.raw, opts)
+        if combine is not None:
+            combine(self.raw)
+        else:
+            combine_stats(self.raw, P, group)
+        self.eng.cp_quantize_kv(self.ws, k, v, self.raw, self.T * P, self.kv[0], opts)
+        self.acc.zero_()
+        self.lse.fill_(float("-inf"))
+        if exchange is None and P > 1:
+            exchange = nccl_exchange(group)
+        cur = 0
+        for s, (src, pairs) in enumerate(ring_schedule(r, P)):
+            wait = None
+            if s + 1 < P:
+                wait = exchange(self.kv[cur].tensors(), self.kv[1 - cur].tensors())
+            for pr in pairs:
+                self.eng.cp_attend(self.ws, self.kv[cur], pr.q_local * self.C, self.C, pr.k_local * self.C, self.C,
+                                   pr.causal, self.acc, self.lse)
+            if wait is not None:
+                wait()
+                cur = 1 - cur
+        self.eng.cp_finish(self.ws, self.acc, out)
+
+    def close(self):
+        for kv in self.kv:
+            kv.close()
+        self.ws.close()
+
+
+def emulate_ring(rings: Sequence[RingAttention], qs, ks, vs, outs, opts=None):
+    """All ranks of a ring in one process on one GPU (for tests): the
+    statistics are combined and the K/V "exchanged" by copies, in the same
+    order as the multi-GPU run."""
+    import torch
+    P = len(rings)
+    for i, rg in enumerate(rings):
+        rg.eng.cp_prepare(rg.ws, qs[i], ks[i], vs[i], rg.raw, opts)
+    total = torch.stack([rg.raw for rg in rings])
+    comb = torch.cat([total[:, :, :2].sum(0), total[:, :, 2:].amax(0)], dim=1)
+    for i, rg in enumerate(rings):
+        rg.raw.copy_(comb)
+        rg.eng.cp_quantize_kv(rg.ws, ks[i], vs[i], rg.raw, rg.T * P, rg.kv[0], opts)
+        rg.acc.zero_()
+        rg.lse.fill_(float("-inf"))
+    for i, rg in enumerate(rings):
+        for s, (src, pairs) in enumerate(ring_schedule(i, P)):
+            kv = rings[src].kv[0]
+            for pr in pairs:
+                rg.eng.cp_attend(rg.ws, kv, pr.q_local * rg.C, rg.C, pr.k_local * rg.C, rg.C, pr.causal, rg.acc,
+                                 rg.lse)
+        rg.eng.cp_finish(rg.ws, rg.acc, outs[i])

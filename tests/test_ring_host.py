@@ -1,0 +1,108 @@
+"""Host logic of the context-parallel ring (sota-papers-lab_b200/ring.py), on
+CPU: the zig-zag schedule, the sharding helpers and, with world_size 2 on
+gloo, the K/V exchange and the statistics combination the GPU run uses."""
+from __future__ import annotations
+
+import importlib
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ring = importlib.import_module("sota-papers-lab_b200.ring")
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_schedule_covers_every_visible_chunk_pair_once(world):
+    for rank in range(world):
+        seen = []
+        for src, pairs in ring.ring_schedule(rank, world):
+            for p in pairs:
+                cq = ring.zigzag_chunks(rank, world)[p.q_local]
+                ck = ring.zigzag_chunks(src, world)[p.k_local]
+                assert ck <= cq
+                assert p.causal == (ck == cq)
+                seen.append((cq, ck))
+        want = [(cq, ck) for cq in ring.zigzag_chunks(rank, world) for ck in range(2 * world) if ck <= cq]
+        assert sorted(seen) == sorted(want)
+        # the first step attends the rank's own K/V
+        assert ring.ring_schedule(rank, world)[0][0] == rank
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_zigzag_balances_causal_work(world):
+    # key chunks seen per rank, a diagonal chunk counting one half
+    work = []
+    for rank in range(world):
+        w = 0.0
+        for _, pairs in ring.ring_schedule(rank, world):
+            w += sum(0.5 if p.causal else 1.0 for p in pairs)
+        work.append(w)
+    assert max(work) == min(work)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_shard_unshard_round_trip(world):
+    x = torch.arange(2 * 3 * 16 * world * 4, dtype=torch.float32).view(2, 16 * world, 3, 4)
+    parts = [ring.shard_zigzag(x, r, world, dim=1) for r in range(world)]
+    assert all(p.shape == (2, 16, 3, 4) for p in parts)
+    assert torch.equal(ring.unshard_zigzag(parts, world, dim=1), x)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        r = importlib.import_module("sota-papers-lab_b200.ring")
+        # the ring's exchange: after s steps each rank holds rank (r - s)'s buffers
+        ex = r.nccl_exchange()
+        cur = [torch.full((3,), float(rank)), torch.full((2,), 10.0 + rank)]
+        nxt = [torch.zeros(3), torch.zeros(2)]
+        held = []
+        for s, (src, _) in enumerate(r.ring_schedule(rank, world)):
+            held.append((src, int(cur[0][0].item()), int(cur[1][0].item()) - 10))
+            if s + 1 < world:
+                ex(cur, nxt)()
+                cur, nxt = nxt, cur
+        # statistics: sums added, -min / max maxed
+        raw = torch.tensor([[[1.0 + rank], [2.0 * rank], [-(5.0 - rank)], [3.0 * rank]]])  # [1][4][1]
+        r.combine_stats(raw, world)
+        q.put((rank, held, raw.flatten().tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_exchange_and_statistics_over_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, held, raw = q.get(timeout=120)
+        results[rank] = (held, raw)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, (held, raw) in results.items():
+        for src, a, b in held:
+            assert a == src and b == src  # the K/V of the scheduled source rank
+        assert raw[0] == sum(1.0 + r for r in range(world))
+        assert raw[1] == sum(2.0 * r for r in range(world))
+        assert raw[2] == max(-(5.0 - r) for r in range(world))
+        assert raw[3] == max(3.0 * r for r in range(world))
