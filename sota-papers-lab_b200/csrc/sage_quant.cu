@@ -65,12 +65,18 @@ __device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const flo
     if (tid < QTILE / QGROUP) gmax[tid] = 0u;
     __syncthreads();
     float qv[NI][8];
+    uint4 raw[NI];  // every load of the tile first
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        raw[i] = load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, tok < g.tokens);
+    }
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tl = tid / CH + i * TPI;
         const int tok = tile * QTILE + tl;
         const bool ok = tok < g.tokens;
-        unpack_bf16x8(load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, ok), qv[i]);
+        unpack_bf16x8(raw[i], qv[i]);
         if (g.flags & LN_Q) layernorm8<D>(qv[i], ln, ln + D, ch, g.ln_eps);
         float amax = 0.f;
 #pragma unroll
@@ -119,14 +125,22 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
         vmn[e] = 3.0e38f;
         vmx[e] = -3.0e38f;
     }
+    uint4 kr[NI], vr[NI];  // every load of the tile first
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        const bool ok = tok < g.tokens;
+        kr[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, ok);
+        vr[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, ok);
+    }
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tl = tid / CH + i * TPI;
         const int tok = tile * QTILE + tl;
         const bool ok = tok < g.tokens;
         float fk[8], fv[8];
-        unpack_bf16x8(load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, ok), fk);
-        unpack_bf16x8(load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, ok), fv);
+        unpack_bf16x8(kr[i], fk);
+        unpack_bf16x8(vr[i], fv);
         if (g.flags & LN_K) layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
         if (ok) {
 #pragma unroll
@@ -182,16 +196,17 @@ __global__ void __launch_bounds__(256) sp_prep(const uint16_t* __restrict__ q, c
         prep_stats<D>(k, v, ln, part, g, tile, y - g.heads, b);
 }
 
-// Per (kv head, batch): K mean, V mean, V scale and its reciprocal from the
-// tile partials, the tiles summed as two interleaved accumulators.
+// Per (kv head, batch, 32 channels): K mean, V mean, V scale and its
+// reciprocal from the tile partials, the tiles summed as two interleaved
+// accumulators.  128 threads: (statistic, channel).
 template <int D>
-__global__ void __launch_bounds__(256) sp_finalize(const float* __restrict__ part, float* __restrict__ stats,
+__global__ void __launch_bounds__(128) sp_finalize(const float* __restrict__ part, float* __restrict__ stats,
                                                    const Geom g) {
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const long long bh = (long long)b * g.kv_heads + h;
-    __shared__ float st[4][D];
-    for (int c = tid; c < 4 * D; c += 256) {
-        const int stat = c / D, d = c % D;
+    const int stat = tid >> 5, d = blockIdx.z * 32 + (tid & 31);
+    __shared__ float st[4][32];
+    {
         const float* p = part + bh * g.q_tiles * 4 * D + stat * D + d;
         float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
         float r1 = r0;
@@ -213,14 +228,14 @@ __global__ void __launch_bounds__(256) sp_finalize(const float* __restrict__ par
             const float x0 = p[(long long)t * 4 * D];
             r0 = stat < 2 ? r0 + x0 : (stat == 2 ? fminf(r0, x0) : fmaxf(r0, x0));
         }
-        st[stat][d] = stat < 2 ? r0 + r1 : (stat == 2 ? fminf(r0, r1) : fmaxf(r0, r1));
+        st[stat][tid & 31] = stat < 2 ? r0 + r1 : (stat == 2 ? fminf(r0, r1) : fmaxf(r0, r1));
     }
     __syncthreads();
-    for (int d = tid; d < D; d += 256) {
+    if (tid < 32) {
         const float n = (float)g.tokens;
-        const float mk = (g.flags & SMOOTH_K) ? st[0][d] / n : 0.f;
-        const float mv = (g.flags & SMOOTH_V) ? st[1][d] / n : 0.f;
-        const float amax = fmaxf(st[3][d] - mv, mv - st[2][d]);
+        const float mk = (g.flags & SMOOTH_K) ? st[0][tid] / n : 0.f;
+        const float mv = (g.flags & SMOOTH_V) ? st[1][tid] / n : 0.f;
+        const float amax = fmaxf(st[3][tid] - mv, mv - st[2][tid]);
         const float scale = amax > 0.f ? amax / g.v_range : 1.0f;
         float* o = stats + bh * 4 * D;
         o[d] = mk;
@@ -285,6 +300,40 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
     const float* st = stats + bh * 4 * D;
     float kv[NI][8];
     float amax = 0.f;
+    if (g.merge == 1 && !(g.flags & LN_K)) {
+        // Dense keys: every load of the block first (one member per key, so
+        // ksum = 0 + k and rc = 1 exactly: the same arithmetic as below).
+        uint4 kr[NI], vr[NI];
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const int j = blk * KBLOCK + tid / CH + i * TPI;
+            const bool ok = j < g.tk;
+            kr[i] = load8(k + b * g.k_sb + (long long)j * g.k_st + h * g.k_sh + ch * 8, ok);
+            vr[i] = load8(v + b * g.v_sb + (long long)j * g.v_st + h * g.v_sh + ch * 8, ok);
+        }
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const int kl = tid / CH + i * TPI;
+            const bool ok = blk * KBLOCK + kl < g.tk;
+            float fk[8], fv[8], vq[8];
+            unpack_bf16x8(kr[i], fk);
+            unpack_bf16x8(vr[i], fv);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int d = ch * 8 + e;
+                // 0 + x: the member sum of the general path (it maps -0 to +0)
+                kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -st[d]) : 0.f;
+                amax = fmaxf(amax, fabsf(kv[i][e]));
+                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -st[D + d]) * st[3 * D + d] : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
+                vt[ch * 8 + e][kl] = (uint8_t)(two & 0xff);
+                vt[ch * 8 + e + 1][kl] = (uint8_t)(two >> 8);
+            }
+        }
+    } else
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int kl = tid / CH + i * TPI;
@@ -382,7 +431,7 @@ static cudaError_t prepare_d(const void* q, const void* k, const void* v, const 
                              const Geom& g, cudaStream_t st) {
     sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g);
-    sp_finalize<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(buf.part, buf.stats, g);
+    sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
     sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
     return cudaGetLastError();
