@@ -298,6 +298,71 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
     __syncthreads();
 
     const float* st = stats + bh * 4 * D;
+    if (NI == 4 && g.merge == 1 && !(g.flags & LN_K)) {
+        // Dense keys, D = 128: thread (m, ch) takes the 4 consecutive keys
+        // 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7, so that each channel's
+        // 4 E4M3 bytes form one 32-bit word of the transposed tile (rows of
+        // 17 words: at most 4-way bank conflicts).  Every load first; one
+        // member per key, so ksum = 0 + k and rc = 1 exactly: the same
+        // arithmetic as the general path.
+        __shared__ uint32_t vw[D][17];
+        const int m = tid / CH;
+        uint4 kr[NI], vr[NI];
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const int j = blk * KBLOCK + 4 * m + i;
+            const bool ok = j < g.tk;
+            kr[i] = load8(k + b * g.k_sb + (long long)j * g.k_st + h * g.k_sh + ch * 8, ok);
+            vr[i] = load8(v + b * g.v_sb + (long long)j * g.v_st + h * g.v_sh + ch * 8, ok);
+        }
+        float kq[NI][8];
+        float amx = 0.f;
+        uint32_t word[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const bool ok = blk * KBLOCK + 4 * m + i < g.tk;
+            float fk[8], fv[8];
+            unpack_bf16x8(kr[i], fk);
+            unpack_bf16x8(vr[i], fv);
+            float vq[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int d = ch * 8 + e;
+                kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -st[d]) : 0.f;
+                amx = fmaxf(amx, fabsf(kq[i][e]));
+                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -st[D + d]) * st[3 * D + d] : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
+                word[e] |= (two & 0xffu) << (8 * i);
+                word[e + 1] |= (two >> 8) << (8 * i);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
+        if (lane == 0) atomicMax(&kmax, __float_as_uint(amx));
+        __syncthreads();
+        const float km = __uint_as_float(kmax);
+        const float inv = km > 0.f ? 127.0f / km : 0.f;
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const float* f = kq[i];
+            uint2 w;
+            w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
+            w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+            *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + 4 * m + i) * D + ch * 8) = w;
+        }
+        if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
+        // V: channel d's 64 keys are the 16 words of row d
+        for (int c = tid; c < D * 16; c += 256) {
+            const int d = c >> 4, w = c & 15;
+            *reinterpret_cast<uint32_t*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) = vw[d][w];
+        }
+        return;
+    }
     float kv[NI][8];
     float amax = 0.f;
     if (g.merge == 1 && !(g.flags & LN_K)) {
