@@ -7,9 +7,10 @@
 // P = 448 * 2^(x - m) rounded to FP8 E4M3; each block's PV starts from zero
 // (FP32, in TMEM) and is folded into the FP32 output O = O * alpha + PV held
 // in registers (two-level accumulation); out = O / l * v_scale + v_mean in
-// bf16.  The S accumulator is read as the float 1.5 * 2^23 + S (exact for
-// |S| < 2^22) after one integer add, and the 1.5 * 2^23 offset is folded
-// into the exp2 FFMA, as the reference does.
+// bf16.  The S accumulator starts at the integer 1.5 * 2^23 (copied from
+// shared memory by tcgen05.cp ahead of each QK^T), so the finished S32 value
+// read as a float is 1.5 * 2^23 + S (exact for |S| < 2^22); the offset folds
+// into the exp2 FFMA, as the reference's float trick does.
 //
 // Structure: one CTA = 128 query rows of one (batch, q head), 12 warps.
 //   warps 0-7  softmax + correction.  Warp w owns the 16 rows
@@ -84,7 +85,8 @@ struct AttnSmem {
     static constexpr int K_OFF = Q_OFF + Q_BYTES;
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
     static constexpr int P_OFF = V_OFF + VST * V_BYTES;
-    static constexpr int END = P_OFF + 2 * P_BYTES;
+    static constexpr int M_OFF = P_OFF + 2 * P_BYTES;  // 4 KB of 1.5 * 2^23 for the S refill
+    static constexpr int END = M_OFF + 4096;
     static constexpr int DYN = END + 1024;  // slack to align the base to 1024
 };
 
@@ -148,8 +150,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
     const uint32_t sQ = sbase + L::Q_OFF, sK = sbase + L::K_OFF, sV = sbase + L::V_OFF, sP = sbase + L::P_OFF;
+    const uint32_t sM = sbase + L::M_OFF;
     auto bar = [](uint64_t& x) { return smem_u32(&x); };
 
+    for (int i = tid; i < 1024; i += NTHREADS)
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(sM + 4 * i), "r"(MAGIC_I) : "memory");
+    fence_proxy_async_smem();
     if (tid == 0) {
         abort_s = ld_volatile(err) != 0 ? 1u : 0u;
         mbar_init(bar(bars.q_full), 1);
@@ -227,6 +233,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ QK^T issuer
         if (lane == 0) {
             bool ok = mbar_wait(bar(bars.q_full), 0, err, 10);
+            const uint64_t mdesc = smem_desc(sM, 256, 0);  // 4 KB of 1.5 * 2^23 (no swizzle)
             auto issue_qk = [&](int jj) -> bool {
                 const int s = jj % KST;
                 if (!mbar_wait(bar(bars.k_full[s]), (jj / KST) & 1, err, 11)) return false;
@@ -234,10 +241,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc_fence_after();
                 const uint32_t d_s = tmem + ((jj & 1) ? TM_S1 : TM_S0);
                 const uint32_t kaddr = sK + s * L::K_BYTES;
+                // S starts at 1.5 * 2^23 (tcgen05.cp from shared memory, in
+                // issue order before the MMAs that accumulate onto it)
+#pragma unroll
+                for (int c = 0; c < 128; c += 8) tmem_cp_128x256b(d_s + c, mdesc);
 #pragma unroll
                 for (int kk = 0; kk < D / 32; kk++)
                     umma_i8(d_s, smem_desc(sQ + kk * 32, QK_SBO, SWZ), smem_desc(kaddr + kk * 32, QK_SBO, SWZ),
-                            IDESC_QK, kk > 0);
+                            IDESC_QK, 1);  // onto 1.5 * 2^23
                 tc_commit(bar(bars.s_full[jj & 1]));
                 tc_commit(bar(bars.k_empty[s]));
                 return true;
@@ -354,11 +365,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int c = 0; c < 64; c++) {
                     const int key = key0 + c;
                     const float kb = key < g.tk_pad ? __ldg(kbias + key) : __int_as_float(0xff800000);
-                    x[c] = fmaf(__uint_as_float(sr[c] + MAGIC_I), sc, kb + c0);
+                    x[c] = fmaf(__uint_as_float(sr[c]), sc, kb + c0);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < 64; c++) x[c] = __uint_as_float(sr[c] + MAGIC_I);
+                for (int c = 0; c < 64; c++) x[c] = __uint_as_float(sr[c]);
             }
             if (j * BLK + BLK > g.tk || (CAUSAL && j * BLK + BLK > qt * 128)) {
 #pragma unroll

@@ -278,6 +278,12 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// TMEM <- shared memory, 128 lanes x 256 bits (8 columns), asynchronous,
+// ordered with this thread's tcgen05.mma.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc));
+}
+
 // Instruction descriptor (tcgen05 "instruction descriptor" for kind::f16 /
 // f8f6f4 / i8): c_format bits 4-5, a/b formats 7-9 / 10-12, K-major A and B
 // (bits 15/16 clear), N>>3 at 17-22, M>>4 at 24-28.
