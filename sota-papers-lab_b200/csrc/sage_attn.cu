@@ -12,7 +12,10 @@
 // read as a float is 1.5 * 2^23 + S (exact for |S| < 2^22); the offset folds
 // into the exp2 FFMA, as the reference's float trick does.
 //
-// Structure: one CTA = 128 query rows of one (batch, q head), 12 warps.
+// Structure: persistent, one CTA per SM working through 128-row query tiles
+// of (batch, q head) in turn (causal: the heaviest first); every ring and
+// buffer carries on from one tile to the next, so a tile's output is written
+// while the next tile's loads and QK^T run.  12 warps.
 //   warps 0-7  softmax + correction.  Warp w owns the 16 rows
 //              32*(w%4) + 16*(w/4) + (0..15) (its TMEM lane quarter is w%4);
 //              lane t < 16 handles keys 0-63 of every 128-key block and
@@ -44,21 +47,6 @@
 
 namespace sp {
 
-// Pipeline timestamps of the first CTA (debug builds with -DSP_TRACE only;
-// compiled out otherwise).  Slot = role * 1024 + block * 8 + event.
-#ifdef SP_TRACE
-__device__ unsigned long long sp_trace_buf[4096];
-#define SP_TR(cond, role, jb, ev)                                      \
-    do {                                                               \
-        if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && (jb) < 128) \
-            sp_trace_buf[(role) * 1024 + (jb) * 8 + (ev)] = clock64(); \
-    } while (0)
-#else
-#define SP_TR(cond, role, jb, ev) \
-    do {                          \
-    } while (0)
-#endif
-
 constexpr int KST = 3;   // K ring depth
 constexpr int VST = 3;   // V ring depth
 #ifndef SP_EXP_POLY
@@ -82,7 +70,7 @@ struct AttnSmem {
     static constexpr int V_BYTES = D * 128;
     static constexpr int P_BYTES = 128 * 128;
     static constexpr int Q_OFF = 0;
-    static constexpr int K_OFF = Q_OFF + Q_BYTES;
+    static constexpr int K_OFF = Q_OFF + 2 * Q_BYTES;  // Q double-buffered (consecutive tiles)
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
     static constexpr int P_OFF = V_OFF + VST * V_BYTES;
     static constexpr int M_OFF = P_OFF + 2 * P_BYTES;  // 4 KB of 1.5 * 2^23 for the S refill
@@ -91,7 +79,7 @@ struct AttnSmem {
 };
 
 struct Bars {
-    uint64_t q_full;
+    uint64_t q_full[2], q_empty[2];
     uint64_t k_full[KST], k_empty[KST];
     uint64_t v_full[VST], v_empty[VST];
     uint64_t s_full[2];
@@ -109,9 +97,9 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_
     return warp_all_wait(bar, parity, err, site);
 }
 
-// PARTIAL (context parallelism): the CTA's query tiles are tiles
-// q_tile0 + blockIdx.y of the workspace, its keys keys k_key0 .. k_key0 + tk
-// of the K/V buffer (CAUSAL then means key i is seen by query i and later of
+// PARTIAL (context parallelism): query tile i of the segment is tile
+// q_tile0 + i of the workspace, the keys are keys k_key0 .. k_key0 + tk of
+// the K/V buffer (CAUSAL then means key i is seen by query i and later of
 // the segment); the result is merged into the fp32 accumulator acc and the
 // per-row log2 softmax denominator lse by log-sum-exp instead of written.
 template <int D, bool CAUSAL, bool MERGE, bool PARTIAL>
@@ -135,18 +123,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint32_t abort_s;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int bh_q = blockIdx.x;
-    const int n_qt = (int)gridDim.y;
-    const int qt = CAUSAL ? n_qt - 1 - (int)blockIdx.y : (int)blockIdx.y;  // tile within the segment
-    const int b = bh_q / g.heads, h = bh_q % g.heads;
+    // Persistent: CTA c takes tiles c, c + gridDim.x, ...  Tile t is query
+    // tile row t / (B*H) (causal: the heaviest rows first) of (batch, head)
+    // t % (B*H), so that CTAs running together share each kv head's K/V.
+    const int n_qt = g.q_tiles;  // query tiles per (batch, head) (of the segment)
+    const int n_bh = g.batch * g.heads;
+    const int ntiles = n_bh * n_qt;
     const int group = g.heads / g.kv_heads;
-    const int bh_kv = b * g.kv_heads + h / group;
     const int nkb64 = g.tk_pad / KBLOCK;  // k_scale row length of the K/V buffer
     // segment offsets (context parallelism only; compile-time zero otherwise)
     const int q_tile0 = PARTIAL ? g.q_tile0 : 0, k_key0 = PARTIAL ? g.k_key0 : 0;
     const int nkb64_seg = PARTIAL ? (g.tk + KBLOCK - 1) / KBLOCK : nkb64;  // 64-key blocks attended
     const int nkb = (g.tk + BLK - 1) / BLK;
-    const int nb = CAUSAL ? min(nkb, qt + 1) : nkb;
+    struct Tile {
+        int bh_q, b, h, bh_kv, qt, nb;
+    };
+    auto tile_of = [&](int t) {
+        Tile x;
+        const int qi = t / n_bh;
+        x.bh_q = t % n_bh;
+        x.b = x.bh_q / g.heads;
+        x.h = x.bh_q % g.heads;
+        x.bh_kv = x.b * g.kv_heads + x.h / group;
+        x.qt = CAUSAL ? n_qt - 1 - qi : qi;  // tile within the segment
+        x.nb = CAUSAL ? min(nkb, x.qt + 1) : nkb;
+        return x;
+    };
 
     const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
     const uint32_t sQ = sbase + L::Q_OFF, sK = sbase + L::K_OFF, sV = sbase + L::V_OFF, sP = sbase + L::P_OFF;
@@ -158,7 +160,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     fence_proxy_async_smem();
     if (tid == 0) {
         abort_s = ld_volatile(err) != 0 ? 1u : 0u;
-        mbar_init(bar(bars.q_full), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(bars.q_full[i]), 1);
+            mbar_init(bar(bars.q_empty[i]), 1);
+        }
         for (int i = 0; i < KST; i++) {
             mbar_init(bar(bars.k_full[i]), 1);
             mbar_init(bar(bars.k_empty[i]), 1);
@@ -187,27 +192,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
 
+    // Every role walks the same tiles; J counts this CTA's 128-key blocks over
+    // all its tiles and drives every ring index and phase, so the buffers
+    // carry from one tile to the next.
     if (warp == K_WARP) {
         // ------------------------------------------------------------ Q and K loads
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
-            mbar_expect_tx(bar(bars.q_full), L::Q_BYTES);
-            tma_load_3d(sQ, &map_q, bar(bars.q_full), 0, (q_tile0 + qt) * 128, bh_q);
-            int nk = 0;
-            for (int j = 0; j < nb; j++) {
-                const int ks = j % KST;
-                if (j >= KST && !mbar_wait(bar(bars.k_empty[ks]), ((j / KST) - 1) & 1, err, 1)) break;
-                SP_TR(true, 0, j, 0);
-                mbar_expect_tx(bar(bars.k_full[ks]), L::K_BYTES);
-                tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, k_key0 + j * BLK, bh_kv);
-                nk++;
+            int J = 0, nq = 0;
+            bool ok = true;
+            for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+                const Tile x = tile_of(t);
+                const int qb = it & 1;
+                // Q buffer qb is free once the QK^T of tile it - 2 is done
+                if (it >= 2 && !mbar_wait(bar(bars.q_empty[qb]), ((it >> 1) - 1) & 1, err, 6)) break;
+                mbar_expect_tx(bar(bars.q_full[qb]), L::Q_BYTES);
+                tma_load_3d(sQ + qb * L::Q_BYTES, &map_q, bar(bars.q_full[qb]), 0, (q_tile0 + x.qt) * 128, x.bh_q);
+                nq++;
+                for (int j = 0; j < x.nb; j++) {
+                    const int ks = J % KST;
+                    if (J >= KST && !mbar_wait(bar(bars.k_empty[ks]), ((J / KST) - 1) & 1, err, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(bar(bars.k_full[ks]), L::K_BYTES);
+                    tma_load_3d(sK + ks * L::K_BYTES, &map_k, bar(bars.k_full[ks]), 0, k_key0 + j * BLK, x.bh_kv);
+                    J++;
+                }
             }
             // Drain: every load issued lands before the CTA exits (these
             // waits ignore the error word and stop only at the time limit).
-            mbar_wait(bar(bars.q_full), 0, err, 3, false);
-            for (int s = 0; s < KST && s < nk; s++) {
-                const int last = s + ((nk - 1 - s) / KST) * KST;
+            for (int qb = 0; qb < 2 && qb < nq; qb++) {
+                const int last = qb + ((nq - 1 - qb) / 2) * 2;
+                mbar_wait(bar(bars.q_full[qb]), (last >> 1) & 1, err, 3, false);
+            }
+            for (int s = 0; s < KST && s < J; s++) {
+                const int last = s + ((J - 1 - s) / KST) * KST;
                 mbar_wait(bar(bars.k_full[s]), (last / KST) & 1, err, 4, false);
             }
         }
@@ -215,51 +236,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------------------------------------ V loads
         if (lane == 0) {
             tma_prefetch_desc(&map_v);
-            int nv = 0;
-            for (int j = 0; j < nb; j++) {
-                const int vs = j % VST;
-                if (j >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((j / VST) - 1) & 1, err, 2)) break;
-                SP_TR(true, 0, j, 1);
-                mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
-                tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), k_key0 + j * BLK, 0, bh_kv);
-                nv++;
+            int J = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const Tile x = tile_of(t);
+                for (int j = 0; j < x.nb; j++) {
+                    const int vs = J % VST;
+                    if (J >= VST && !mbar_wait(bar(bars.v_empty[vs]), ((J / VST) - 1) & 1, err, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(bar(bars.v_full[vs]), L::V_BYTES);
+                    tma_load_3d(sV + vs * L::V_BYTES, &map_v, bar(bars.v_full[vs]), k_key0 + j * BLK, 0, x.bh_kv);
+                    J++;
+                }
             }
-            for (int s = 0; s < VST && s < nv; s++) {
-                const int last = s + ((nv - 1 - s) / VST) * VST;
+            for (int s = 0; s < VST && s < J; s++) {
+                const int last = s + ((J - 1 - s) / VST) * VST;
                 mbar_wait(bar(bars.v_full[s]), (last / VST) & 1, err, 5, false);
             }
         }
     } else if (warp == QK_WARP) {
         // ------------------------------------------------------------ QK^T issuer
         if (lane == 0) {
-            bool ok = mbar_wait(bar(bars.q_full), 0, err, 10);
             const uint64_t mdesc = smem_desc(sM, 256, 0);  // 4 KB of 1.5 * 2^23 (no swizzle)
-            auto issue_qk = [&](int jj) -> bool {
-                const int s = jj % KST;
-                if (!mbar_wait(bar(bars.k_full[s]), (jj / KST) & 1, err, 11)) return false;
-                SP_TR(true, 1, jj, 0);
-                tc_fence_after();
-                const uint32_t d_s = tmem + ((jj & 1) ? TM_S1 : TM_S0);
-                const uint32_t kaddr = sK + s * L::K_BYTES;
-                // S starts at 1.5 * 2^23 (tcgen05.cp from shared memory, in
-                // issue order before the MMAs that accumulate onto it)
+            int J = 0;
+            bool ok = true;
+            for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+                const Tile x = tile_of(t);
+                const int qb = it & 1;
+                const uint32_t qaddr = sQ + qb * L::Q_BYTES;
+                if (!(ok = mbar_wait(bar(bars.q_full[qb]), (it >> 1) & 1, err, 10))) break;
+                for (int j = 0; j < x.nb; j++, J++) {
+                    // S[J % 2] was read by every softmax warp (block J - 2)
+                    if (J >= 2 && !(ok = mbar_wait(bar(bars.p_full[J & 1]), ((J - 2) >> 1) & 1, err, 12))) break;
+                    const int s = J % KST;
+                    if (!(ok = mbar_wait(bar(bars.k_full[s]), (J / KST) & 1, err, 11))) break;
+                    tc_fence_after();
+                    const uint32_t d_s = tmem + ((J & 1) ? TM_S1 : TM_S0);
+                    const uint32_t kaddr = sK + s * L::K_BYTES;
+                    // S starts at 1.5 * 2^23 (tcgen05.cp from shared memory, in
+                    // issue order before the MMAs that accumulate onto it)
 #pragma unroll
-                for (int c = 0; c < 128; c += 8) tmem_cp_128x256b(d_s + c, mdesc);
+                    for (int c = 0; c < 128; c += 8) tmem_cp_128x256b(d_s + c, mdesc);
 #pragma unroll
-                for (int kk = 0; kk < D / 32; kk++)
-                    umma_i8(d_s, smem_desc(sQ + kk * 32, QK_SBO, SWZ), smem_desc(kaddr + kk * 32, QK_SBO, SWZ),
-                            IDESC_QK, 1);  // onto 1.5 * 2^23
-                tc_commit(bar(bars.s_full[jj & 1]));
-                tc_commit(bar(bars.k_empty[s]));
-                return true;
-            };
-            if (ok) ok = issue_qk(0);
-            if (ok && nb > 1) ok = issue_qk(1);
-            for (int j = 0; j + 2 < nb && ok; j++) {
-                // S[j % 2] has been read by every softmax warp
-                ok = mbar_wait(bar(bars.p_full[j & 1]), (j >> 1) & 1, err, 12);
-                SP_TR(true, 1, j, 1);
-                if (ok) ok = issue_qk(j + 2);
+                    for (int kk = 0; kk < D / 32; kk++)
+                        umma_i8(d_s, smem_desc(qaddr + kk * 32, QK_SBO, SWZ), smem_desc(kaddr + kk * 32, QK_SBO, SWZ),
+                                IDESC_QK, 1);  // onto 1.5 * 2^23
+                    tc_commit(bar(bars.s_full[J & 1]));
+                    tc_commit(bar(bars.k_empty[s]));
+                }
+                if (ok) tc_commit(bar(bars.q_empty[qb]));  // the tile's Q is read once its MMAs complete
             }
             // No MMA may be in flight when TMEM is freed.
             tc_commit(bar(bars.qk_done));
@@ -268,24 +295,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == PV_WARP) {
         // ------------------------------------------------------------ PV issuer
         if (lane == 0) {
+            int J = 0;
             bool ok = true;
-            for (int j = 0; j < nb && ok; j++) {
-                const int pb = j & 1, vs = j % VST;
-                // P(j) is written; p_full(j) also means every warp has folded
-                // PV(j - 2) into its O, so PV buffer pb is free.
-                ok = mbar_wait(bar(bars.p_full[pb]), (j >> 1) & 1, err, 13);
-                if (ok) ok = mbar_wait(bar(bars.v_full[vs]), (j / VST) & 1, err, 14);
-                if (!ok) break;
-                SP_TR(true, 1, j, 3);
-                tc_fence_after();
-                const uint32_t paddr = sP + pb * L::P_BYTES, vaddr = sV + vs * L::V_BYTES;
-                const uint32_t d_pv = tmem + (pb ? TM_PV1 : TM_PV0);
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const Tile x = tile_of(t);
+                for (int j = 0; j < x.nb && ok; j++, J++) {
+                    const int pb = J & 1, vs = J % VST;
+                    // P(J) is written; p_full(J) also means every warp has
+                    // folded PV(J - 2) into its O, so PV buffer pb is free.
+                    ok = mbar_wait(bar(bars.p_full[pb]), (J >> 1) & 1, err, 13) &&
+                         mbar_wait(bar(bars.v_full[vs]), (J / VST) & 1, err, 14);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t paddr = sP + pb * L::P_BYTES, vaddr = sV + vs * L::V_BYTES;
+                    const uint32_t d_pv = tmem + (pb ? TM_PV1 : TM_PV0);
 #pragma unroll
-                for (int kk = 0; kk < BLK / 32; kk++)
-                    umma_f8(d_pv, smem_desc(paddr + kk * 32, 1024, SWZ_128B),
-                            smem_desc(vaddr + kk * 32, 1024, SWZ_128B), IDESC_PV, kk > 0);
-                tc_commit(bar(bars.v_empty[vs]));
-                tc_commit(bar(bars.p_free[pb]));
+                    for (int kk = 0; kk < BLK / 32; kk++)
+                        umma_f8(d_pv, smem_desc(paddr + kk * 32, 1024, SWZ_128B),
+                                smem_desc(vaddr + kk * 32, 1024, SWZ_128B), IDESC_PV, kk > 0);
+                    tc_commit(bar(bars.v_empty[vs]));
+                    tc_commit(bar(bars.p_free[pb]));
+                }
             }
             tc_commit(bar(bars.pv_done));
             mbar_wait(bar(bars.pv_done), 0, err, 16, false);
@@ -296,11 +326,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int half = lane >> 4;                             // 0: keys 0-63, 1: keys 64-127
         const int r = quarter * 32 + sub * 16 + (lane & 15);    // query row in the tile = TMEM lane
         const uint32_t lane_base = (uint32_t)(quarter * 32 + sub * 16) << 16;
+        const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+        int J = 0;  // this CTA's blocks so far
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const Tile tl = tile_of(t);
+        const int bh_q = tl.bh_q, bh_kv = tl.bh_kv, qt = tl.qt, nb = tl.nb;
         const int qrow = qt * 128 + r;                          // within the segment (masking)
         const int qrow_ws = PARTIAL ? (q_tile0 + qt) * 128 + r : qrow;  // within the workspace
         const float qs = q_scale[(long long)bh_q * (g.tq_pad / QGROUP) + qrow_ws / QGROUP];
         const float* ksc = k_scale + (long long)bh_kv * nkb64 + k_key0 / KBLOCK;
-        const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
         float o[DH];
 #pragma unroll
         for (int c = 0; c < DH; c++) o[c] = 0.f;
@@ -310,7 +345,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return __ldg(ksc + (i < nkb64_seg ? i : 2 * jb));
         };
         float ks = kscale(0);
-        bool ok = true;
         // O = O * a + PV[block jj] for this lane's D/2 columns: the second
         // level of the FP32 accumulation (each block's PV starts from zero).
         // Waiting for p_free[jj % 2] (committed after PV(jj)) also frees
@@ -318,7 +352,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         auto correct = [&](int jj, float a) -> bool {
             const int pb = jj & 1;
             if (!warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31)) return false;
-            SP_TR(lane == 0 && warp == 0, 2, jj, 6);
             tc_fence_after();
             const uint64_t a2 = pk2(a, a);
 #pragma unroll
@@ -335,16 +368,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             return true;
         };
-        for (int j = 0; j < nb; j++) {
-            const int sb = j & 1;
+        for (int j = 0; j < nb; j++, J++) {
+            const int sb = J & 1;
             const float sc = qs * ks;
             if (j + 1 < nb) ks = kscale(j + 1);
-            SP_TR(lane == 0 && warp == 0, 2, j, 0);
-            if (!warp_wait(bar(bars.s_full[sb]), (j >> 1) & 1, err, 20)) {
+            if (!warp_wait(bar(bars.s_full[sb]), (J >> 1) & 1, err, 20)) {
                 ok = false;
                 break;
             }
-            SP_TR(lane == 0 && warp == 0, 2, j, 1);
             tc_fence_after();
             uint32_t sr[64];
             {
@@ -389,10 +420,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float mnew = fmax3(m, pm, __shfl_xor_sync(0xffffffffu, pm, 16));
             const float alpha = ex2(m - mnew);
             m = mnew;
-            SP_TR(lane == 0 && warp == 0, 2, j, 2);
             // P = 448 * 2^(x - m) as E4M3 into the swizzled P tile (buffer
             // sb is free: PV(j - 2) is done, see correct()).
-            SP_TR(lane == 0 && warp == 0, 2, j, 3);
             const uint32_t prow_addr = sP + sb * L::P_BYTES + prow;
             const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
             const uint64_t sc2 = pk2(MERGE ? 1.0f : sc, MERGE ? 1.0f : sc), off2 = pk2(off, off);
@@ -432,23 +461,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(bars.p_full[sb]));  // one arrival per warp
-            SP_TR(lane == 0 && warp == 0, 2, j, 4);
             // fold the previous block's PV into O while this block's PV runs
-            if (j >= 1 && !correct(j - 1, alpha_prev)) {
+            if (j >= 1 && !correct(J - 1, alpha_prev)) {
                 ok = false;
                 break;
             }
-            SP_TR(lane == 0 && warp == 0, 2, j, 5);
             alpha_prev = alpha;
         }
-        if (ok) ok = correct(nb - 1, alpha_prev);
+        if (ok) ok = correct(J - 1, alpha_prev);  // the tile's last block
         if (ok && !PARTIAL) {
             // out = O / l * v_scale + v_mean for this lane's D/2 columns
             const float inv = 1.0f / (l + __shfl_xor_sync(0xffffffffu, l, 16));
             const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
             const float* vscale = vmean + D;
             uint16_t* orow =
-                out + (long long)b * g.o_sb + (long long)qrow_ws * g.o_st + (long long)h * g.o_sh + half * DH;
+                out + (long long)(bh_q / g.heads) * g.o_sb + (long long)qrow_ws * g.o_st +
+                (long long)(bh_q % g.heads) * g.o_sh + half * DH;
             if (qrow_ws < g.tokens) {
 #pragma unroll
                 for (int c = 0; c < DH; c += 8) {
@@ -471,7 +499,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
             const float inv = 1.0f / lt;
             const float lse_new = m + log2f(lt) - LOG2_448;
-            float* lrow = lse + ((long long)b * g.heads + h) * g.tokens + qrow_ws;
+            float* lrow = lse + (long long)bh_q * g.tokens + qrow_ws;
             const float lse_old = *lrow;
             const float mx = fmaxf(lse_old, lse_new);
             const float w_old = lse_old == __int_as_float(0xff800000) ? 0.f : exp2f(lse_old - mx);
@@ -480,7 +508,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float a_old = w_old * s_inv, a_new = w_new * inv * s_inv;
             const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
             const float* vscale = vmean + D;
-            float* arow = acc + (long long)b * g.o_sb + (long long)qrow_ws * g.o_st + (long long)h * g.o_sh + half * DH;
+            float* arow = acc + (long long)(bh_q / g.heads) * g.o_sb + (long long)qrow_ws * g.o_st +
+                          (long long)(bh_q % g.heads) * g.o_sh + half * DH;
             if (qrow_ws < g.tokens) {
 #pragma unroll
                 for (int c = 0; c < DH; c += 4) {
@@ -495,8 +524,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             if (half == 0 && qrow_ws < g.tokens) *lrow = mx + log2f(w_old + w_new);
         }
+        }  // tiles
     }
-
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -515,7 +544,11 @@ static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom
         if (e != cudaSuccess) return e;
         if (dev < 32) attr_set |= 1u << dev;
     }
-    dim3 grid(g.batch * g.heads, q_tiles);
+    static int sms[32] = {0};  // SMs per device ordinal
+    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    const long long ntiles = (long long)g.batch * g.heads * q_tiles;
+    dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
     kern<<<grid, NTHREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,
                                                    buf.kbias, (uint16_t*)out, acc, lse, buf.err, g);
     return cudaGetLastError();
