@@ -123,9 +123,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __shared__ uint32_t abort_s;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // Persistent: CTA c takes tiles c, c + gridDim.x, ...  Tile t is query
-    // tile row t / (B*H) (causal: the heaviest rows first) of (batch, head)
-    // t % (B*H), so that CTAs running together share each kv head's K/V.
+    // Persistent: each CTA takes one tile of every round of gridDim.x tiles
+    // (tile_at).  Tile t is query tile row t / (B*H) (causal: the heaviest
+    // rows first) of (batch, head) t % (B*H), so that CTAs running together
+    // share each kv head's K/V.
     const int n_qt = g.q_tiles;  // query tiles per (batch, head) (of the segment)
     const int n_bh = g.batch * g.heads;
     const int ntiles = n_bh * n_qt;
@@ -135,6 +136,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int q_tile0 = PARTIAL ? g.q_tile0 : 0, k_key0 = PARTIAL ? g.k_key0 : 0;
     const int nkb64_seg = PARTIAL ? (g.tk + KBLOCK - 1) / KBLOCK : nkb64;  // 64-key blocks attended
     const int nkb = (g.tk + BLK - 1) / BLK;
+    // The CTA's it-th tile: round it of gridDim.x tiles, taken forwards in
+    // even rounds and backwards in odd ones, so that the heavy causal tiles
+    // of one round and the light ones of the next share a CTA.
+    auto tile_at = [&](int it) {
+        const int c = (it & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+        return it * (int)gridDim.x + c;
+    };
     struct Tile {
         int bh_q, b, h, bh_kv, qt, nb;
     };
@@ -202,7 +210,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tma_prefetch_desc(&map_k);
             int J = 0, nq = 0;
             bool ok = true;
-            for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+            for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
                 const Tile x = tile_of(t);
                 const int qb = it & 1;
                 // Q buffer qb is free once the QK^T of tile it - 2 is done
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tma_prefetch_desc(&map_v);
             int J = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
                 const Tile x = tile_of(t);
                 for (int j = 0; j < x.nb; j++) {
                     const int vs = J % VST;
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint64_t mdesc = smem_desc(sM, 256, 0);  // 4 KB of 1.5 * 2^23 (no swizzle)
             int J = 0;
             bool ok = true;
-            for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+            for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
                 const Tile x = tile_of(t);
                 const int qb = it & 1;
                 const uint32_t qaddr = sQ + qb * L::Q_BYTES;
@@ -297,7 +305,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) {
             int J = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
                 const Tile x = tile_of(t);
                 for (int j = 0; j < x.nb && ok; j++, J++) {
                     const int pb = J & 1, vs = J % VST;
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
         int J = 0;  // this CTA's blocks so far
         bool ok = true;
-        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
         const Tile tl = tile_of(t);
         const int bh_q = tl.bh_q, bh_kv = tl.bh_kv, qt = tl.qt, nb = tl.nb;
         const int qrow = qt * 128 + r;                          // within the segment (masking)
