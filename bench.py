@@ -54,6 +54,15 @@ WORKLOADS = {
 METRIC = "effective attention TOPS (4*B*H*N^2*D/t) at N=8k, d=128"
 
 
+def tensor_peak(eng):
+    """The tcgen05 INT8 and FP8 E4M3 dense rates measured by the library's
+    probe (best of two runs each, on a GPU not yet heated by the timed loop):
+    the burst figures, for kernels timed on their own."""
+    i8 = max(eng.tensor_peak(0, 128)[0] for _ in range(2))
+    f8 = max(eng.tensor_peak(1, 128)[0] for _ in range(2))
+    return i8, f8
+
+
 def effective_flops(w, batch):
     return 4.0 * batch * w["heads"] * w["tokens"] ** 2 * w["d"]
 
@@ -192,6 +201,7 @@ def run_layers(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
+    peaks_hw = tensor_peak(eng) if rank == 0 else (0.0, 0.0)
     for _ in range(args.warmup):
         for i in range(Lr):
             layer(i)
@@ -226,8 +236,7 @@ def run_layers(args, rank, world, local_rank):
         return None
     step_ms = ms_max / args.steps
     eff = Lr * effective_flops(w, B * world)
-    i8_peak, _ = eng.tensor_peak(0, 128)
-    f8_peak, _ = eng.tensor_peak(1, 128)
+    i8_peak, f8_peak = peaks_hw
     peak = min(i8_peak, f8_peak)
     alg = algorithmic_flops(w, B)
     return {
@@ -284,6 +293,7 @@ def run_ring(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
+    peaks_hw = tensor_peak(eng) if rank == 0 else (0.0, 0.0)
     for _ in range(args.warmup):
         rg.forward(tq, tk, tv, to)
     torch.cuda.synchronize()
@@ -330,8 +340,7 @@ def run_ring(args, rank, world, local_rank):
     value = effective_flops(w, B) / (step_ms * 1e-3) / 1e12
     alg_per_rank = algorithmic_flops(w, B) / world
     achieved = alg_per_rank / (step_ms * 1e-3) / 1e12
-    i8_peak, _ = eng.tensor_peak(0, 128)
-    f8_peak, _ = eng.tensor_peak(1, 128)
+    i8_peak, f8_peak = peaks_hw
     peak = min(i8_peak, f8_peak)
     pairs = 2 * world + 1
     return {
@@ -381,6 +390,7 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
+    peaks_hw = tensor_peak(eng) if rank == 0 else (0.0, 0.0)
     for _ in range(args.warmup):
         eng.forward(ws, tq, tk, tv, to, opts)
     torch.cuda.synchronize()
@@ -482,8 +492,7 @@ def run_ours(args, rank, world, local_rank):
     # The INT8 / FP8 dense tcgen05 rates are not in MEASURED_PEAKS.json: they
     # are measured here by the library's probe (one CTA per SM issuing
     # back-to-back M128 N128 MMAs); the slower of the two is the denominator.
-    i8_peak, _ = eng.tensor_peak(0, 128)
-    f8_peak, _ = eng.tensor_peak(1, 128)
+    i8_peak, f8_peak = peaks_hw
     peak = min(i8_peak, f8_peak)
     if qkv is not None:
         qkv["peak"] = peaks["bf16_tflops"]
