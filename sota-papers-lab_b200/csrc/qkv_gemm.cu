@@ -8,9 +8,11 @@
 // and write Q, K, V in [B][T][H][D] for the quantiser.
 //
 // Tile: 128 rows x 256 output channels (two heads of 128 or four of 64), K in
-// 64-element (128-byte) blocks through a 4-stage TMA ring.  Warp 0 loads,
-// warp 1 issues the MMAs (4 x M128 N256 K16 per block) and owns the 256 TMEM
-// columns, warps 4-7 run the epilogue, one thread per row.
+// 64-element (128-byte) blocks through a 4-stage TMA ring.  Persistent: one
+// CTA per SM works through the output tiles in turn, with two TMEM
+// accumulators (2 x 256 columns), so the epilogue of one tile overlaps the
+// MMAs of the next.  Warp 0 loads, warp 1 issues the MMAs (4 x M128 N256 K16
+// per block) and owns TMEM, warps 4-7 run the epilogue, one thread per row.
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
@@ -33,12 +35,15 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
     using namespace gemm;
     constexpr uint32_t IDESC = make_idesc(C_F32, F_BF16, F_BF16, BM, BN);
     extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full;
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t tmem_base_s;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int n_tiles = g.n / BN, ntiles = n_tiles * ((g.m + BM - 1) / BM);
     const int kblocks = (g.k + BK - 1) / BK;
+    // the CTA's it-th tile; consecutive tiles share their rows of x
+    auto tile_m0 = [&](int t) { return (t / n_tiles) * BM; };
+    auto tile_n0 = [&](int t) { return (t % n_tiles) * BN; };
     const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
     auto bar = [](uint64_t& x) { return smem_u32(&x); };
 
@@ -47,11 +52,15 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
             mbar_init(bar(full[i]), 1);
             mbar_init(bar(empty[i]), 1);
         }
-        mbar_init(bar(acc_full), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(acc_full[i]), 1);
+            mbar_init(bar(acc_empty[i]), 4);
+        }
+        mbar_init(bar(done), 1);
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(&tmem_base_s), BN);
+        tmem_alloc(smem_u32(&tmem_base_s), 2 * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -63,15 +72,22 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
         if (lane == 0) {
             tma_prefetch_desc(&map_x);
             tma_prefetch_desc(&map_w);
-            int issued = 0;
-            for (int kb = 0; kb < kblocks; kb++) {
-                const int s = kb % STAGES;
-                if (kb >= STAGES && !mbar_wait(bar(empty[s]), ((kb / STAGES) - 1) & 1, err, 40)) break;
-                const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
-                mbar_expect_tx(bar(full[s]), STAGE_BYTES);
-                tma_load_2d(sa, &map_x, bar(full[s]), kb * BK, m0);
-                tma_load_2d(sb, &map_w, bar(full[s]), kb * BK, n0);
-                issued++;
+            int issued = 0;  // k-blocks over all of this CTA's tiles
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int m0 = tile_m0(t), n0 = tile_n0(t);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    const int s = issued % STAGES;
+                    if (issued >= STAGES && !mbar_wait(bar(empty[s]), ((issued / STAGES) - 1) & 1, err, 40)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+                    mbar_expect_tx(bar(full[s]), STAGE_BYTES);
+                    tma_load_2d(sa, &map_x, bar(full[s]), kb * BK, m0);
+                    tma_load_2d(sb, &map_w, bar(full[s]), kb * BK, n0);
+                    issued++;
+                }
             }
             for (int s = 0; s < STAGES && s < issued; s++) {
                 const int last = s + ((issued - 1 - s) / STAGES) * STAGES;
@@ -81,29 +97,41 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             bool ok = true;
-            for (int kb = 0; kb < kblocks && ok; kb++) {
-                const int s = kb % STAGES;
-                ok = mbar_wait(bar(full[s]), (kb / STAGES) & 1, err, 42);
-                if (!ok) break;
+            int used = 0;  // k-blocks over all of this CTA's tiles
+            for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+                const int ab = it & 1;
+                // accumulator ab is free once the epilogue read tile it - 2
+                if (it >= 2 && !(ok = mbar_wait(bar(acc_empty[ab]), ((it >> 1) - 1) & 1, err, 45))) break;
                 tc_fence_after();
-                const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+                const uint32_t acc = tmem + ab * BN;
+                for (int kb = 0; kb < kblocks; kb++, used++) {
+                    const int s = used % STAGES;
+                    if (!(ok = mbar_wait(bar(full[s]), (used / STAGES) & 1, err, 42))) break;
+                    tc_fence_after();
+                    const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++)
-                    umma_bf16(tmem, smem_desc(sa + kk * 32, 1024, SWZ_128B), smem_desc(sb + kk * 32, 1024, SWZ_128B),
-                              IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(bar(empty[s]));
+                    for (int kk = 0; kk < BK / 16; kk++)
+                        umma_bf16(acc, smem_desc(sa + kk * 32, 1024, SWZ_128B),
+                                  smem_desc(sb + kk * 32, 1024, SWZ_128B), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(bar(empty[s]));
+                }
+                if (ok) tc_commit(bar(acc_full[ab]));
             }
-            tc_commit(bar(acc_full));
-            mbar_wait(bar(acc_full), 0, err, 43, false);
+            tc_commit(bar(done));
+            mbar_wait(bar(done), 0, err, 43, false);
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ epilogue, one thread per row
         const int r = tid - 128;
-        const int row = m0 + r;
         const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
-        const bool ok = warp_all_wait(bar(acc_full), 0, err, 44);
-        if (ok) {
+        bool ok = true;
+        for (int t = blockIdx.x, it = 0; t < ntiles && ok; t += gridDim.x, it++) {
+            const int ab = it & 1;
+            const int m0 = tile_m0(t), n0 = tile_n0(t);
+            const int row = m0 + r;
+            if (!(ok = warp_all_wait(bar(acc_full[ab]), (it >> 1) & 1, err, 44))) break;
             tc_fence_after();
+            const uint32_t acc = tmem + lane_off + ab * BN;
             const int bb = row / g.tokens, tok = row % g.tokens;
             // the row's position inside its frame selects the RoPE table row
             const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
@@ -126,7 +154,7 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
 #pragma unroll
                 for (int c = 0; c < D; c += 32) {
                     uint32_t v[32];
-                    tmem_ld32(tmem + lane_off + hh * D + c, v);
+                    tmem_ld32(acc + hh * D + c, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
@@ -161,13 +189,20 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
                         *reinterpret_cast<uint4*>(dst + c) = w;
                     }
                 }
+                if (hh == BN / D - 1) {
+                    // every TMEM read of the tile is done: the next tile may
+                    // accumulate into ab again
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(acc_empty[ab]));
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, BN);
+    if (warp == 1) tmem_dealloc(tmem, 2 * BN);
 }
 
 template <int D, int HALF>
@@ -182,7 +217,11 @@ static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float*
         if (e != cudaSuccess) return e;
         if (dev < 32) attr_set |= 1u << dev;
     }
-    dim3 grid(g.n / gemm::BN, (g.m + gemm::BM - 1) / gemm::BM);
+    static int sms[32] = {0};  // SMs per device ordinal
+    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    const long long ntiles = (long long)(g.n / gemm::BN) * ((g.m + gemm::BM - 1) / gemm::BM);
+    dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
     sp_qkv_gemm<D, HALF><<<grid, gemm::NTHREADS, gemm::SMEM, st>>>(maps.x, maps.w, bias, (const float2*)rope, q, k,
                                                                    v, err, g);
     return cudaGetLastError();
