@@ -64,26 +64,30 @@ __device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const flo
     __shared__ unsigned gmax[QTILE / QGROUP];
     if (tid < QTILE / QGROUP) gmax[tid] = 0u;
     __syncthreads();
-    float qv[NI][8];
-    uint4 raw[NI];  // every load of the tile first
+    // every load of the tile first; the values are unpacked (and normalised)
+    // again for the quantisation pass rather than kept as floats
+    uint4 raw[NI];
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tok = tile * QTILE + tid / CH + i * TPI;
         raw[i] = load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, tok < g.tokens);
     }
+    auto values = [&](int i, float (&f)[8]) {
+        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
+        unpack_bf16x8(raw[i], f);
+        if (g.flags & LN_Q) layernorm8<D>(f, ln, ln + D, ch, g.ln_eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (!ok) f[e] = 0.f;
+    };
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tl = tid / CH + i * TPI;
-        const int tok = tile * QTILE + tl;
-        const bool ok = tok < g.tokens;
-        unpack_bf16x8(raw[i], qv[i]);
-        if (g.flags & LN_Q) layernorm8<D>(qv[i], ln, ln + D, ch, g.ln_eps);
+        float qv[8];
+        values(i, qv);
         float amax = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            if (!ok) qv[i][e] = 0.f;
-            amax = fmaxf(amax, fabsf(qv[i][e]));
-        }
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(qv[e]));
         // The rows of one warp lie in one 16-row group (32 / CH <= 16 rows).
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -95,7 +99,8 @@ __device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const flo
         const int tl = tid / CH + i * TPI;
         const float amax = __uint_as_float(gmax[tl / QGROUP]);
         const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-        const float* f = qv[i];
+        float f[8];
+        values(i, f);
         uint2 w;
         w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
         w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
@@ -125,27 +130,49 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
         vmn[e] = 3.0e38f;
         vmx[e] = -3.0e38f;
     }
-    uint4 kr[NI], vr[NI];  // every load of the tile first
+    // K, then V: each a pass of loads issued first, then summed in token
+    // order (the K and V statistics are independent accumulations)
+    uint4 raw[NI];
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tok = tile * QTILE + tid / CH + i * TPI;
-        const bool ok = tok < g.tokens;
-        kr[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, ok);
-        vr[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, ok);
+        raw[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, tok < g.tokens);
     }
 #pragma unroll
     for (int i = 0; i < NI; i++) {
-        const int tl = tid / CH + i * TPI;
-        const int tok = tile * QTILE + tl;
-        const bool ok = tok < g.tokens;
-        float fk[8], fv[8];
-        unpack_bf16x8(kr[i], fk);
-        unpack_bf16x8(vr[i], fv);
+        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
+        float fk[8];
+        unpack_bf16x8(raw[i], fk);
         if (g.flags & LN_K) layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
         if (ok) {
 #pragma unroll
+            for (int e = 0; e < 8; e++) ks[e] += fk[e];
+        }
+    }
+    // the K sums through the lane butterfly now, so they need no registers
+    // during the V pass
+#pragma unroll
+    for (int o = CH; o < 32; o <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
+    }
+    if (lane < CH) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) red[warp][0][ch * 8 + e] = ks[e];
+    }
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        raw[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, tok < g.tokens);
+    }
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
+        float fv[8];
+        unpack_bf16x8(raw[i], fv);
+        if (ok) {
+#pragma unroll
             for (int e = 0; e < 8; e++) {
-                ks[e] += fk[e];
                 vs[e] += fv[e];
                 vmn[e] = fminf(vmn[e], fv[e]);
                 vmx[e] = fmaxf(vmx[e], fv[e]);
@@ -156,7 +183,6 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
     for (int o = CH; o < 32; o <<= 1) {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
             vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
             vmn[e] = fminf(vmn[e], __shfl_xor_sync(0xffffffffu, vmn[e], o));
             vmx[e] = fmaxf(vmx[e], __shfl_xor_sync(0xffffffffu, vmx[e], o));
@@ -165,7 +191,6 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
     if (lane < CH) {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            red[warp][0][ch * 8 + e] = ks[e];
             red[warp][1][ch * 8 + e] = vs[e];
             red[warp][2][ch * 8 + e] = vmn[e];
             red[warp][3][ch * 8 + e] = vmx[e];
@@ -185,7 +210,7 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
 }
 
 template <int D>
-__global__ void __launch_bounds__(256) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+__global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
                                                const uint16_t* __restrict__ v, const float* __restrict__ ln,
                                                int8_t* __restrict__ q8, float* __restrict__ q_scale,
                                                float* __restrict__ part, const Geom g) {
