@@ -285,7 +285,7 @@ def run_ring(args, rank, world, local_rank):
     k = (k + torch.randn(1, 1, G, D, generator=gb, device=dev) * w["k_bias"]).to(torch.bfloat16)
     out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
     eng = sage.SageAttention(stream, D)
-    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D)
+    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D, reserved_sms=args.reserve_sms)
     sq, skv = sage.Strides.bthd(T, H, D), sage.Strides.bthd(T, G, D)
     tq, tk, tv, to = sage.Tensor(q, sq), sage.Tensor(k, skv), sage.Tensor(v, skv), sage.Tensor(out, sq)
 
@@ -342,7 +342,6 @@ def run_ring(args, rank, world, local_rank):
     achieved = alg_per_rank / (step_ms * 1e-3) / 1e12
     i8_peak, f8_peak = peaks_hw
     peak = min(i8_peak, f8_peak)
-    pairs = 2 * world + 1
     return {
         "metric": f"effective attention TOPS (4*B*H*N^2*D/t), {args.workload}", "value": round(value, 2),
         "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
@@ -361,7 +360,8 @@ def run_ring(args, rank, world, local_rank):
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q, k, v)),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
                 "api": "RingAttention.forward via libsplsage C ABI, pinned host buffers (rank 0's bytes)"},
-        "gpu_launches": (4 + pairs + 1) * args.steps,
+        # per forward: prepare 2, K/V quantiser 2, one segment per ring step, finish 1
+        "gpu_launches": (5 + world) * args.steps,
         "clocks": clk.summary(),
         "device_error_word": word,
     }
@@ -639,6 +639,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="C4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reserve-sms", type=int, default=None,
+                    help="C5: SMs the attention leaves to NCCL during ring steps (default: the ring's own)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -126,6 +126,13 @@ void spl_sage_default_options(spl_sage_options* out);
 int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_sage** out);
 void spl_sage_destroy(spl_sage* s);
 
+/* No counterpart in the reference.  The attention and QKV GEMM kernels are
+ * persistent (one CTA per SM, each taking many tiles); with n > 0 they
+ * launch on all but n SMs, so that kernels running beside them on other
+ * streams (NCCL's send/recv during a ring step) find free SMs at once
+ * instead of waiting for the whole persistent launch.  0 by default. */
+int spl_sage_reserve_sms(spl_sage* s, int n);
+
 /* SageAttention::workspace (mod.rs:649-670) via Plan::new (mod.rs:405-440):
  * allocates the quantised buffers (zeroed, on the engine's stream).  merge
  * NULL = dense.  Causal with merging is rejected. */
@@ -248,7 +255,8 @@ int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const sp
  *      statistics (total_tokens = the whole sequence) into a K/V buffer.
  *   4. for every (query chunk, key chunk) pair that is not wholly masked,
  *      spl_sage_cp_attend against the K/V buffer holding those keys
- *      (received from their owner), merged into acc / lse.
+ *      (received from their owner), merged into acc / lse; pairs whose
+ *      queries and keys are contiguous go in one call.
  *   5. spl_sage_cp_finish: acc to bf16.
  * The quantised K/V are not bit-identical to a single-GPU prepare (the
  * channel sums are added in another order); results are tolerance-equal. */
@@ -268,12 +276,19 @@ int spl_sage_cp_quantize_kv(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor k, spl
                             spl_sage_kv* kv);
 /* Queries [q_begin, q_begin + q_len) of this rank (whole 128-row tiles)
  * against keys [k_begin, k_begin + k_len) of kv (k_begin a multiple of 128).
- * causal: the two segments cover the same positions (key i is seen by query
- * i and later); otherwise every key is seen.  Merged into acc f32
- * [b][t][h][D] and lse f32 [b][h][t] (t = this rank's tokens), which start
- * at 0 and -inf, by log-sum-exp. */
+ * flags:
+ *   SPL_SAGE_CP_CAUSAL  query i of the segment sees keys 0 .. i of the key
+ *                       segment (the two cover the same positions);
+ *                       otherwise every key is seen;
+ *   SPL_SAGE_CP_FIRST   the first segment of these query rows: acc and lse
+ *                       are written; otherwise the segment is merged into
+ *                       them by log-sum-exp.
+ * acc f32 [b][t][h][D], lse f32 [b][h][t] (t = this rank's tokens, lse the
+ * log2 softmax denominator). */
+#define SPL_SAGE_CP_CAUSAL 1
+#define SPL_SAGE_CP_FIRST 2
 int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
-                       int64_t k_begin, int64_t k_len, int causal, float* acc, float* lse);
+                       int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse);
 int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out);
 
 /* Tensor-core peak probe (the analog of the reference's sage_peak kernels,

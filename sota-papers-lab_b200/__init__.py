@@ -95,7 +95,12 @@ EXPORTS = [
     "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
+    "spl_sage_reserve_sms",
 ]
+
+# spl_sage_cp_attend flags
+CP_CAUSAL = 1
+CP_FIRST = 2
 
 _lib = None
 
@@ -114,6 +119,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_default_options.argtypes = [ctypes.POINTER(_Options)]
         L.spl_sage_create.argtypes = [P, I, ctypes.POINTER(_Config), ctypes.POINTER(P)]
         L.spl_sage_destroy.argtypes = [P]
+        L.spl_sage_reserve_sms.argtypes = [P, I]
         L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
         L.spl_sage_ws_destroy.argtypes = [P]
         L.spl_sage_ws_bytes.restype = ctypes.c_int64
@@ -362,6 +368,7 @@ class SageAttention:
         self.head_dim = head_dim
         self.config = cfg
         self.stream = stream
+        self.reserved_sms = 0
 
     @staticmethod
     def new(stream, head_dim: int) -> "SageAttention":
@@ -370,6 +377,12 @@ class SageAttention:
     @staticmethod
     def with_config(stream, head_dim: int, config: Config) -> "SageAttention":
         return SageAttention(stream, head_dim, config)
+
+    def reserve_sms(self, n: int):
+        """Persistent kernels of this engine leave n SMs free (for kernels on
+        other streams, e.g. NCCL's during a ring step); 0 restores all."""
+        _check(lib().spl_sage_reserve_sms(self._h, n))
+        self.reserved_sms = n
 
     def close(self):
         if self._h:
@@ -468,10 +481,12 @@ class SageAttention:
                                              ctypes.c_void_p(raw_global.data_ptr()), total_tokens, kv._h))
 
     def cp_attend(self, ws: Workspace, kv: "KvBuffer", q_begin: int, q_len: int, k_begin: int, k_len: int,
-                  causal: bool, acc, lse):
+                  causal: bool, acc, lse, first: bool = False):
         """Segment attention merged into acc (f32 [b][t][h][D]) and lse (f32
-        [b][h][t]) by log-sum-exp."""
-        _check(lib().spl_sage_cp_attend(self._h, ws._h, kv._h, q_begin, q_len, k_begin, k_len, int(causal),
+        [b][h][t]) by log-sum-exp; first: the segment is the first of its
+        query rows and overwrites acc and lse instead."""
+        flags = (CP_CAUSAL if causal else 0) | (CP_FIRST if first else 0)
+        _check(lib().spl_sage_cp_attend(self._h, ws._h, kv._h, q_begin, q_len, k_begin, k_len, flags,
                                         ctypes.c_void_p(acc.data_ptr()), ctypes.c_void_p(lse.data_ptr())))
 
     def cp_finish(self, ws: Workspace, acc, out: Tensor):

@@ -219,7 +219,8 @@ static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float*
     }
     static int sms[32] = {0};  // SMs per device ordinal
     if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)(g.n / gemm::BN) * ((g.m + gemm::BM - 1) / gemm::BM);
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
     sp_qkv_gemm<D, HALF><<<grid, gemm::NTHREADS, gemm::SMEM, st>>>(maps.x, maps.w, bias, (const float2*)rope, q, k,

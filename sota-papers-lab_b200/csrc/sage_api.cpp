@@ -98,8 +98,19 @@ struct spl_sage {
     int head_dim;
     spl_sage_config config;
     int device;
-    uint32_t* err;  // device error word of the calls that run without a workspace
+    int sm_count;
+    int reserved_sms;  // SMs the persistent kernels leave free (spl_sage_reserve_sms)
+    uint32_t* err;     // device error word of the calls that run without a workspace
 };
+
+namespace {
+// The CTA cap of this engine's persistent kernels (0: one per SM).
+int max_ctas(const spl_sage* s) {
+    if (s->reserved_sms <= 0) return 0;
+    const int n = s->sm_count - s->reserved_sms;
+    return n > 1 ? n : 1;
+}
+}  // namespace
 
 struct spl_sage_ws {
     int head_dim;
@@ -179,8 +190,19 @@ int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_
     s->head_dim = head_dim;
     s->config = c;
     s->device = dev;
+    s->sm_count = 0;
+    cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, dev);
+    s->reserved_sms = 0;
     s->err = errw;
     *out = s;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_reserve_sms(spl_sage* s, int n) {
+    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_reserve_sms: NULL engine");
+    if (n < 0 || n >= s->sm_count)
+        return fail(SPL_SAGE_ERR_INVALID, "cannot leave %d of %d SMs free", n, s->sm_count);
+    s->reserved_sms = n;
     return SPL_SAGE_OK;
 }
 
@@ -424,6 +446,7 @@ int spl_sage_attend(spl_sage* s, const spl_sage_ws* ws, spl_sage_tensor_mut out)
     g.o_sb = out.batch;
     g.o_st = out.token;
     g.o_sh = out.head;
+    g.max_ctas = max_ctas(s);
     cudaError_t e = sp::launch_attend(s->head_dim, ws->maps, ws->buf, g, out.data, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage attention");
     return SPL_SAGE_OK;
@@ -580,6 +603,7 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
     g.hkv = (int)G;
     g.frame_len = rope ? (int)sh.frame_len : 1;
     g.rope_half = half;
+    g.max_ctas = max_ctas(s);
     cudaError_t e = sp::launch_qkv_gemm((int)D, maps, (const uint16_t*)bias, rope, (uint16_t*)q, (uint16_t*)k,
                                         (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
@@ -812,7 +836,7 @@ int spl_sage_cp_quantize_kv(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor k, spl
 }
 
 int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
-                       int64_t k_begin, int64_t k_len, int causal, float* acc, float* lse) {
+                       int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse) {
     if (!s || !ws || !kv || !acc || !lse) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend: NULL argument");
     if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
     if (kv->head_dim != ws->head_dim || kv->tk_pad != ws->tk_pad || kv->batch != ws->shape.batch ||
@@ -824,6 +848,9 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
     if (k_begin < 0 || k_len <= 0 || k_begin % BLK || k_begin + k_len > ws->tk)
         return fail(SPL_SAGE_ERR_INVALID, "key segment [%lld, +%lld) must start on a 128-key block within %lld keys",
                     (long long)k_begin, (long long)k_len, (long long)ws->tk);
+    if (flags & ~(SPL_SAGE_CP_CAUSAL | SPL_SAGE_CP_FIRST))
+        return fail(SPL_SAGE_ERR_INVALID, "unknown segment flags 0x%x", flags);
+    const bool causal = (flags & SPL_SAGE_CP_CAUSAL) != 0;
     if (causal && k_len < q_len)
         return fail(SPL_SAGE_ERR_INVALID, "a causal segment needs at least as many keys as queries");
     if (q_len / QTILE > 65535) return fail(SPL_SAGE_ERR_INVALID, "too many query tiles");
@@ -838,6 +865,8 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
     g.tk = (int)k_len;
     g.tk_pad = (int)kv->tk_pad;
     g.causal = causal ? 1 : 0;
+    g.cp_first = (flags & SPL_SAGE_CP_FIRST) ? 1 : 0;
+    g.max_ctas = max_ctas(s);
     g.merge = 1;
     sp::AttnMaps maps;
     maps.q = ws->maps.q;

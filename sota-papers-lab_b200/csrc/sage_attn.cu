@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float inv = 1.0f / lt;
             const float lse_new = m + log2f(lt) - LOG2_448;
             float* lrow = lse + (long long)bh_q * g.tokens + qrow_ws;
-            const float lse_old = *lrow;
+            const float lse_old = g.cp_first ? __int_as_float(0xff800000) : *lrow;
             const float mx = fmaxf(lse_old, lse_new);
             const float w_old = lse_old == __int_as_float(0xff800000) ? 0.f : exp2f(lse_old - mx);
             const float w_new = exp2f(lse_new - mx);
@@ -554,7 +554,8 @@ static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom
     }
     static int sms[32] = {0};  // SMs per device ordinal
     if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)g.batch * g.heads * q_tiles;
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
     kern<<<grid, NTHREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,

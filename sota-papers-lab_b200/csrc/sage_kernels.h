@@ -25,7 +25,11 @@ struct Geom {
     // Segment attention (context parallelism): the query tiles start at
     // tile q_tile0 of the workspace's Q, the keys at key k_key0 of the K/V
     // buffer; tk is then the segment's key count.  Both 0 otherwise.
-    int q_tile0, k_key0;
+    // cp_first: the segment is the first of its query rows (acc and lse are
+    // written, not merged into).
+    int q_tile0, k_key0, cp_first;
+    // Persistent kernels launch at most this many CTAs (0: one per SM).
+    int max_ctas;
 };
 
 // Device buffers of one workspace.  Layouts (b = batch, h = q head,
@@ -65,6 +69,7 @@ struct AttnMaps {
 struct QkvGeom {
     int m, n, k, tokens;
     int hq, hkv, frame_len, rope_half;
+    int max_ctas;  // persistent CTAs at most (0: one per SM)
 };
 
 struct QkvMaps {

@@ -13,10 +13,17 @@ work).  Its Q, K and V are those 2C tokens, chunk r first.
    attends its two query chunks to that rank's two key chunks (a pair of
    chunks is skipped when the key chunk lies after the query chunk, causal
    when they are the same chunk, full otherwise) and merges the result into
-   an fp32 accumulator by log-sum-exp.  Meanwhile the K/V it holds travels
-   to rank r + 1 and the next arrives from rank r - 1 (NCCL send/recv, on
-   NCCL's own stream, double-buffered): the transfer of ~2 * C * Hkv * D
-   bytes overlaps the attention of the step.
+   an fp32 accumulator by log-sum-exp.  The pairs of a step always form one
+   contiguous segment of queries and keys (ring_segments), so a step is one
+   launch: step 0 is causal attention over the rank's own 2C tokens (in
+   local order, chunk r then chunk 2P-1-r, the causal mask is exactly the
+   global one) and writes the accumulator; a later step attends either both
+   query chunks to the sender's first key chunk (sender before r) or the
+   second query chunk to both key chunks (sender after r), unmasked.
+   Meanwhile the K/V it holds travels to rank r + 1 and the next arrives
+   from rank r - 1 (NCCL send/recv, on NCCL's own stream, double-buffered):
+   the transfer of ~2 * C * Hkv * D bytes overlaps the attention of the
+   step, on SMs the attention leaves free for it (reserve_sms).
 3. The accumulator is converted to bf16.
 
 With P = 1 this is one GPU attending the whole sequence in two chunks.
@@ -55,6 +62,42 @@ def ring_schedule(rank: int, world: int) -> List[Tuple[int, List[Pair]]]:
                 pairs.append(Pair(qi, ki, ck == cq))
         steps.append((src, pairs))
     return steps
+
+
+@dataclass(frozen=True)
+class Segment:
+    q_chunk: int   # first query chunk (local, 0 or 1)
+    q_chunks: int  # query chunks (1 or 2)
+    k_chunk: int   # first key chunk of the source rank (0 or 1)
+    k_chunks: int  # key chunks (1 or 2)
+    causal: bool
+
+
+def ring_segments(rank: int, world: int) -> List[Tuple[int, Segment]]:
+    """ring_schedule with each step's chunk pairs as one contiguous segment
+    (one attention launch per step)."""
+    steps = []
+    for s, (src, pairs) in enumerate(ring_schedule(rank, world)):
+        if s == 0:
+            seg = Segment(0, 2, 0, 2, True)
+        elif src < rank:
+            seg = Segment(0, 2, 0, 1, False)
+        else:
+            seg = Segment(1, 1, 0, 2, False)
+        steps.append((src, seg))
+    return steps
+
+
+def segment_pairs(seg: Segment) -> List[Pair]:
+    """The chunk pairs a segment covers (for a causal segment over both
+    chunks: the pairs its local causal mask leaves visible)."""
+    out = []
+    for qi in range(seg.q_chunk, seg.q_chunk + seg.q_chunks):
+        for ki in range(seg.k_chunk, seg.k_chunk + seg.k_chunks):
+            if seg.causal and ki > qi:
+                continue
+            out.append(Pair(qi, ki, seg.causal and ki == qi))
+    return out
 
 
 def shard_zigzag(x, rank: int, world: int, dim: int = 1):
@@ -118,13 +161,17 @@ def combine_stats(raw, world: int, group=None):
     return raw
 
 
+# SMs the attention leaves to NCCL's send/recv kernels during a ring step
+RESERVED_SMS = 8
+
+
 class RingAttention:
     """Ring attention of one rank.  Holds the workspace (this rank's tokens),
     two K/V buffers (the one being attended, the one being received) and the
     fp32 accumulator; reuse it for every call of the same shape."""
 
     def __init__(self, eng, batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int, world: int,
-                 head_dim: int):
+                 head_dim: int, reserved_sms: int | None = None):
         import torch
         sage = importlib.import_module("sota-papers-lab_b200")
         if local_tokens % 256:
@@ -133,6 +180,8 @@ class RingAttention:
         self.rank, self.world = rank, world
         self.B, self.H, self.G, self.T, self.D = batch, heads, kv_heads, local_tokens, head_dim
         self.C = local_tokens // 2
+        # SMs left free during the ring steps (none without a transfer)
+        self.reserved_sms = (RESERVED_SMS if world > 1 else 0) if reserved_sms is None else reserved_sms
         self.ws = eng.workspace(sage.Shape(batch, heads, local_tokens, kv_heads, False))
         self.kv = [sage.KvBuffer(eng, self.ws), sage.KvBuffer(eng, self.ws)]
         self.raw = torch.empty(batch * kv_heads, 4, head_dim, dtype=torch.float32, device="cuda")
@@ -152,22 +201,28 @@ class RingAttention:
         else:
             combine_stats(self.raw, P, group)
         self.eng.cp_quantize_kv(self.ws, k, v, self.raw, self.T * P, self.kv[0], opts)
-        self.acc.zero_()
-        self.lse.fill_(float("-inf"))
         if exchange is None and P > 1:
             exchange = nccl_exchange(group)
         cur = 0
-        for s, (src, pairs) in enumerate(ring_schedule(r, P)):
-            wait = None
-            if s + 1 < P:
-                wait = exchange(self.kv[cur].tensors(), self.kv[1 - cur].tensors())
-            for pr in pairs:
-                self.eng.cp_attend(self.ws, self.kv[cur], pr.q_local * self.C, self.C, pr.k_local * self.C, self.C,
-                                   pr.causal, self.acc, self.lse)
-            if wait is not None:
-                wait()
-                cur = 1 - cur
+        keep = self.eng.reserved_sms
+        self.eng.reserve_sms(self.reserved_sms)
+        try:
+            for s, (src, seg) in enumerate(ring_segments(r, P)):
+                wait = None
+                if s + 1 < P:
+                    wait = exchange(self.kv[cur].tensors(), self.kv[1 - cur].tensors())
+                self.attend_segment(self.kv[cur], seg, first=s == 0)
+                if wait is not None:
+                    wait()
+                    cur = 1 - cur
+        finally:
+            self.eng.reserve_sms(keep)
         self.eng.cp_finish(self.ws, self.acc, out)
+
+    def attend_segment(self, kv, seg: Segment, first: bool):
+        C = self.C
+        self.eng.cp_attend(self.ws, kv, seg.q_chunk * C, seg.q_chunks * C, seg.k_chunk * C, seg.k_chunks * C,
+                           seg.causal, self.acc, self.lse, first=first)
 
     def close(self):
         for kv in self.kv:
@@ -188,12 +243,7 @@ def emulate_ring(rings: Sequence[RingAttention], qs, ks, vs, outs, opts=None):
     for i, rg in enumerate(rings):
         rg.raw.copy_(comb)
         rg.eng.cp_quantize_kv(rg.ws, ks[i], vs[i], rg.raw, rg.T * P, rg.kv[0], opts)
-        rg.acc.zero_()
-        rg.lse.fill_(float("-inf"))
     for i, rg in enumerate(rings):
-        for s, (src, pairs) in enumerate(ring_schedule(i, P)):
-            kv = rings[src].kv[0]
-            for pr in pairs:
-                rg.eng.cp_attend(rg.ws, kv, pr.q_local * rg.C, rg.C, pr.k_local * rg.C, rg.C, pr.causal, rg.acc,
-                                 rg.lse)
+        for s, (src, seg) in enumerate(ring_segments(i, P)):
+            rg.attend_segment(rings[src].kv[0], seg, first=s == 0)
         rg.eng.cp_finish(rg.ws, rg.acc, outs[i])

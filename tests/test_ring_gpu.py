@@ -85,6 +85,67 @@ def test_ring_attention_single_rank_path():
     rg.close()
 
 
+def test_pairwise_segments_equal_one_launch_per_step():
+    """The ring's one launch per step (contiguous chunk pairs together, the
+    first step writing the accumulator) against one launch per chunk pair
+    merged into a zeroed accumulator: the same attention within the gate."""
+    world, d, heads, kv_heads, tokens = 4, 128, 4, 2, 4096
+    c = st.Case(batch=1, heads=heads, kv_heads=kv_heads, tokens=tokens, d=d, causal=True, packed=False, seed=31)
+    x, q, k, v = _inputs(c)
+    eng = st.engine(c)
+    T = tokens // world
+    rings = [ring.RingAttention(eng, 1, heads, kv_heads, T, r, world, d) for r in range(world)]
+    sq, skv = sage.Strides.bthd(T, heads, d), sage.Strides.bthd(T, kv_heads, d)
+    shards = [(ring.shard_zigzag(q, r, world), ring.shard_zigzag(k, r, world), ring.shard_zigzag(v, r, world))
+              for r in range(world)]
+    outs = [torch.zeros(1, T, heads, d, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    ring.emulate_ring(rings, [sage.Tensor(a, sq) for a, _, _ in shards], [sage.Tensor(b, skv) for _, b, _ in shards],
+                      [sage.Tensor(cc, skv) for _, _, cc in shards], [sage.Tensor(o, sq) for o in outs])
+    torch.cuda.synchronize()
+    for i, rg in enumerate(rings):
+        acc1, lse1 = rg.acc.clone(), rg.lse.clone()
+        rg.acc.zero_()
+        rg.lse.fill_(float("-inf"))
+        for src, pairs in ring.ring_schedule(i, world):
+            for pr in pairs:
+                eng.cp_attend(rg.ws, rings[src].kv[0], pr.q_local * rg.C, rg.C, pr.k_local * rg.C, rg.C, pr.causal,
+                              rg.acc, rg.lse)
+        torch.cuda.synchronize()
+        assert eng.status(rg.ws) == 0
+        # P is rounded to E4M3 against the running row maximum, which a
+        # longer key segment reaches at other blocks: attention tolerance for
+        # the output; the denominators are fp32 sums of the unrounded P
+        e = O.errors(rg.acc.cpu().numpy().astype(np.float64), acc1.cpu().numpy().astype(np.float64))
+        assert st.attention_gate(e), e
+        assert torch.allclose(rg.lse, lse1, rtol=1e-5, atol=1e-3), (rg.lse - lse1).abs().max()
+    for rg in rings:
+        rg.close()
+
+
+def test_reserved_sms_give_the_same_result():
+    """Attention on all but n SMs (fewer persistent CTAs, more tiles each)
+    is bit-identical to attention on all SMs."""
+    c = st.Case(batch=2, heads=8, kv_heads=2, tokens=2048, d=128, causal=True, packed=False, seed=5)
+    x, q, k, v = _inputs(c)
+    eng = st.engine(c)
+    ws = eng.workspace(sage.Shape(2, 8, 2048, 2, True))
+    sq, skv = sage.Strides.bthd(2048, 8, 128), sage.Strides.bthd(2048, 2, 128)
+    tq, tk, tv = sage.Tensor(q.contiguous(), sq), sage.Tensor(k.contiguous(), skv), sage.Tensor(v.contiguous(), skv)
+    outs = []
+    for n in (0, 8, 100):
+        eng.reserve_sms(n)
+        o = torch.zeros(2, 2048, 8, 128, dtype=torch.bfloat16, device="cuda")
+        eng.forward(ws, tq, tk, tv, sage.Tensor(o, sq))
+        outs.append(o)
+    eng.reserve_sms(0)
+    torch.cuda.synchronize()
+    assert eng.status(ws) == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    with pytest.raises(sage.SageError):
+        eng.reserve_sms(-1)
+    ws.close()
+
+
 def test_segment_arguments_are_checked():
     c = st.Case(batch=1, heads=2, kv_heads=2, tokens=512, d=128, causal=True, packed=False)
     eng = st.engine(c)

@@ -32,6 +32,22 @@ def test_schedule_covers_every_visible_chunk_pair_once(world):
         assert ring.ring_schedule(rank, world)[0][0] == rank
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_segments_cover_the_scheduled_pairs(world):
+    """One launch per step: each step's segment covers exactly that step's
+    chunk pairs, with the same masks."""
+    for rank in range(world):
+        segs = ring.ring_segments(rank, world)
+        sched = ring.ring_schedule(rank, world)
+        assert len(segs) == len(sched) == world
+        for (src, seg), (src2, pairs) in zip(segs, sched):
+            assert src == src2
+            assert sorted(ring.segment_pairs(seg), key=str) == sorted(pairs, key=str)
+            assert seg.q_chunk + seg.q_chunks <= 2 and seg.k_chunk + seg.k_chunks <= 2
+        # the first step covers every local query row (it writes the accumulator)
+        assert segs[0][1].q_chunk == 0 and segs[0][1].q_chunks == 2
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_zigzag_balances_causal_work(world):
     # key chunks seen per rank, a diagonal chunk counting one half
