@@ -349,7 +349,9 @@ def run_ring(args, rank, world, local_rank):
         "dtype": "int8/e4m3 (fp32 accumulate; bf16 in/out)", "data": "synthetic (seeded torch.randn on device)",
         "config": {"workload": w["desc"], "global_batch": B,
                    "seq_len": N, "q_heads": H, "kv_heads": G, "head_dim": D, "causal": True,
-                   "parallelism": f"cp{world}: zig-zag chunks, K/V ring over NCCL send/recv",
+                   "parallelism": f"cp{world}: zig-zag chunks, one attention launch per ring step, K/V ring over "
+                                  f"NCCL send/recv in a group capped at {ring.NCCL_CTAS} CTA(s), "
+                                  f"{rg.reserved_sms} SM(s) left free for it",
                    "l2": "inputs exceed the 126 MB L2; no flush"},
         "roofline": {"bound": "tensor", "kernel": "whole ring step per GPU (quantiser, segment attention, merge)",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",

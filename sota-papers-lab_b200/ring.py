@@ -23,7 +23,11 @@ work).  Its Q, K and V are those 2C tokens, chunk r first.
    Meanwhile the K/V it holds travels to rank r + 1 and the next arrives
    from rank r - 1 (NCCL send/recv, on NCCL's own stream, double-buffered):
    the transfer of ~2 * C * Hkv * D bytes overlaps the attention of the
-   step, on SMs the attention leaves free for it (reserve_sms).
+   step.  The attention kernels are persistent (one CTA per SM for the
+   whole launch), so NCCL's kernel would find no free SM until the step
+   ends; the ring therefore runs NCCL in its own group capped at
+   NCCL_CTAS CTAs and has the attention leave that many SMs free
+   (reserve_sms).
 3. The accumulator is converted to bf16.
 
 With P = 1 this is one GPU attending the whole sequence in two chunks.
@@ -147,6 +151,26 @@ def nccl_exchange(group=None):
     return exchange
 
 
+# NCCL kernels of the ring's process group use at most this many CTAs, and
+# the attention leaves as many SMs free during the ring steps (measured on
+# 8 B200s, C5: 1 CTA + 1 SM 18.0 ms per step; 2 + 2 18.6; 8 + 8 19.3;
+# NCCL's default with none free 20.5)
+NCCL_CTAS = 1
+RESERVED_SMS = NCCL_CTAS
+
+
+def nccl_ring_group(ranks=None):
+    """A new NCCL process group over `ranks` (default all) whose kernels use
+    at most NCCL_CTAS CTAs; every rank must call it (a collective)."""
+    import torch.distributed as dist
+    o = dist.ProcessGroupNCCL.Options()
+    o.config.max_ctas = NCCL_CTAS
+    o.config.min_ctas = 1
+    if ranks is None:
+        ranks = list(range(dist.get_world_size()))
+    return dist.new_group(ranks, pg_options=o)
+
+
 def combine_stats(raw, world: int, group=None):
     """raw [b*g, 4, D] summed (entries 0-1) and maxed (2-3) over the ranks."""
     if world == 1:
@@ -161,17 +185,20 @@ def combine_stats(raw, world: int, group=None):
     return raw
 
 
-# SMs the attention leaves to NCCL's send/recv kernels during a ring step
-RESERVED_SMS = 8
-
-
 class RingAttention:
     """Ring attention of one rank.  Holds the workspace (this rank's tokens),
     two K/V buffers (the one being attended, the one being received) and the
-    fp32 accumulator; reuse it for every call of the same shape."""
+    fp32 accumulator; reuse it for every call of the same shape.
+
+    group: the process group of the ring's NCCL calls; by default (world > 1
+    with torch.distributed initialised) the ring makes its own with
+    nccl_ring_group(), so construct the ring on every rank together.
+    reserved_sms: SMs the attention leaves free during the steps (default
+    RESERVED_SMS when there is a transfer, else 0); it must cover the CTAs
+    of the group's NCCL kernels."""
 
     def __init__(self, eng, batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int, world: int,
-                 head_dim: int, reserved_sms: int | None = None):
+                 head_dim: int, reserved_sms: int | None = None, group=None):
         import torch
         sage = importlib.import_module("sota-papers-lab_b200")
         if local_tokens % 256:
@@ -182,6 +209,11 @@ class RingAttention:
         self.C = local_tokens // 2
         # SMs left free during the ring steps (none without a transfer)
         self.reserved_sms = (RESERVED_SMS if world > 1 else 0) if reserved_sms is None else reserved_sms
+        self.group, self._own_group = group, False
+        if group is None and world > 1:
+            import torch.distributed as dist
+            if dist.is_available() and dist.is_initialized() and dist.get_backend() == "nccl":
+                self.group, self._own_group = nccl_ring_group(), True
         self.ws = eng.workspace(sage.Shape(batch, heads, local_tokens, kv_heads, False))
         self.kv = [sage.KvBuffer(eng, self.ws), sage.KvBuffer(eng, self.ws)]
         self.raw = torch.empty(batch * kv_heads, 4, head_dim, dtype=torch.float32, device="cuda")
@@ -191,10 +223,11 @@ class RingAttention:
     def forward(self, q, k, v, out, *, exchange: Callable | None = None, group=None, opts=None,
                 combine: Callable | None = None):
         """q, k, v, out: this rank's tokens (sage.Tensor views); exchange: the
-        K/V transfer (default NCCL P2P over `group`); combine: the statistics
-        reduction (default all-reduce over `group`)."""
-        sage = self.sage
+        K/V transfer (default NCCL P2P over `group`, default the ring's own);
+        combine: the statistics reduction (default all-reduce over `group`)."""
         P, r = self.world, self.rank
+        if group is None:
+            group = self.group
         self.eng.cp_prepare(self.ws, q, k, v, self.raw, opts)
         if combine is not None:
             combine(self.raw)
@@ -228,6 +261,10 @@ class RingAttention:
         for kv in self.kv:
             kv.close()
         self.ws.close()
+        if self._own_group:
+            import torch.distributed as dist
+            dist.destroy_process_group(self.group)
+            self._own_group, self.group = False, None
 
 
 def emulate_ring(rings: Sequence[RingAttention], qs, ks, vs, outs, opts=None):
