@@ -481,6 +481,7 @@ def run_ours(args, rank, world, local_rank):
     d2h = out.numel() * out.element_size()
 
     qkv = qkv_gemm_time(eng, w, dev, stream) if w.get("qkv") else None
+    qkv8 = qkv_fp8_time(eng, w, dev, stream) if w.get("qkv") else None
 
     if rank != 0:
         return None
@@ -532,6 +533,12 @@ def run_ours(args, rank, world, local_rank):
     }
     if qkv is not None:
         line["qkv_gemm"] = qkv
+    if qkv8 is not None:
+        qkv8["peak"] = round(f8_peak, 1)
+        qkv8["frac"] = round(qkv8["achieved"] / f8_peak, 4)
+        qkv8["peak_source"] = "FP8 E4M3 tcgen05 rate measured in this run by the probe"
+        qkv8["ln_frac_of_hbm"] = round(qkv8["ln_gbs"] / peaks["hbm_gbs"], 4)
+        line["qkv_fp8"] = qkv8
     return line
 
 
@@ -569,6 +576,57 @@ def qkv_gemm_time(eng, w, dev, stream, iters=10):
     return {"kernel": "sp_qkv_gemm (tcgen05 kind::f16, bias + RoPE + bf16 epilogue)",
             "shape": f"[{B * N}x{hidden}] x [{n_out}x{hidden}]^T", "ms": round(ms, 4),
             "achieved": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "bound": "tensor"}
+
+
+def qkv_fp8_time(eng, w, dev, stream, iters=10):
+    """The FP8 QKV side of the reference's FP8 block (row f1): LN1 of the
+    bf16 activations to per-token E4M3 (spl_sage_layer_norm_fp8) and the FP8
+    QKV GEMM with token / channel scales, RoPE and bf16 out fused
+    (spl_sage_qkv_gemm_fp8), at the workload's shape; weights E4M3 with one
+    scale per output channel."""
+    import torch
+    B, H, G, N, D = w["batch"], w["heads"], w["kv_heads"], w["tokens"], w["d"]
+    hidden = w["qkv"]["hidden"]
+    n_out = (H + 2 * G) * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(98)
+    x = torch.randn(B * N, hidden, generator=g, device=dev).to(torch.bfloat16)
+    gamma = 1.0 + 0.1 * torch.randn(hidden, generator=g, device=dev)
+    beta = 0.1 * torch.randn(hidden, generator=g, device=dev)
+    wt = torch.randn(n_out, hidden, generator=g, device=dev) * 0.02
+    w_scale = (wt.abs().amax(dim=1) / 448.0).clamp_min(1e-12)
+    w8 = (wt / w_scale[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    del wt
+    sage = importlib.import_module("sota-papers-lab_b200")
+    rope = torch.from_numpy(sage.rope_table_1d(w["qkv"]["rope_theta"], D, N)).to(dev)
+    x8 = torch.empty(B * N, hidden, dtype=torch.uint8, device=dev)
+    xs = torch.empty(B * N, dtype=torch.float32, device=dev)
+    q = torch.empty(B, N, H, D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(B, N, G, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    ln = lambda: eng.layer_norm_fp8(x, gamma, beta, 1e-6, x8, xs)
+    gemm = lambda: eng.qkv_gemm_fp8(x8, xs, w8, w_scale, None, rope, q, k, v, batch=B, tokens=N, heads=H,
+                                    kv_heads=G, rope_half=D // 2, frame_len=N)
+    times = {}
+    for name, call in (("ln", ln), ("gemm", gemm)):
+        for _ in range(3):
+            call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(iters):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times[name] = e0.elapsed_time(e1) / iters
+    assert eng.engine_status() == 0
+    flops = 2.0 * B * N * hidden * n_out
+    ln_bytes = B * N * hidden * (2 + 1) + B * N * 4  # bf16 in, E4M3 out, scales
+    return {"kernels": "sp_ln_fp8 (LN1 -> per-token E4M3) + sp_qkv_gemm<FP8> (tcgen05 kind::f8f6f4, "
+                       "token/channel scales + RoPE + bf16 epilogue)",
+            "shape": f"[{B * N}x{hidden}] x [{n_out}x{hidden}]^T", "ln_ms": round(times["ln"], 4),
+            "ln_gbs": round(ln_bytes / (times["ln"] * 1e-3) / 1e9, 1), "gemm_ms": round(times["gemm"], 4),
+            "achieved": round(flops / (times["gemm"] * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "bound": "tensor"}
 
 
 # ---------------------------------------------------------------- CPU arms

@@ -199,6 +199,29 @@ typedef struct {
 int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const void* bias,
                       const float* rope, void* q, void* k, void* v);
 
+/* The FP8 QKV side (the reference's FP8 block,
+ * apps/image-to-3d/src/vggt/trunk/block.rs:353-395): Gemm::linear_fp8 with
+ * deferred weight scales (gemm.rs:294-337, y = bf16(x8 w8^T)) followed by
+ * QkvPrologue::run with per-token and per-channel scales (qkv.cu:55-73:
+ * y * x_scale[token] * w_scale[channel] + bias), RoPE and head-major bf16,
+ * in one tcgen05 kind::f8f6f4 GEMM.  x8 E4M3 [batch*tokens][hidden] with
+ * x_scale f32 [batch*tokens] (spl_sage_layer_norm_fp8 writes both); w8 E4M3
+ * [(heads + 2*kv_heads)*head_dim][hidden] with w_scale f32 per output
+ * channel; hidden a multiple of 16; the rest as spl_sage_qkv_gemm. */
+int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x8, const float* x_scale,
+                          const void* w8, const float* w_scale, const void* bias, const float* rope, void* q, void* k,
+                          void* v);
+
+/* Norm::layer_norm with Quant::PerToken (platform/spl-nn/src/norm.rs:171-274,
+ * cuda/norm.cu:37-137), the LN1 that feeds the FP8 QKV GEMM: x f32 (x_f32 =
+ * 1) or bf16 [rows][c], gamma and beta f32 [c]; writes q8 E4M3 [rows][c],
+ * scales f32 [rows] (amax / 448, 1 for an all-zero row) and, when out is
+ * not NULL, the normalised rows as bf16.  Same bytes as the reference's
+ * kernel.  c = 256, 512, 768, 1024, 1536, 2048 (the reference's widths),
+ * 3072 or 4096; buffers 16-byte aligned. */
+int spl_sage_layer_norm_fp8(spl_sage* s, const void* x, int x_f32, int64_t rows, int64_t c, const float* gamma,
+                            const float* beta, float eps, void* out, void* q8, float* scales);
+
 /* spl_sage_qkv_gemm into q, k, v (bf16 scratch the caller owns), then
  * spl_sage_prepare of ws from them: the block's whole QKV path up to the
  * quantised tensors the attention reads. */

@@ -56,6 +56,7 @@ def lib():
         L.or_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         L.or_f32_to_e4m3.restype = ctypes.c_uint8
         L.or_f32_to_e4m3.argtypes = [ctypes.c_float]
+        L.or_f32_to_e4m3_n.argtypes = [P, P, ctypes.c_int64]
         L.or_vpos.restype = ctypes.c_int
         L.or_vpos.argtypes = [ctypes.c_int]
         L.or_rng_next.restype = ctypes.c_uint64
@@ -80,6 +81,8 @@ def lib():
         L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom), ctypes.c_int, ctypes.c_int, P]
         L.or_layer_norm.argtypes = [P, P, P, ctypes.c_int, ctypes.c_float]
         L.or_qkv_reference.argtypes = [P, P, P, P] + [ctypes.c_int] * 10 + [P, P, P]
+        L.or_qkv_reference_fp8.argtypes = [P] * 6 + [ctypes.c_int] * 10 + [P, P, P]
+        L.or_layer_norm_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_float, P, P, P]
         L.or_errors.argtypes = [P, P, ctypes.c_int64, P]
         L.or_flops.restype = ctypes.c_double
         L.or_flops.argtypes = [ctypes.c_int] * 5
@@ -129,6 +132,14 @@ def e4m3_to_f32(b):
 
 def f32_to_e4m3(x: float) -> int:
     return int(lib().or_f32_to_e4m3(float(x)))
+
+
+def f32_to_e4m3_array(x) -> np.ndarray:
+    """or_f32_to_e4m3 over an array (same shape, uint8)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(x.shape, np.uint8)
+    lib().or_f32_to_e4m3_n(_p(x), _p(out), x.size)
+    return out
 
 
 def vpos(k: int) -> int:
@@ -298,6 +309,37 @@ def qkv_reference(x, w, bias, rope, *, tokens, hq, hkv, d, rope_half=0, frame_le
     return q, kk, v
 
 
+def qkv_reference_fp8(x8, x_scale, w8, w_scale, bias, rope, *, tokens, hq, hkv, d, rope_half=0, frame_len=1,
+                      nthreads=None):
+    """f64 FP8 QKV GEMM + prologue: x8 E4M3 bytes [m][k] with x_scale f32
+    [m], w8 [n][k] with w_scale f32 [n], bias bf16 bits [n] or None.  Returns
+    f32 q [m][hq][d], k [m][hkv][d], v [m][hkv][d]."""
+    m, k = x8.shape
+    n = w8.shape[0]
+    q = np.zeros((m, hq, d), np.float32)
+    kk = np.zeros((m, hkv, d), np.float32)
+    v = np.zeros((m, hkv, d), np.float32)
+    c = np.ascontiguousarray
+    lib().or_qkv_reference_fp8(_p(c(x8, np.uint8)), _p(c(x_scale, np.float32)), _p(c(w8, np.uint8)),
+                               _p(c(w_scale, np.float32)), _p(None if bias is None else c(bias)),
+                               _p(None if rope is None else c(rope, np.float32)), rope_half, frame_len, m, n, k, tokens,
+                               hq, hkv, d, nthreads or os.cpu_count() or 1, _p(q), _p(kk), _p(v))
+    return q, kk, v
+
+
+def layer_norm_fp8(x, gamma, beta, eps, with_out=False):
+    """norm.cu:37-137 on the CPU: x f32 or bf16 bits (uint16) [rows][c].
+    Returns (q8 uint8 [rows][c], scales f32 [rows], out bf16 bits or None)."""
+    x = np.ascontiguousarray(x)
+    rows, c = x.shape
+    q8 = np.zeros((rows, c), np.uint8)
+    sc = np.zeros(rows, np.float32)
+    out = np.zeros((rows, c), np.uint16) if with_out else None
+    lib().or_layer_norm_fp8(_p(x), int(x.dtype == np.float32), rows, c, _p(np.ascontiguousarray(gamma, np.float32)),
+                            _p(np.ascontiguousarray(beta, np.float32)), float(eps), _p(out), _p(q8), _p(sc))
+    return q8, sc, out
+
+
 def errors(ours, ref) -> dict:
     a = np.ascontiguousarray(ours, np.float32).ravel()
     r = np.ascontiguousarray(ref, np.float32).ravel()
@@ -338,3 +380,26 @@ def ref_lib(d: int) -> ctypes.CDLL:
 def ref_dims(g: Geom) -> np.ndarray:
     return np.array([g.batch, g.heads, g.tokens, g.merge, g.frames, g.special, g.grid_h, g.grid_w,
                      g.dense_frames, g.flags], np.int32)
+
+
+_norm_ref = None
+
+
+def norm_ref_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libnorm_ref.so"))
+
+
+def ref_layer_norm_fp8(x, gamma, beta, eps, out, q8, scales, stream=0) -> int:
+    """The reference's own ln_{f32,bf16}_c<n> kernels (norm.cu:37-144), on
+    device tensors (x f32 or bf16 [rows][c]); returns a cudaError_t."""
+    global _norm_ref
+    if _norm_ref is None:
+        L = ctypes.CDLL(os.path.join(HERE, "_ref", "libnorm_ref.so"))
+        P = ctypes.c_void_p
+        L.ref_layer_norm_fp8.restype = ctypes.c_int
+        L.ref_layer_norm_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_float, P, P, P, P]
+        _norm_ref = L
+    import torch
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+    return _norm_ref.ref_layer_norm_fp8(p(x), int(x.dtype == torch.float32), x.shape[0], x.shape[-1], p(gamma),
+                                        p(beta), float(eps), p(out), p(q8), p(scales), ctypes.c_void_p(stream))

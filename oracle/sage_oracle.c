@@ -73,6 +73,10 @@ uint8_t or_f32_to_e4m3(float x) {
     return sign | (uint8_t)((e + 7) << 3) | (uint8_t)(k - 8);
 }
 
+void or_f32_to_e4m3_n(const float* x, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = or_f32_to_e4m3(x[i]);
+}
+
 /* reference.rs:74-76 / sage_common.cu:155 */
 int or_vpos(int k) { return ((k >> 1) & 3) * 4 + ((k >> 3) << 1) + (k & 1); }
 
@@ -730,6 +734,9 @@ typedef struct {
     float *q, *kk, *v;
     int64_t next;
     pthread_mutex_t mu;
+    /* FP8 variant (x8 != NULL): E4M3 operands and their scales */
+    const uint8_t *x8, *w8;
+    const float *x_scale, *w_scale;
 } qkv_job;
 
 static void* qkv_worker(void* arg) {
@@ -741,12 +748,27 @@ static void* qkv_worker(void* arg) {
         int64_t r = J->next++;
         pthread_mutex_unlock(&J->mu);
         if (r >= J->m) break;
-        for (int i = 0; i < J->k; i++) xr[i] = (double)or_bf16_to_f32(J->x[r * J->k + i]);
-        for (int c = 0; c < J->n; c++) {
-            const uint16_t* wc = J->w + (int64_t)c * J->k;
-            double acc = 0.0;
-            for (int i = 0; i < J->k; i++) acc += xr[i] * (double)or_bf16_to_f32(wc[i]);
-            y[c] = acc + (J->bias ? (double)or_bf16_to_f32(J->bias[c]) : 0.0);
+        if (J->x8) {
+            /* gemm.rs:294-337 (deferred scales) then qkv.rs:306-330: the
+             * products of the E4M3 values, times the token and channel
+             * scales, plus the bias, in f64 */
+            for (int i = 0; i < J->k; i++) xr[i] = (double)or_e4m3_to_f32(J->x8[r * J->k + i]);
+            for (int c = 0; c < J->n; c++) {
+                const uint8_t* wc = J->w8 + (int64_t)c * J->k;
+                double acc = 0.0;
+                for (int i = 0; i < J->k; i++) acc += xr[i] * (double)or_e4m3_to_f32(wc[i]);
+                acc *= (double)J->x_scale[r];
+                acc *= (double)J->w_scale[c];
+                y[c] = acc + (J->bias ? (double)or_bf16_to_f32(J->bias[c]) : 0.0);
+            }
+        } else {
+            for (int i = 0; i < J->k; i++) xr[i] = (double)or_bf16_to_f32(J->x[r * J->k + i]);
+            for (int c = 0; c < J->n; c++) {
+                const uint16_t* wc = J->w + (int64_t)c * J->k;
+                double acc = 0.0;
+                for (int i = 0; i < J->k; i++) acc += xr[i] * (double)or_bf16_to_f32(wc[i]);
+                y[c] = acc + (J->bias ? (double)or_bf16_to_f32(J->bias[c]) : 0.0);
+            }
         }
         const int d = J->d, tok = (int)(r % J->tokens), half = J->rope_half;
         for (int part = 0; part < 3; part++) {
@@ -775,10 +797,8 @@ static void* qkv_worker(void* arg) {
     return NULL;
 }
 
-void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias, const float* rope, int rope_half,
-                      int frame_len, int m, int n, int k, int tokens, int hq, int hkv, int d, int nthreads, float* q,
-                      float* kk, float* v) {
-    qkv_job J = {x, w, bias, rope, rope_half, frame_len, m, n, k, tokens, hq, hkv, d, q, kk, v, 0};
+static void qkv_run(qkv_job* jp, int nthreads) {
+    qkv_job J = *jp;
     pthread_mutex_init(&J.mu, NULL);
     if (nthreads < 1) nthreads = 1;
     pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * nthreads);
@@ -786,4 +806,86 @@ void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias
     for (int i = 0; i < nthreads; i++) pthread_join(th[i], NULL);
     free(th);
     pthread_mutex_destroy(&J.mu);
+}
+
+void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias, const float* rope, int rope_half,
+                      int frame_len, int m, int n, int k, int tokens, int hq, int hkv, int d, int nthreads, float* q,
+                      float* kk, float* v) {
+    qkv_job J;
+    memset(&J, 0, sizeof J);
+    J.x = x; J.w = w; J.bias = bias; J.rope = rope; J.rope_half = rope_half; J.frame_len = frame_len;
+    J.m = m; J.n = n; J.k = k; J.tokens = tokens; J.hq = hq; J.hkv = hkv; J.d = d;
+    J.q = q; J.kk = kk; J.v = v;
+    qkv_run(&J, nthreads);
+}
+
+void or_qkv_reference_fp8(const uint8_t* x8, const float* x_scale, const uint8_t* w8, const float* w_scale,
+                          const uint16_t* bias, const float* rope, int rope_half, int frame_len, int m, int n, int k,
+                          int tokens, int hq, int hkv, int d, int nthreads, float* q, float* kk, float* v) {
+    qkv_job J;
+    memset(&J, 0, sizeof J);
+    J.x8 = x8; J.x_scale = x_scale; J.w8 = w8; J.w_scale = w_scale;
+    J.bias = bias; J.rope = rope; J.rope_half = rope_half; J.frame_len = frame_len;
+    J.m = m; J.n = n; J.k = k; J.tokens = tokens; J.hq = hq; J.hkv = hkv; J.d = d;
+    J.q = q; J.kk = kk; J.v = v;
+    qkv_run(&J, nthreads);
+}
+
+/* ------------------------------------------------------------------ LayerNorm -> FP8 */
+
+/* norm.cu:37-137 (Quant::PerToken, no residual branch) in f32, in the
+ * kernel's order: lane l of a warp sums its chunks l, l+32, ... (8 channels
+ * each) in order, the 32 lane sums meet in a xor butterfly (16, 8, 4, 2, 1);
+ * mean = sum * (1/C); the variance the same way with fmaf(d, d, ss); rstd =
+ * 1/sqrtf(fmaf(var_sum, 1/C, eps)) -- the kernel's rsqrtf is an
+ * approximation, so rstd, and through it y and q, may differ in the last
+ * place; y = fmaf((v - mean) * rstd, gamma, beta); scale = amax / 448 (1 for
+ * a zero row); q = e4m3(y * (448 / amax)). */
+static float lane_tree(const float* lane_vals) {
+    float v[32];
+    memcpy(v, lane_vals, sizeof v);
+    for (int o = 16; o > 0; o >>= 1) {
+        float t[32];
+        for (int l = 0; l < 32; l++) t[l] = v[l] + v[l ^ o];
+        memcpy(v, t, sizeof v);
+    }
+    return v[0];
+}
+
+void or_layer_norm_fp8(const void* x, int x_f32, int64_t rows, int c, const float* gamma, const float* beta, float eps,
+                       uint16_t* out, uint8_t* q8, float* scales) {
+    const int nch = c / 256;
+    float* v = (float*)malloc(sizeof(float) * (size_t)c);
+    for (int64_t r = 0; r < rows; r++) {
+        for (int i = 0; i < c; i++)
+            v[i] = x_f32 ? ((const float*)x)[r * c + i] : or_bf16_to_f32(((const uint16_t*)x)[r * c + i]);
+        float ls[32];
+        for (int l = 0; l < 32; l++) {
+            float s = 0.0f;
+            for (int i = 0; i < nch; i++)
+                for (int j = 0; j < 8; j++) s += v[(i * 32 + l) * 8 + j];
+            ls[l] = s;
+        }
+        const float mean = lane_tree(ls) * (1.0f / (float)c);
+        for (int l = 0; l < 32; l++) {
+            float ss = 0.0f;
+            for (int i = 0; i < nch; i++)
+                for (int j = 0; j < 8; j++) {
+                    const float d = v[(i * 32 + l) * 8 + j] - mean;
+                    ss = fmaf(d, d, ss);
+                }
+            ls[l] = ss;
+        }
+        const float rstd = 1.0f / sqrtf(fmaf(lane_tree(ls), 1.0f / (float)c, eps));
+        float amax = 0.0f;
+        for (int i = 0; i < c; i++) {
+            v[i] = fmaf((v[i] - mean) * rstd, gamma[i], beta[i]);
+            if (fabsf(v[i]) > amax) amax = fabsf(v[i]);
+            if (out) out[r * c + i] = or_f32_to_bf16(v[i]);
+        }
+        const float inv = amax > 0.0f ? 448.0f / amax : 1.0f;
+        scales[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+        for (int i = 0; i < c; i++) q8[r * c + i] = or_f32_to_e4m3(v[i] * inv);
+    }
+    free(v);
 }

@@ -62,6 +62,7 @@ float or_bf16_to_f32(uint16_t b);
 uint16_t or_f32_to_bf16(float x);
 float or_e4m3_to_f32(uint8_t b);
 uint8_t or_f32_to_e4m3(float x);
+void or_f32_to_e4m3_n(const float* x, uint8_t* out, int64_t n);
 int or_vpos(int k);
 
 /* ---- SplitMix64 (reference.rs:228-254) ---- */
@@ -138,6 +139,17 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
 void or_qkv_reference(const uint16_t* x, const uint16_t* w, const uint16_t* bias, const float* rope, int rope_half,
                       int frame_len, int m, int n, int k, int tokens, int hq, int hkv, int d, int nthreads, float* q,
                       float* kk, float* v);
+/* The FP8 QKV side (gemm.rs:294-337 with deferred scales, then qkv.rs:306-372
+ * with tok and chan): E4M3 x8 [m][k] with x_scale [m], w8 [n][k] with
+ * w_scale [n], in f64; outputs as or_qkv_reference. */
+void or_qkv_reference_fp8(const uint8_t* x8, const float* x_scale, const uint8_t* w8, const float* w_scale,
+                          const uint16_t* bias, const float* rope, int rope_half, int frame_len, int m, int n, int k,
+                          int tokens, int hq, int hkv, int d, int nthreads, float* q, float* kk, float* v);
+/* Norm::layer_norm with Quant::PerToken (norm.cu:37-137) on the CPU, f32 in
+ * the kernel's order; rstd through 1/sqrtf (the kernel's rsqrtf may differ
+ * in the last place).  x f32 (x_f32 = 1) or bf16 [rows][c], c = 256 * n. */
+void or_layer_norm_fp8(const void* x, int x_f32, int64_t rows, int c, const float* gamma, const float* beta, float eps,
+                       uint16_t* out, uint8_t* q8, float* scales);
 
 /* LayerNorm of one row in f64 (reference.rs:110-118). */
 void or_layer_norm(float* x, const float* w, const float* b, int n, float eps);

@@ -95,7 +95,7 @@ EXPORTS = [
     "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
-    "spl_sage_reserve_sms",
+    "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8",
 ]
 
 # spl_sage_cp_attend flags
@@ -133,6 +133,8 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_attn_resources.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
         L.spl_sage_tensor_peak.argtypes = [P, I, I, I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         L.spl_sage_qkv_gemm.argtypes = [P, ctypes.POINTER(_QkvShape)] + [P] * 7
+        L.spl_sage_qkv_gemm_fp8.argtypes = [P, ctypes.POINTER(_QkvShape)] + [P] * 9
+        L.spl_sage_layer_norm_fp8.argtypes = [P, P, I, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_float, P, P, P]
         L.spl_sage_qkv_gemm_quant.argtypes = [P, P, ctypes.POINTER(_QkvShape)] + [P] * 7 + [ctypes.POINTER(_Options)]
         L.spl_sage_rope_table_1d.argtypes = [ctypes.c_double, I, ctypes.c_int64, P]
         L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
@@ -415,6 +417,27 @@ class SageAttention:
         p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
         sh = _QkvShape(batch, tokens, x.shape[-1], heads, kv_heads, rope_half, frame_len)
         _check(lib().spl_sage_qkv_gemm(self._h, ctypes.byref(sh), p(x), p(w), p(bias), p(rope), p(q), p(k), p(v)))
+
+    def qkv_gemm_fp8(self, x8, x_scale, w8, w_scale, bias, rope, q, k, v, *, batch: int, tokens: int, heads: int,
+                     kv_heads: int = 0, rope_half: int = 0, frame_len: int = 0):
+        """The FP8 QKV side (spl_sage_qkv_gemm_fp8): x8 E4M3 (uint8)
+        [batch*tokens][hidden] with x_scale f32 [batch*tokens], w8 E4M3
+        [(heads+2*kv)*D][hidden] with w_scale f32 per output channel; the
+        rest as qkv_gemm."""
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        sh = _QkvShape(batch, tokens, x8.shape[-1], heads, kv_heads, rope_half, frame_len)
+        _check(lib().spl_sage_qkv_gemm_fp8(self._h, ctypes.byref(sh), p(x8), p(x_scale), p(w8), p(w_scale), p(bias),
+                                           p(rope), p(q), p(k), p(v)))
+
+    def layer_norm_fp8(self, x, gamma, beta, eps: float, q8, scales, out=None):
+        """Norm::layer_norm with per-token FP8 output (spl_sage_layer_norm_fp8):
+        x f32 or bf16 [rows][c]; writes q8 (uint8 E4M3) [rows][c], scales f32
+        [rows] and, when given, out bf16 [rows][c]."""
+        import torch
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        rows, c = x.shape[0], x.shape[-1]
+        _check(lib().spl_sage_layer_norm_fp8(self._h, p(x), int(x.dtype == torch.float32), rows, c, p(gamma), p(beta),
+                                             float(eps), p(out), p(q8), p(scales)))
 
     def qkv_gemm_quant(self, ws: Workspace, x, w, bias, rope, q, k, v, opts: Options | None = None, *,
                        rope_half: int = 0, frame_len: int = 0):

@@ -7,33 +7,47 @@
 // pair (d / 2half) * half + d % half), round to bf16 again (qkv.cu:121-133),
 // and write Q, K, V in [B][T][H][D] for the quantiser.
 //
+// FP8 variant (the reference's FP8 block, apps/image-to-3d/src/vggt/trunk/
+// block.rs:353-395: Gemm::linear_fp8 with deferred weight scales,
+// platform/spl-nn/src/gemm.rs:294-337, then QkvPrologue::run with per-token
+// and per-channel scales): x and w E4M3, tcgen05 kind::f8f6f4 (FP32
+// accumulate, twice the BF16 rate); the epilogue rounds the accumulator to
+// bf16 (the GEMM's bf16 output), multiplies by the token's activation scale
+// and the channel's weight scale and adds the bias in that order
+// (cuda/qkv.cu:55-73), then RoPE and bf16 as above.
+//
 // Tile: 128 rows x 256 output channels (two heads of 128 or four of 64), K in
-// 64-element (128-byte) blocks through a 4-stage TMA ring.  Persistent: one
+// 128-byte blocks (64 bf16 or 128 E4M3 elements) through a 4-stage TMA ring.
+// Persistent: one
 // CTA per SM works through the output tiles in turn, with two TMEM
 // accumulators (2 x 256 columns), so the epilogue of one tile overlaps the
 // MMAs of the next.  Warp 0 loads, warp 1 issues the MMAs (4 x M128 N256 K16
-// per block) and owns TMEM, warps 4-7 run the epilogue, one thread per row.
+// per block; 4 x K32 for E4M3) and owns TMEM, warps 4-7 run the epilogue,
+// one thread per row.
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
 namespace sp {
 
 namespace gemm {
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 4;
+constexpr int A_BYTES = BM * BK_BYTES, B_BYTES = BN * BK_BYTES, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
 constexpr int NTHREADS = 256;
 }  // namespace gemm
 
 // HALF: distance between the two channels of a RoPE pair (0: no RoPE).
-template <int D, int HALF>
+// FP8: E4M3 operands with x_scale [m] and w_scale [n] (else BF16, unused).
+template <int D, int HALF, bool FP8>
 __global__ void __launch_bounds__(gemm::NTHREADS, 1)
     sp_qkv_gemm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                const uint16_t* __restrict__ bias, const float2* __restrict__ rope, uint16_t* __restrict__ q_out,
-                uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, uint32_t* __restrict__ err,
-                const QkvGeom g) {
+                const uint16_t* __restrict__ bias, const float2* __restrict__ rope, const float* __restrict__ x_scale,
+                const float* __restrict__ w_scale, uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out,
+                uint16_t* __restrict__ v_out, uint32_t* __restrict__ err, const QkvGeom g) {
     using namespace gemm;
-    constexpr uint32_t IDESC = make_idesc(C_F32, F_BF16, F_BF16, BM, BN);
+    constexpr uint32_t IDESC =
+        FP8 ? make_idesc(C_F32, F_E4M3, F_E4M3, BM, BN) : make_idesc(C_F32, F_BF16, F_BF16, BM, BN);
+    constexpr int BK = FP8 ? BK_BYTES : BK_BYTES / 2;  // K elements per ring stage
     extern __shared__ uint8_t dyn_smem[];
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t tmem_base_s;
@@ -109,10 +123,16 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
                     if (!(ok = mbar_wait(bar(full[s]), (used / STAGES) & 1, err, 42))) break;
                     tc_fence_after();
                     const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+                    // four MMAs of 32 bytes of K each (K16 bf16, K32 E4M3)
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++)
-                        umma_bf16(acc, smem_desc(sa + kk * 32, 1024, SWZ_128B),
-                                  smem_desc(sb + kk * 32, 1024, SWZ_128B), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t da = smem_desc(sa + kk * 32, 1024, SWZ_128B);
+                        const uint64_t db = smem_desc(sb + kk * 32, 1024, SWZ_128B);
+                        if (FP8)
+                            umma_f8(acc, da, db, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                        else
+                            umma_bf16(acc, da, db, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
                     tc_commit(bar(empty[s]));
                 }
                 if (ok) tc_commit(bar(acc_full[ab]));
@@ -133,6 +153,7 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
             tc_fence_after();
             const uint32_t acc = tmem + lane_off + ab * BN;
             const int bb = row / g.tokens, tok = row % g.tokens;
+            const float xs = FP8 && row < g.m ? __ldg(x_scale + row) : 1.0f;
             // the row's position inside its frame selects the RoPE table row
             const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
 #pragma unroll 1
@@ -159,8 +180,16 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
                         float y = __uint_as_float(v[e]);
-                        if (bias) y += __uint_as_float((uint32_t)bias[c0 + c + e] << 16);
-                        x[c + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);  // the GEMM's bf16 output
+                        if (FP8) {
+                            // bf16 GEMM output, then token scale, channel scale, bias
+                            y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                            y = __fmul_rn(__fmul_rn(y, xs), __ldg(w_scale + c0 + c + e));
+                            if (bias) y = __fadd_rn(y, __uint_as_float((uint32_t)bias[c0 + c + e] << 16));
+                            x[c + e] = y;
+                        } else {
+                            if (bias) y += __uint_as_float((uint32_t)bias[c0 + c + e] << 16);
+                            x[c + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);  // the GEMM's bf16 output
+                        }
                     }
                 }
                 if (HALF && part < 2) {
@@ -205,15 +234,16 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
     if (warp == 1) tmem_dealloc(tmem, 2 * BN);
 }
 
-template <int D, int HALF>
-static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q, uint16_t* k,
-                         uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+template <int D, int HALF, bool FP8>
+static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, const float* x_scale,
+                         const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
+                         const QkvGeom& g, cudaStream_t st) {
     static unsigned attr_set = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 32 || !(attr_set & (1u << dev))) {
-        cudaError_t e =
-            cudaFuncSetAttribute(sp_qkv_gemm<D, HALF>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(sp_qkv_gemm<D, HALF, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             gemm::SMEM);
         if (e != cudaSuccess) return e;
         if (dev < 32) attr_set |= 1u << dev;
     }
@@ -223,25 +253,38 @@ static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float*
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)(g.n / gemm::BN) * ((g.m + gemm::BM - 1) / gemm::BM);
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
-    sp_qkv_gemm<D, HALF><<<grid, gemm::NTHREADS, gemm::SMEM, st>>>(maps.x, maps.w, bias, (const float2*)rope, q, k,
-                                                                   v, err, g);
+    sp_qkv_gemm<D, HALF, FP8><<<grid, gemm::NTHREADS, gemm::SMEM, st>>>(maps.x, maps.w, bias, (const float2*)rope,
+                                                                        x_scale, w_scale, q, k, v, err, g);
     return cudaGetLastError();
+}
+
+template <bool FP8>
+static cudaError_t qkv_dispatch(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    const int half = rope ? g.rope_half : 0;
+    if (d == 64) {
+        if (half == 0) return qkv_t<64, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 16) return qkv_t<64, 16, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 32) return qkv_t<64, 32, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        return cudaErrorInvalidValue;
+    }
+    if (half == 0) return qkv_t<128, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    if (half == 64) return qkv_t<128, 64, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    return cudaErrorInvalidValue;
 }
 
 // RoPE pairings: none; D=64 with pairs (i, i+16) in each 32-wide half (VGGT
 // 2-D) or (i, i+32) (DINOv3); D=128 with (i, i+64) (rotate-half, Llama).
 cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q,
                             uint16_t* k, uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st) {
-    const int half = rope ? g.rope_half : 0;
-    if (d == 64) {
-        if (half == 0) return qkv_t<64, 0>(maps, bias, rope, q, k, v, err, g, st);
-        if (half == 16) return qkv_t<64, 16>(maps, bias, rope, q, k, v, err, g, st);
-        if (half == 32) return qkv_t<64, 32>(maps, bias, rope, q, k, v, err, g, st);
-        return cudaErrorInvalidValue;
-    }
-    if (half == 0) return qkv_t<128, 0>(maps, bias, rope, q, k, v, err, g, st);
-    if (half == 64) return qkv_t<128, 64>(maps, bias, rope, q, k, v, err, g, st);
-    return cudaErrorInvalidValue;
+    return qkv_dispatch<false>(d, maps, bias, rope, nullptr, nullptr, q, k, v, err, g, st);
+}
+
+cudaError_t launch_qkv_gemm_fp8(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    return qkv_dispatch<true>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
 }
 
 int qkv_smem_bytes() { return gemm::SMEM; }

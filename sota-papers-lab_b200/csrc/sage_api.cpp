@@ -74,19 +74,24 @@ int make_map(CUtensorMap* m, void* base, uint64_t d0, uint64_t d1, uint64_t d2, 
 
 // A 2-D BF16 tensor map {d0, d1} with row pitch p1 (bytes), box {b0, b1},
 // 128-byte swizzle, zero fill out of bounds.
-int make_map_bf16_2d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t p1, uint32_t b0,
-                     uint32_t b1) {
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, uint64_t d0, uint64_t d1, uint64_t p1,
+                uint32_t b0, uint32_t b1) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     cuuint64_t dims[2] = {d0, d1};
     cuuint64_t strides[1] = {p1};
     cuuint32_t box[2] = {b0, b1};
     cuuint32_t elem[2] = {1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+    CUresult r = enc(m, dtype, 2, const_cast<void*>(base), dims, strides, box, elem,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SPL_SAGE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return SPL_SAGE_OK;
+}
+
+int make_map_bf16_2d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t p1, uint32_t b0,
+                     uint32_t b1) {
+    return make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, d0, d1, p1, b0, b1);
 }
 
 bool fits_i32(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
@@ -564,10 +569,10 @@ int spl_sage_rope_table_1d(double base, int head_dim, int64_t positions, float* 
     return SPL_SAGE_OK;
 }
 
-int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const void* bias,
-                      const float* rope, void* q, void* k, void* v) {
-    if (!s || !shape || !x || !w || !q || !k || !v)
-        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm: NULL argument");
+// Checks of the QKV GEMM's arguments and its geometry; kmul = the hidden
+// size's required multiple.
+static int qkv_setup(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const float* rope,
+                     void* q, void* k, void* v, int kmul, sp::QkvGeom* out) {
     const spl_sage_qkv_shape& sh = *shape;
     const int64_t D = s->head_dim;
     const int64_t G = sh.kv_heads ? sh.kv_heads : sh.heads;
@@ -578,7 +583,8 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
         return fail(SPL_SAGE_ERR_INVALID,
                     "qkv: q and k/v widths (%lld, %lld channels) must be multiples of 256 (the GEMM tile)",
                     (long long)(sh.heads * D), (long long)(G * D));
-    if (kd % 8 != 0) return fail(SPL_SAGE_ERR_INVALID, "qkv: hidden size %lld must be a multiple of 8", (long long)kd);
+    if (kd % kmul != 0)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: hidden size %lld must be a multiple of %d", (long long)kd, kmul);
     if (!fits_i32(m) || !fits_i32(n) || !fits_i32(kd)) return fail(SPL_SAGE_ERR_INVALID, "qkv: size does not fit i32");
     if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16)
         return fail(SPL_SAGE_ERR_INVALID, "qkv: buffers must be 16-byte aligned");
@@ -590,11 +596,7 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
                               (long long)D);
         if (sh.frame_len <= 0) return fail(SPL_SAGE_ERR_INVALID, "qkv: RoPE frame length is 0");
     }
-    sp::QkvMaps maps;
-    int rc = make_map_bf16_2d(&maps.x, x, kd, m, kd * 2, 64, 128);
-    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, kd, n, kd * 2, 64, 256);
-    if (rc != SPL_SAGE_OK) return rc;
-    sp::QkvGeom g;
+    sp::QkvGeom& g = *out;
     g.m = (int)m;
     g.n = (int)n;
     g.k = (int)kd;
@@ -604,9 +606,59 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
     g.frame_len = rope ? (int)sh.frame_len : 1;
     g.rope_half = half;
     g.max_ctas = max_ctas(s);
-    cudaError_t e = sp::launch_qkv_gemm((int)D, maps, (const uint16_t*)bias, rope, (uint16_t*)q, (uint16_t*)k,
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x, const void* w, const void* bias,
+                      const float* rope, void* q, void* k, void* v) {
+    if (!s || !shape || !x || !w || !q || !k || !v)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm: NULL argument");
+    sp::QkvGeom g;
+    int rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g);
+    if (rc) return rc;
+    sp::QkvMaps maps;
+    rc = make_map_bf16_2d(&maps.x, x, g.k, g.m, (uint64_t)g.k * 2, 64, 128);
+    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, g.k, g.n, (uint64_t)g.k * 2, 64, 256);
+    if (rc != SPL_SAGE_OK) return rc;
+    cudaError_t e = sp::launch_qkv_gemm(s->head_dim, maps, (const uint16_t*)bias, rope, (uint16_t*)q, (uint16_t*)k,
                                         (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x8, const float* x_scale,
+                          const void* w8, const float* w_scale, const void* bias, const float* rope, void* q, void* k,
+                          void* v) {
+    if (!s || !shape || !x8 || !x_scale || !w8 || !w_scale || !q || !k || !v)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm_fp8: NULL argument");
+    sp::QkvGeom g;
+    int rc = qkv_setup(s, shape, x8, w8, rope, q, k, v, 16, &g);
+    if (rc) return rc;
+    sp::QkvMaps maps;
+    rc = make_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, x8, g.k, g.m, (uint64_t)g.k, 128, 128);
+    if (rc == SPL_SAGE_OK) rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, g.k, g.n, (uint64_t)g.k, 128, 256);
+    if (rc != SPL_SAGE_OK) return rc;
+    cudaError_t e = sp::launch_qkv_gemm_fp8(s->head_dim, maps, (const uint16_t*)bias, rope, x_scale, w_scale,
+                                            (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch fp8 qkv gemm");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_layer_norm_fp8(spl_sage* s, const void* x, int x_f32, int64_t rows, int64_t c, const float* gamma,
+                            const float* beta, float eps, void* out, void* q8, float* scales) {
+    if (!s || !x || !gamma || !beta || !q8 || !scales)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_layer_norm_fp8: NULL argument");
+    if (!sp::layer_norm_width_ok(c))
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "layer_norm: %lld channels unsupported (256, 512, 768, 1024, 1536, 2048, 3072 or 4096)",
+                    (long long)c);
+    if (rows < 0 || !fits_i32(rows)) return fail(SPL_SAGE_ERR_INVALID, "layer_norm: %lld rows", (long long)rows);
+    if (((uintptr_t)x | (uintptr_t)gamma | (uintptr_t)beta | (uintptr_t)out | (uintptr_t)q8) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "layer_norm: buffers must be 16-byte aligned");
+    if (rows == 0) return SPL_SAGE_OK;
+    cudaError_t e = sp::launch_layer_norm_fp8(x, x_f32 != 0, c, gamma, beta, eps, (int)rows, (uint16_t*)out,
+                                              (uint8_t*)q8, scales, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch layer_norm");
     return SPL_SAGE_OK;
 }
 

@@ -73,13 +73,22 @@ struct QkvGeom {
 };
 
 struct QkvMaps {
-    CUtensorMap x;  // bf16 {k, m}, box {64, 128}
-    CUtensorMap w;  // bf16 {k, n}, box {64, 256}
+    CUtensorMap x;  // bf16 {k, m}, box {64, 128} (E4M3: box {128, 128})
+    CUtensorMap w;  // bf16 {k, n}, box {64, 256} (E4M3: box {128, 256})
 };
 
 cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope, uint16_t* q,
                             uint16_t* k, uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st);
+// E4M3 operands, x_scale [m] and w_scale [n] (qkv_gemm.cu).
+cudaError_t launch_qkv_gemm_fp8(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                uint32_t* err, const QkvGeom& g, cudaStream_t st);
 int qkv_smem_bytes();
+
+// LayerNorm -> per-token E4M3 (layer_norm.cu): x f32 or bf16 [rows][c].
+bool layer_norm_width_ok(long long c);
+cudaError_t launch_layer_norm_fp8(const void* x, bool xf32, long long c, const float* gamma, const float* beta,
+                                  float eps, int rows, uint16_t* out, uint8_t* q8, float* qscale, cudaStream_t st);
 
 // Fixed device scratch of spl_sage_quantize_noalloc (sage_quant.cu).
 cudaError_t noalloc_part_buffer(float** out);

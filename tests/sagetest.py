@@ -131,29 +131,32 @@ def run_ours(c: Case, x: Inputs, *, export=True) -> Run:
         ln_dev = torch.from_numpy(x.ln).cuda()
         opts.qk_norm = sage.QkNorm(ln_dev, 1e-5)
     eng.forward(ws, tq, tk, tv, sage.Tensor(out, sage.Strides.bthd(c.tokens, c.heads, c.d)), opts)
-    quant = None
-    if export:
-        p = ws.plan
-        b, hq, hkv, d = c.batch, c.heads, c.kv_heads, c.d
-        q8 = torch.zeros(b * hq * p.tq_pad * d, dtype=torch.int8, device="cuda")
-        qs = torch.zeros(b * hq * p.tq_pad // 16, dtype=torch.float32, device="cuda")
-        k8 = torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.int8, device="cuda")
-        ks = torch.zeros(b * hkv * p.tk_pad // 64, dtype=torch.float32, device="cuda")
-        v8 = torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.uint8, device="cuda")
-        st = torch.zeros(b * hkv * 4 * d, dtype=torch.float32, device="cuda")
-        kb = torch.zeros(p.tk_pad, dtype=torch.float32, device="cuda")
-        eng.export_reference_layout(ws, q8, qs, k8, ks, v8, st, kb)
-        torch.cuda.synchronize()
-        quant = O.Quant(q8=q8.cpu().numpy().reshape(b, hq, p.tq_pad, d),
-                        q_scale=qs.cpu().numpy().reshape(b, hq, p.tq_pad // 16),
-                        k8=k8.cpu().numpy().reshape(b, hkv, p.tk_pad, d),
-                        k_scale=ks.cpu().numpy().reshape(b, hkv, p.tk_pad // 64),
-                        v8=v8.cpu().numpy().reshape(b, hkv, p.tk_pad // 64, d, 64),
-                        stats=st.cpu().numpy().reshape(b, hkv, 4, d), kbias=kb.cpu().numpy(), part=None)
+    quant = export_quant(eng, ws, c) if export else None
     word = eng.status(ws)
     assert word == 0
     o = out.view(torch.int16).cpu().numpy().view(np.uint16)
     return Run(O.bf16_to_f32(o).reshape(c.batch, c.tokens, c.heads, c.d), quant, ws, eng)
+
+
+def export_quant(eng, ws, c: Case) -> O.Quant:
+    """The workspace's quantised tensors in the reference's byte layouts."""
+    p = ws.plan
+    b, hq, hkv, d = c.batch, c.heads, c.kv_heads, c.d
+    q8 = torch.zeros(b * hq * p.tq_pad * d, dtype=torch.int8, device="cuda")
+    qs = torch.zeros(b * hq * p.tq_pad // 16, dtype=torch.float32, device="cuda")
+    k8 = torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.int8, device="cuda")
+    ks = torch.zeros(b * hkv * p.tk_pad // 64, dtype=torch.float32, device="cuda")
+    v8 = torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.uint8, device="cuda")
+    st = torch.zeros(b * hkv * 4 * d, dtype=torch.float32, device="cuda")
+    kb = torch.zeros(p.tk_pad, dtype=torch.float32, device="cuda")
+    eng.export_reference_layout(ws, q8, qs, k8, ks, v8, st, kb)
+    torch.cuda.synchronize()
+    return O.Quant(q8=q8.cpu().numpy().reshape(b, hq, p.tq_pad, d),
+                   q_scale=qs.cpu().numpy().reshape(b, hq, p.tq_pad // 16),
+                   k8=k8.cpu().numpy().reshape(b, hkv, p.tk_pad, d),
+                   k_scale=ks.cpu().numpy().reshape(b, hkv, p.tk_pad // 64),
+                   v8=v8.cpu().numpy().reshape(b, hkv, p.tk_pad // 64, d, 64),
+                   stats=st.cpu().numpy().reshape(b, hkv, 4, d), kbias=kb.cpu().numpy(), part=None)
 
 
 def run_reference_gpu(c: Case, x: Inputs, *, attend=True):
