@@ -222,6 +222,25 @@ int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const vo
 int spl_sage_layer_norm_fp8(spl_sage* s, const void* x, int x_f32, int64_t rows, int64_t c, const float* gamma,
                             const float* beta, float eps, void* out, void* q8, float* scales);
 
+/* Norm::row_epilogue with Quant::PerToken (norm.rs:280-336, cuda/norm.cu:
+ * 170-229): bf16 rows y [rows][ld] (e.g. the attention output, which the
+ * reference's FP8 block quantises for the proj GEMM) with optional token
+ * scales tok f32 [rows], channel scales chan f32 [c] and bias bf16 [c]
+ * (v = y * tok * chan + bias) to q8 E4M3 [rows][c] and scales f32 [rows]
+ * (amax / 448, 1 for an all-zero row).  c = 1024, 2048, 3072 or 4096, ld a
+ * multiple of 8; no activation. */
+int spl_sage_rows_fp8(spl_sage* s, const void* y, int64_t rows, int64_t c, int64_t ld, const float* tok,
+                      const float* chan, const void* bias, void* q8, float* scales);
+
+/* Gemm::linear_fp8 (gemm.rs:294-337): y bf16 [m][n] = x8 [m][k] w8 [n][k]^T
+ * in E4M3 on tcgen05 kind::f8f6f4 (FP32 accumulate), rounded to bf16, then,
+ * with x_scale f32 [m] and w_scale f32 [n], times both scales plus bias
+ * (bf16 [n] or NULL); with both scales NULL the scales are deferred to the
+ * consumer (WeightScale::Deferred) and y = bf16(x8 w8^T).  n a multiple of
+ * 256, k of 16. */
+int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const void* w8, const float* w_scale,
+                        const void* bias, int64_t m, int64_t n, int64_t k, void* y);
+
 /* spl_sage_qkv_gemm into q, k, v (bf16 scratch the caller owns), then
  * spl_sage_prepare of ws from them: the block's whole QKV path up to the
  * quantised tensors the attention reads. */

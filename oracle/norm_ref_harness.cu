@@ -46,3 +46,31 @@ extern "C" int ref_layer_norm_fp8(const void* x, int x_f32, int rows, int c, con
     }
     return (int)cudaGetLastError();
 }
+
+// Norm::row_epilogue (norm.rs:280-336) with Quant::PerToken and no
+// activation: RowArgs as the host fills it, row_c<n> with one 128-thread
+// block per row.
+extern "C" int ref_rows_fp8(const void* y, int rows, int c, int ld, const float* tok, const float* chan,
+                            const void* bias, void* q8, float* scales, void* stream_ptr) {
+    cudaStream_t st = (cudaStream_t)stream_ptr;
+    RowArgs a;
+    memset(&a, 0, sizeof a);
+    a.y = (unsigned long long)y;
+    a.ytok = (unsigned long long)tok;
+    a.ychan = (unsigned long long)chan;
+    a.bias = (unsigned long long)bias;
+    a.q = (unsigned long long)q8;
+    a.qscale = (unsigned long long)scales;
+    a.rows = rows;
+    a.ld = ld;
+    a.act = 0;
+    const dim3 grid((unsigned)rows);
+    switch (c) {
+        case 1024: row_c1<<<grid, 128, 0, st>>>(a); break;
+        case 2048: row_c2<<<grid, 128, 0, st>>>(a); break;
+        case 3072: row_c3<<<grid, 128, 0, st>>>(a); break;
+        case 4096: row_c4<<<grid, 128, 0, st>>>(a); break;
+        default: return (int)cudaErrorInvalidValue;
+    }
+    return (int)cudaGetLastError();
+}

@@ -83,6 +83,7 @@ def lib():
         L.or_qkv_reference.argtypes = [P, P, P, P] + [ctypes.c_int] * 10 + [P, P, P]
         L.or_qkv_reference_fp8.argtypes = [P] * 6 + [ctypes.c_int] * 10 + [P, P, P]
         L.or_layer_norm_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_float, P, P, P]
+        L.or_rows_fp8.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, P, P, P, P, P]
         L.or_errors.argtypes = [P, P, ctypes.c_int64, P]
         L.or_flops.restype = ctypes.c_double
         L.or_flops.argtypes = [ctypes.c_int] * 5
@@ -340,6 +341,19 @@ def layer_norm_fp8(x, gamma, beta, eps, with_out=False):
     return q8, sc, out
 
 
+def rows_fp8(y, c=None, tok=None, chan=None, bias=None):
+    """norm.cu:170-229 on the CPU: y bf16 bits [rows][ld].  Returns (q8, scales)."""
+    y = np.ascontiguousarray(y, np.uint16)
+    rows, ld = y.shape
+    c = c or ld
+    q8 = np.zeros((rows, c), np.uint8)
+    sc = np.zeros(rows, np.float32)
+    a = lambda t, dt: None if t is None else np.ascontiguousarray(t, dt)
+    lib().or_rows_fp8(_p(y), rows, c, ld, _p(a(tok, np.float32)), _p(a(chan, np.float32)), _p(a(bias, np.uint16)),
+                      _p(q8), _p(sc))
+    return q8, sc
+
+
 def errors(ours, ref) -> dict:
     a = np.ascontiguousarray(ours, np.float32).ravel()
     r = np.ascontiguousarray(ref, np.float32).ravel()
@@ -389,17 +403,35 @@ def norm_ref_available() -> bool:
     return os.path.exists(os.path.join(HERE, "_ref", "libnorm_ref.so"))
 
 
+def _load_norm_ref():
+    global _norm_ref
+    L = ctypes.CDLL(os.path.join(HERE, "_ref", "libnorm_ref.so"))
+    P = ctypes.c_void_p
+    L.ref_layer_norm_fp8.restype = ctypes.c_int
+    L.ref_layer_norm_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_float, P, P, P, P]
+    L.ref_rows_fp8.restype = ctypes.c_int
+    L.ref_rows_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P, P, P]
+    _norm_ref = L
+
+
 def ref_layer_norm_fp8(x, gamma, beta, eps, out, q8, scales, stream=0) -> int:
     """The reference's own ln_{f32,bf16}_c<n> kernels (norm.cu:37-144), on
     device tensors (x f32 or bf16 [rows][c]); returns a cudaError_t."""
     global _norm_ref
     if _norm_ref is None:
-        L = ctypes.CDLL(os.path.join(HERE, "_ref", "libnorm_ref.so"))
-        P = ctypes.c_void_p
-        L.ref_layer_norm_fp8.restype = ctypes.c_int
-        L.ref_layer_norm_fp8.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_float, P, P, P, P]
-        _norm_ref = L
+        _load_norm_ref()
     import torch
     p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
     return _norm_ref.ref_layer_norm_fp8(p(x), int(x.dtype == torch.float32), x.shape[0], x.shape[-1], p(gamma),
                                         p(beta), float(eps), p(out), p(q8), p(scales), ctypes.c_void_p(stream))
+
+
+def ref_rows_fp8(y, c, tok, chan, bias, q8, scales, stream=0) -> int:
+    """The reference's own row_c<n> kernels (norm.cu:170-235) on device
+    tensors: y bf16 [rows][ld]; returns a cudaError_t."""
+    global _norm_ref
+    if _norm_ref is None:
+        _load_norm_ref()
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+    return _norm_ref.ref_rows_fp8(p(y), y.shape[0], c, y.shape[-1], p(tok), p(chan), p(bias), p(q8), p(scales),
+                                  ctypes.c_void_p(stream))

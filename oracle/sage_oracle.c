@@ -889,3 +889,28 @@ void or_layer_norm_fp8(const void* x, int x_f32, int64_t rows, int c, const floa
     }
     free(v);
 }
+
+/* ------------------------------------------------------------------ rows -> FP8 */
+
+/* norm.cu:170-229 (Quant::PerToken, no activation): v = y * tok * chan +
+ * bias (separate roundings), amax over the row (order-free), scale =
+ * amax / 448 (1 for a zero row), q = e4m3(v * (448 / amax)).  Exact. */
+void or_rows_fp8(const uint16_t* y, int64_t rows, int c, int64_t ld, const float* tok, const float* chan,
+                 const uint16_t* bias, uint8_t* q8, float* scales) {
+    float* v = (float*)malloc(sizeof(float) * (size_t)c);
+    for (int64_t r = 0; r < rows; r++) {
+        const float ts = tok ? tok[r] : 1.0f;
+        float amax = 0.0f;
+        for (int i = 0; i < c; i++) {
+            float x = or_bf16_to_f32(y[r * ld + i]) * ts;
+            if (chan) x = x * chan[i];
+            if (bias) x = x + or_bf16_to_f32(bias[i]);
+            v[i] = x;
+            if (fabsf(x) > amax) amax = fabsf(x);
+        }
+        const float inv = amax > 0.0f ? 448.0f / amax : 1.0f;
+        scales[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+        for (int i = 0; i < c; i++) q8[r * c + i] = or_f32_to_e4m3(v[i] * inv);
+    }
+    free(v);
+}

@@ -150,6 +150,10 @@ void or_qkv_reference_fp8(const uint8_t* x8, const float* x_scale, const uint8_t
  * in the last place).  x f32 (x_f32 = 1) or bf16 [rows][c], c = 256 * n. */
 void or_layer_norm_fp8(const void* x, int x_f32, int64_t rows, int c, const float* gamma, const float* beta, float eps,
                        uint16_t* out, uint8_t* q8, float* scales);
+/* Norm::row_epilogue with Quant::PerToken, no activation (norm.cu:170-229):
+ * y bf16 [rows][ld], tok [rows], chan [c], bias bf16 [c] each optional. */
+void or_rows_fp8(const uint16_t* y, int64_t rows, int c, int64_t ld, const float* tok, const float* chan,
+                 const uint16_t* bias, uint8_t* q8, float* scales);
 
 /* LayerNorm of one row in f64 (reference.rs:110-118). */
 void or_layer_norm(float* x, const float* w, const float* b, int n, float eps);

@@ -95,7 +95,8 @@ EXPORTS = [
     "spl_sage_qkv_gemm", "spl_sage_qkv_gemm_quant", "spl_sage_rope_table_1d", "spl_sage_engine_status",
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
-    "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8",
+    "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
+    "spl_sage_linear_fp8",
 ]
 
 # spl_sage_cp_attend flags
@@ -135,6 +136,8 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_qkv_gemm.argtypes = [P, ctypes.POINTER(_QkvShape)] + [P] * 7
         L.spl_sage_qkv_gemm_fp8.argtypes = [P, ctypes.POINTER(_QkvShape)] + [P] * 9
         L.spl_sage_layer_norm_fp8.argtypes = [P, P, I, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_float, P, P, P]
+        L.spl_sage_rows_fp8.argtypes = [P, P] + [ctypes.c_int64] * 3 + [P] * 5
+        L.spl_sage_linear_fp8.argtypes = [P] * 6 + [ctypes.c_int64] * 3 + [P]
         L.spl_sage_qkv_gemm_quant.argtypes = [P, P, ctypes.POINTER(_QkvShape)] + [P] * 7 + [ctypes.POINTER(_Options)]
         L.spl_sage_rope_table_1d.argtypes = [ctypes.c_double, I, ctypes.c_int64, P]
         L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
@@ -438,6 +441,22 @@ class SageAttention:
         rows, c = x.shape[0], x.shape[-1]
         _check(lib().spl_sage_layer_norm_fp8(self._h, p(x), int(x.dtype == torch.float32), rows, c, p(gamma), p(beta),
                                              float(eps), p(out), p(q8), p(scales)))
+
+    def rows_fp8(self, y, q8, scales, *, c: int | None = None, tok=None, chan=None, bias=None):
+        """Norm::row_epilogue with per-token FP8 (spl_sage_rows_fp8): y bf16
+        [rows][ld] (its first c channels) -> q8 uint8 [rows][c], scales f32."""
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        rows, ld = y.shape[0], y.shape[-1]
+        _check(lib().spl_sage_rows_fp8(self._h, p(y), rows, c or ld, ld, p(tok), p(chan), p(bias), p(q8),
+                                       p(scales)))
+
+    def linear_fp8(self, x8, x_scale, w8, w_scale, bias, y):
+        """Gemm::linear_fp8 (spl_sage_linear_fp8): y bf16 [m][n] from E4M3 x8
+        [m][k] and w8 [n][k]; scales None for deferred scales."""
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+        m, k = x8.shape
+        n = w8.shape[0]
+        _check(lib().spl_sage_linear_fp8(self._h, p(x8), p(x_scale), p(w8), p(w_scale), p(bias), m, n, k, p(y)))
 
     def qkv_gemm_quant(self, ws: Workspace, x, w, bias, rope, q, k, v, opts: Options | None = None, *,
                        rope_half: int = 0, frame_len: int = 0):

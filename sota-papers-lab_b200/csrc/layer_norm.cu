@@ -142,3 +142,68 @@ cudaError_t launch_layer_norm_fp8(const void* x, bool xf32, long long c, const f
 }
 
 }  // namespace sp
+
+namespace sp {
+
+// Norm::row_epilogue with Quant::PerToken (platform/spl-nn/src/norm.rs:280-336,
+// cuda/norm.cu:170-229): the attention output (or any bf16 GEMM output) to
+// per-token E4M3 for the next FP8 GEMM (block.rs: attention output -> FP8 ->
+// proj).  y bf16 [rows][ld], optional token scale, channel scale and bias
+// (v = y * tok * chan + bias, in that order), amax over the row, scale =
+// amax / 448 (1 for a zero row), q = E4M3(v * (448 / amax)).  One 128-thread
+// block per row; thread t owns the 8-channel chunks t, t + 128, ...
+// (C = 1024 * NCH); the warp maxima meet in shared memory.
+template <int NCH>
+__global__ void __launch_bounds__(128) sp_rows_fp8(const uint16_t* __restrict__ y, long long ld,
+                                                   const float* __restrict__ tok, const float* __restrict__ chan,
+                                                   const uint16_t* __restrict__ bias, uint8_t* __restrict__ q8,
+                                                   float* __restrict__ qscale) {
+    constexpr int C = NCH * 1024;
+    __shared__ float wmax[4];
+    const int row = blockIdx.x, t = threadIdx.x;
+    const float ts = tok ? __ldg(tok + row) : 1.0f;
+    float v[NCH][8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NCH; i++) {
+        const int c0 = (i * 128 + t) * 8;
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(y + (long long)row * ld + c0)), v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float x = __fmul_rn(v[i][j], ts);
+            if (chan) x = __fmul_rn(x, __ldg(chan + c0 + j));
+            if (bias) x = __fadd_rn(x, __uint_as_float((uint32_t)__ldg(bias + c0 + j) << 16));
+            v[i][j] = x;
+            amax = fmaxf(amax, fabsf(x));
+        }
+    }
+    amax = warp_max_xor(amax);
+    if ((t & 31) == 0) wmax[t >> 5] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    const float inv = amax > 0.0f ? 448.0f / amax : 1.0f;
+    if (t == 0) qscale[row] = amax > 0.0f ? amax / 448.0f : 1.0f;
+#pragma unroll
+    for (int i = 0; i < NCH; i++) {
+        float s[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) s[j] = v[i][j] * inv;
+        const uint2 w = make_uint2(e4m3x4(s[0], s[1], s[2], s[3]), e4m3x4(s[4], s[5], s[6], s[7]));
+        *reinterpret_cast<uint2*>(q8 + (long long)row * C + (i * 128 + t) * 8) = w;
+    }
+}
+
+cudaError_t launch_rows_fp8(const uint16_t* y, long long ld, long long c, int rows, const float* tok,
+                            const float* chan, const uint16_t* bias, uint8_t* q8, float* qscale, cudaStream_t st) {
+    const dim3 grid((unsigned)rows);
+    switch (c) {
+        case 1024: sp_rows_fp8<1><<<grid, 128, 0, st>>>(y, ld, tok, chan, bias, q8, qscale); break;
+        case 2048: sp_rows_fp8<2><<<grid, 128, 0, st>>>(y, ld, tok, chan, bias, q8, qscale); break;
+        case 3072: sp_rows_fp8<3><<<grid, 128, 0, st>>>(y, ld, tok, chan, bias, q8, qscale); break;
+        case 4096: sp_rows_fp8<4><<<grid, 128, 0, st>>>(y, ld, tok, chan, bias, q8, qscale); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace sp

@@ -37,7 +37,9 @@ constexpr int NTHREADS = 256;
 }  // namespace gemm
 
 // HALF: distance between the two channels of a RoPE pair (0: no RoPE).
-// FP8: E4M3 operands with x_scale [m] and w_scale [n] (else BF16, unused).
+// FP8: E4M3 operands with x_scale [m] and w_scale [n] (else BF16, unused);
+// NULL scales leave the bf16 accumulator unscaled (the reference's deferred
+// weight scales, applied by the consumer).
 template <int D, int HALF, bool FP8>
 __global__ void __launch_bounds__(gemm::NTHREADS, 1)
     sp_qkv_gemm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
             tc_fence_after();
             const uint32_t acc = tmem + lane_off + ab * BN;
             const int bb = row / g.tokens, tok = row % g.tokens;
-            const float xs = FP8 && row < g.m ? __ldg(x_scale + row) : 1.0f;
+            const float xs = FP8 && x_scale && row < g.m ? __ldg(x_scale + row) : 1.0f;
             // the row's position inside its frame selects the RoPE table row
             const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
 #pragma unroll 1
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
                         if (FP8) {
                             // bf16 GEMM output, then token scale, channel scale, bias
                             y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
-                            y = __fmul_rn(__fmul_rn(y, xs), __ldg(w_scale + c0 + c + e));
+                            y = __fmul_rn(__fmul_rn(y, xs), w_scale ? __ldg(w_scale + c0 + c + e) : 1.0f);
                             if (bias) y = __fadd_rn(y, __uint_as_float((uint32_t)bias[c0 + c + e] << 16));
                             x[c + e] = y;
                         } else {

@@ -644,6 +644,62 @@ int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const vo
     return SPL_SAGE_OK;
 }
 
+int spl_sage_rows_fp8(spl_sage* s, const void* y, int64_t rows, int64_t c, int64_t ld, const float* tok,
+                      const float* chan, const void* bias, void* q8, float* scales) {
+    if (!s || !y || !q8 || !scales) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_rows_fp8: NULL argument");
+    if (c != 1024 && c != 2048 && c != 3072 && c != 4096)
+        return fail(SPL_SAGE_ERR_INVALID, "row_epilogue: %lld channels unsupported (1024, 2048, 3072 or 4096)",
+                    (long long)c);
+    if (ld < c || ld % 8 != 0)
+        return fail(SPL_SAGE_ERR_INVALID, "row_epilogue: ld %lld must be a multiple of 8 and at least %lld",
+                    (long long)ld, (long long)c);
+    if (rows < 0 || !fits_i32(rows)) return fail(SPL_SAGE_ERR_INVALID, "row_epilogue: %lld rows", (long long)rows);
+    if (((uintptr_t)y | (uintptr_t)chan | (uintptr_t)bias | (uintptr_t)q8) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "row_epilogue: buffers must be 16-byte aligned");
+    if (rows == 0) return SPL_SAGE_OK;
+    cudaError_t e = sp::launch_rows_fp8((const uint16_t*)y, ld, c, (int)rows, tok, chan, (const uint16_t*)bias,
+                                        (uint8_t*)q8, scales, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch row_epilogue");
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const void* w8, const float* w_scale,
+                        const void* bias, int64_t m, int64_t n, int64_t k, void* y) {
+    if (!s || !x8 || !w8 || !y) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_linear_fp8: NULL argument");
+    if ((x_scale == nullptr) != (w_scale == nullptr))
+        return fail(SPL_SAGE_ERR_INVALID, "gemm: give both scales, or neither (deferred)");
+    if (!x_scale && bias) return fail(SPL_SAGE_ERR_INVALID, "gemm: deferred scales leave the bias to the consumer");
+    if (m <= 0 || n <= 0 || k <= 0) return fail(SPL_SAGE_ERR_INVALID, "gemm: empty shape");
+    if (n % 256 != 0)
+        return fail(SPL_SAGE_ERR_INVALID, "gemm: %lld output channels must be a multiple of 256 (the tile)",
+                    (long long)n);
+    if (k % 16 != 0) return fail(SPL_SAGE_ERR_INVALID, "gemm: k %lld must be a multiple of 16", (long long)k);
+    if (!fits_i32(m) || !fits_i32(n) || !fits_i32(k)) return fail(SPL_SAGE_ERR_INVALID, "gemm: size does not fit i32");
+    if (((uintptr_t)x8 | (uintptr_t)w8 | (uintptr_t)y) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "gemm: buffers must be 16-byte aligned");
+    // the QKV kernel with one part of n / 128 "heads" of 128 channels and no
+    // RoPE writes y row-major [m][n]
+    sp::QkvGeom g;
+    memset(&g, 0, sizeof g);
+    g.m = (int)m;
+    g.n = (int)n;
+    g.k = (int)k;
+    g.tokens = (int)m;
+    g.hq = (int)(n / 128);
+    g.hkv = 0;
+    g.frame_len = 1;
+    g.rope_half = 0;
+    g.max_ctas = max_ctas(s);
+    sp::QkvMaps maps;
+    int rc = make_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, x8, k, m, k, 128, 128);
+    if (rc == SPL_SAGE_OK) rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, k, n, k, 128, 256);
+    if (rc != SPL_SAGE_OK) return rc;
+    cudaError_t e = sp::launch_qkv_gemm_fp8(128, maps, (const uint16_t*)bias, nullptr, x_scale, w_scale,
+                                            (uint16_t*)y, nullptr, nullptr, s->err, g, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch fp8 gemm");
+    return SPL_SAGE_OK;
+}
+
 int spl_sage_layer_norm_fp8(spl_sage* s, const void* x, int x_f32, int64_t rows, int64_t c, const float* gamma,
                             const float* beta, float eps, void* out, void* q8, float* scales) {
     if (!s || !x || !gamma || !beta || !q8 || !scales)

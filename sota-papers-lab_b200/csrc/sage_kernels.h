@@ -89,6 +89,9 @@ int qkv_smem_bytes();
 bool layer_norm_width_ok(long long c);
 cudaError_t launch_layer_norm_fp8(const void* x, bool xf32, long long c, const float* gamma, const float* beta,
                                   float eps, int rows, uint16_t* out, uint8_t* q8, float* qscale, cudaStream_t st);
+// bf16 rows -> per-token E4M3 (layer_norm.cu): y [rows][ld], c = 1024 * n.
+cudaError_t launch_rows_fp8(const uint16_t* y, long long ld, long long c, int rows, const float* tok,
+                            const float* chan, const uint16_t* bias, uint8_t* q8, float* qscale, cudaStream_t st);
 
 // Fixed device scratch of spl_sage_quantize_noalloc (sage_quant.cu).
 cudaError_t noalloc_part_buffer(float** out);

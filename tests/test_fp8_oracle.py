@@ -49,3 +49,17 @@ def test_fp8_qkv_oracle_against_numpy():
     np.testing.assert_allclose(q.reshape(m, -1), y[:, :hq * d], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(kk.reshape(m, -1), y[:, hq * d:(hq + hkv) * d], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(v.reshape(m, -1), y[:, (hq + hkv) * d:], rtol=1e-6, atol=1e-6)
+
+
+def test_rows_fp8_oracle_against_numpy():
+    rng = np.random.default_rng(5)
+    y = O.f32_to_bf16(rng.normal(size=(6, 2056)) * 5)
+    y[2] = 0
+    tok = rng.uniform(0.5, 2, size=6).astype(np.float32)
+    q8, sc = O.rows_fp8(y, 2048, tok=tok)
+    v = O.bf16_to_f32(y)[:, :2048].astype(np.float64) * tok[:, None]
+    amax = np.abs(v).max(1)
+    np.testing.assert_allclose(sc, np.where(amax > 0, amax / 448, 1.0), rtol=1e-6)
+    deq = O.e4m3_to_f32(q8) * sc[:, None]
+    assert np.all(np.abs(deq - v) <= np.maximum(np.abs(v) * 2.0 ** -4, sc[:, None] * 2.0 ** -9) * 1.01)
+    assert sc[2] == 1.0 and not q8[2].any()

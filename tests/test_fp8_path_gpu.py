@@ -175,3 +175,88 @@ def test_fp8_chain_feeds_the_quantiser_bit_exactly():
     want = O.prepare(qb, kb, vb, st.geom(c))
     st.assert_quant_equal(got, want, kbias=False, what="fp8 chain")
     ws_.close()
+
+
+# ---------------------------------------------------------------- the output side: attention -> FP8 -> proj
+
+def _bf16_dev(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("c,ld", [(1024, 1024), (2048, 2056), (4096, 4096)])
+def test_rows_fp8_bytes_equal_the_reference_kernel(c, ld):
+    if not O.norm_ref_available():
+        pytest.skip("the reference's LayerNorm kernels were not built (oracle/_ref)")
+    rows = 77
+    rng = np.random.default_rng(c)
+    y = O.f32_to_bf16(rng.normal(size=(rows, ld)) * 3)
+    y[5] = 0
+    tok = rng.uniform(0.5, 2, size=rows).astype(np.float32)
+    yd, td = _bf16_dev(y), torch.from_numpy(tok).cuda()
+    eng = _engine()
+    for t in (None, td):
+        ours = (torch.zeros(rows, c, dtype=torch.uint8, device="cuda"), torch.zeros(rows, device="cuda"))
+        ref = (torch.zeros(rows, c, dtype=torch.uint8, device="cuda"), torch.zeros(rows, device="cuda"))
+        eng.rows_fp8(yd, ours[0], ours[1], c=c, tok=t)
+        assert O.ref_rows_fp8(yd, c, t, None, None, ref[0], ref[1], torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(ours[0], ref[0]) and torch.equal(ours[1], ref[1])
+        # and the CPU restatement, exactly (no approximate functions on this path)
+        q8, sc = O.rows_fp8(y, c, tok=None if t is None else tok)
+        assert np.array_equal(ours[0].cpu().numpy(), q8) and np.array_equal(ours[1].cpu().numpy(), sc)
+        assert sc[5] == 1.0
+
+
+def test_linear_fp8_matches_f64_oracle_and_defers_scales():
+    m, n, k = 300, 1024, 1024
+    rng = np.random.default_rng(4)
+    x8 = O.f32_to_e4m3_array(rng.normal(size=(m, k)) * 40)
+    w8, ws = _quant_weights(rng.normal(0, 0.02, size=(n, k)).astype(np.float32))
+    xs = rng.uniform(0.005, 0.02, size=m).astype(np.float32)
+    bias = O.f32_to_bf16(rng.normal(0, 0.1, size=n))
+    eng = _engine()
+    x8d, w8d = torch.from_numpy(x8).cuda(), torch.from_numpy(w8).cuda()
+    y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    eng.linear_fp8(x8d, torch.from_numpy(xs).cuda(), w8d, torch.from_numpy(ws).cuda(), _bf16_dev(bias), y)
+    yd = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    eng.linear_fp8(x8d, None, w8d, None, None, yd)
+    torch.cuda.synchronize()
+    assert eng.engine_status() == 0
+    want, _, _ = O.qkv_reference_fp8(x8, xs, w8, ws, bias, None, tokens=m, hq=n // 128, hkv=0, d=128)
+    e = O.errors(O.bf16_to_f32(y.view(torch.int16).cpu().numpy().view(np.uint16)), want.reshape(m, n))
+    assert e["rel_l2"] < 5e-3, e
+    ones_m, ones_n = np.ones(m, np.float32), np.ones(n, np.float32)
+    raw, _, _ = O.qkv_reference_fp8(x8, ones_m, w8, ones_n, None, None, tokens=m, hq=n // 128, hkv=0, d=128)
+    e = O.errors(O.bf16_to_f32(yd.view(torch.int16).cpu().numpy().view(np.uint16)), raw.reshape(m, n))
+    assert e["rel_l2"] < 5e-3, e
+    with pytest.raises(sage.SageError):  # one scale without the other
+        eng.linear_fp8(x8d, torch.from_numpy(xs).cuda(), w8d, None, None, yd)
+
+
+def test_attention_output_to_fp8_proj():
+    """The reference's FP8 block after attention: the bf16 attention output
+    [T][H*D] -> per-token E4M3 -> FP8 proj GEMM (deferred weight scales), then
+    y * tok * chan, against the f64 oracle on the quantised operands."""
+    c = st.Case(batch=1, heads=8, kv_heads=8, tokens=384, d=128, causal=False, packed=False, seed=3)
+    x = st.make_inputs(c)
+    run = st.run_ours(c, x, export=False)
+    dim = c.heads * c.d
+    o_bits = O.f32_to_bf16(run.out.reshape(c.tokens, dim))
+    eng = _engine()
+    o8 = torch.zeros(c.tokens, dim, dtype=torch.uint8, device="cuda")
+    osc = torch.zeros(c.tokens, device="cuda")
+    eng.rows_fp8(_bf16_dev(o_bits), o8, osc)
+    rng = np.random.default_rng(8)
+    w8, ws = _quant_weights(rng.normal(0, 0.02, size=(dim, dim)).astype(np.float32))
+    y = torch.empty(c.tokens, dim, dtype=torch.bfloat16, device="cuda")
+    eng.linear_fp8(o8, osc, torch.from_numpy(w8).cuda(), torch.from_numpy(ws).cuda(), None, y)
+    torch.cuda.synchronize()
+    q8, sc = O.rows_fp8(o_bits)
+    assert np.array_equal(o8.cpu().numpy(), q8) and np.array_equal(osc.cpu().numpy(), sc)
+    want, _, _ = O.qkv_reference_fp8(q8, sc, w8, ws, None, None, tokens=c.tokens, hq=dim // 128, hkv=0, d=128)
+    e = O.errors(O.bf16_to_f32(y.view(torch.int16).cpu().numpy().view(np.uint16)), want.reshape(c.tokens, dim))
+    assert e["rel_l2"] < 5e-3, e
+    # and the FP8 path against the bf16 projection of the unquantised output
+    exact = O.bf16_to_f32(o_bits).astype(np.float64) @ (O.e4m3_to_f32(w8) * ws[:, None]).T.astype(np.float64)
+    e = O.errors(O.bf16_to_f32(y.view(torch.int16).cpu().numpy().view(np.uint16)), exact)
+    assert e["cos"] > 0.999, e
