@@ -573,7 +573,7 @@ def qkv_gemm_time(eng, w, dev, stream, iters=10):
     assert eng.engine_status() == 0
     ms = e0.elapsed_time(e1) / iters
     flops = 2.0 * B * N * hidden * n_out
-    return {"kernel": "sp_qkv_gemm (tcgen05 kind::f16, bias + RoPE + bf16 epilogue)",
+    return {"kernel": "sp_qkv_gemm_2sm (tcgen05 kind::f16 on SM pairs, cta_group::2; bias + RoPE + bf16 epilogue)",
             "shape": f"[{B * N}x{hidden}] x [{n_out}x{hidden}]^T", "ms": round(ms, 4),
             "achieved": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "bound": "tensor"}
 
@@ -622,8 +622,8 @@ def qkv_fp8_time(eng, w, dev, stream, iters=10):
     assert eng.engine_status() == 0
     flops = 2.0 * B * N * hidden * n_out
     ln_bytes = B * N * hidden * (2 + 1) + B * N * 4  # bf16 in, E4M3 out, scales
-    return {"kernels": "sp_ln_fp8 (LN1 -> per-token E4M3) + sp_qkv_gemm<FP8> (tcgen05 kind::f8f6f4, "
-                       "token/channel scales + RoPE + bf16 epilogue)",
+    return {"kernels": "sp_ln_fp8 (LN1 -> per-token E4M3) + sp_qkv_gemm_2sm<FP8> (tcgen05 kind::f8f6f4 on SM "
+                       "pairs, token/channel scales + RoPE + bf16 epilogue)",
             "shape": f"[{B * N}x{hidden}] x [{n_out}x{hidden}]^T", "ln_ms": round(times["ln"], 4),
             "ln_gbs": round(ln_bytes / (times["ln"] * 1e-3) / 1e9, 1), "gemm_ms": round(times["gemm"], 4),
             "achieved": round(flops / (times["gemm"] * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "bound": "tensor"}

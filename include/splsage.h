@@ -133,6 +133,12 @@ void spl_sage_destroy(spl_sage* s);
  * instead of waiting for the whole persistent launch.  0 by default. */
 int spl_sage_reserve_sms(spl_sage* s, int n);
 
+/* No counterpart in the reference.  on = 1 (default): the QKV and FP8
+ * GEMMs run on SM pairs (clusters of two CTAs, tcgen05 cta_group::2,
+ * 256 x 256 tiles, each CTA loading half of both operands); 0: one SM per
+ * 128 x 256 tile. */
+int spl_sage_gemm_pairs(spl_sage* s, int on);
+
 /* SageAttention::workspace (mod.rs:649-670) via Plan::new (mod.rs:405-440):
  * allocates the quantised buffers (zeroed, on the engine's stream).  merge
  * NULL = dense.  Causal with merging is rejected. */

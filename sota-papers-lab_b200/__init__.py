@@ -96,7 +96,7 @@ EXPORTS = [
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
-    "spl_sage_linear_fp8",
+    "spl_sage_linear_fp8", "spl_sage_gemm_pairs",
 ]
 
 # spl_sage_cp_attend flags
@@ -121,6 +121,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_create.argtypes = [P, I, ctypes.POINTER(_Config), ctypes.POINTER(P)]
         L.spl_sage_destroy.argtypes = [P]
         L.spl_sage_reserve_sms.argtypes = [P, I]
+        L.spl_sage_gemm_pairs.argtypes = [P, I]
         L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
         L.spl_sage_ws_destroy.argtypes = [P]
         L.spl_sage_ws_bytes.restype = ctypes.c_int64
@@ -388,6 +389,10 @@ class SageAttention:
         other streams, e.g. NCCL's during a ring step); 0 restores all."""
         _check(lib().spl_sage_reserve_sms(self._h, n))
         self.reserved_sms = n
+
+    def gemm_pairs(self, on: bool):
+        """Run this engine's GEMMs on SM pairs (tcgen05 cta_group::2)."""
+        _check(lib().spl_sage_gemm_pairs(self._h, int(on)))
 
     def close(self):
         if self._h:

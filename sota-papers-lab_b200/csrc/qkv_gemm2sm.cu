@@ -1,0 +1,356 @@
+// The QKV GEMM of qkv_gemm.cu on SM pairs: a cluster of two CTAs computes a
+// 256 x 256 output tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA
+// loads its own 128 rows of x and its own 128 rows of W (TMA, no
+// multicast), so a 128-byte K stage is 32 KB per CTA instead of 48 KB for
+// the same work, and six stages fit where four did: at the FP8 rate the
+// single-SM kernel's four 48 KB stages cover too little of the L2 latency.
+//
+// Roles per CTA: warp 0 loads (both CTAs' loads complete on the leader's
+// stage barrier, which the leader arms for both halves), warp 1 owns TMEM
+// (allocated for the pair) and, in the leader (cluster rank 0), issues the
+// MMAs, whose commits arrive on the stage and accumulator barriers of both
+// CTAs; warps 4-7 read their own CTA's accumulator (rows rank * 128 + lane)
+// and run the same epilogue as qkv_gemm.cu, then tell the leader the
+// accumulator is free.  Every mbarrier wait is bounded; both CTAs always
+// reach the closing cluster barrier, after which TMEM is freed.
+#include "sage_dev.cuh"
+#include "sage_kernels.h"
+
+namespace sp {
+
+namespace gemm2 {
+constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 6;      // per CTA: 128 rows of the 256-row tile
+constexpr int A_BYTES = BM * BK_BYTES, B_BYTES = (BN / 2) * BK_BYTES;  // each CTA holds half of B's rows
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+constexpr int NTHREADS = 256;
+}  // namespace gemm2
+
+namespace {
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of this CTA's shared-memory word `addr` in the
+// cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+// Arrive once on the barrier at shared offset `bar` of both CTAs of the pair
+// when this thread's tcgen05.mma so far complete.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            bar),
+        "h"((unsigned short)3)
+        : "memory");
+}
+
+template <bool FP8>
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    if (FP8)
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n}"
+            ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    else
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}"
+            ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// TMA load into this CTA's shared memory, completing on a barrier of either
+// CTA of the pair (bar: a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.cta_group::2 [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(dst),
+        "l"(map), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+}  // namespace
+
+template <int D, int HALF, bool FP8>
+__global__ void __launch_bounds__(gemm2::NTHREADS, 1)
+    sp_qkv_gemm_2sm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                    const uint16_t* __restrict__ bias, const float2* __restrict__ rope,
+                    const float* __restrict__ x_scale, const float* __restrict__ w_scale, uint16_t* __restrict__ q_out,
+                    uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out, uint32_t* __restrict__ err,
+                    const QkvGeom g) {
+    using namespace gemm2;
+    constexpr int TM = 2 * BM;  // rows of the pair's tile
+    constexpr uint32_t IDESC =
+        FP8 ? make_idesc(C_F32, F_E4M3, F_E4M3, TM, BN) : make_idesc(C_F32, F_BF16, F_BF16, TM, BN);
+    constexpr int BK = FP8 ? BK_BYTES : BK_BYTES / 2;  // K elements per ring stage
+    extern __shared__ uint8_t dyn_smem[];
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], done;
+    __shared__ uint32_t tmem_base_s;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int n_tiles = g.n / BN, ntiles = n_tiles * ((g.m + TM - 1) / TM);
+    const int kblocks = (g.k + BK - 1) / BK;
+    auto tile_m0 = [&](int t) { return (t / n_tiles) * TM; };
+    auto tile_n0 = [&](int t) { return (t % n_tiles) * BN; };
+    const uint32_t sbase = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    auto bar = [](uint64_t& x) { return smem_u32(&x); };
+
+    if (tid == 0) {
+        for (int i = 0; i < STAGES; i++) {
+            mbar_init(bar(full[i]), 1);   // the leader's arrival (with both CTAs' bytes)
+            mbar_init(bar(empty[i]), 1);  // one commit from the leader's MMA thread
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(acc_full[i]), 1);
+            mbar_init(bar(acc_empty[i]), 8);  // four epilogue warps of each CTA (leader's barrier)
+        }
+        mbar_init(bar(done), 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(&tmem_base_s), 2 * BN);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&map_x);
+            tma_prefetch_desc(&map_w);
+            int issued = 0;
+            bool ok = true;
+            for (int t = pair; t < ntiles && ok; t += npairs) {
+                const int m0 = tile_m0(t) + (int)rank * BM, n0 = tile_n0(t) + (int)rank * (BN / 2);
+                for (int kb = 0; kb < kblocks; kb++) {
+                    const int s = issued % STAGES;
+                    // this CTA's half of stage s is free once the pair's MMAs read it
+                    if (issued >= STAGES && !mbar_wait(bar(empty[s]), ((issued / STAGES) - 1) & 1, err, 50)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+                    const uint32_t fb = map_to_rank(bar(full[s]), 0);  // the leader's stage barrier
+                    if (leader) mbar_expect_tx(bar(full[s]), 2 * STAGE_BYTES);
+                    tma_load_2d_pair(sa, &map_x, fb, kb * BK, m0);
+                    tma_load_2d_pair(sb, &map_w, fb, kb * BK, n0);
+                    issued++;
+                }
+            }
+            if (leader) {
+                // drain: every stage's last loads (both halves) have landed
+                for (int s = 0; s < STAGES && s < issued; s++) {
+                    const int last = s + ((issued - 1 - s) / STAGES) * STAGES;
+                    mbar_wait(bar(full[s]), (last / STAGES) & 1, err, 51, false);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            bool ok = true;
+            int used = 0;
+            for (int t = pair, it = 0; t < ntiles && ok; t += npairs, it++) {
+                const int ab = it & 1;
+                if (it >= 2 && !(ok = mbar_wait(bar(acc_empty[ab]), ((it >> 1) - 1) & 1, err, 55))) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + ab * BN;
+                for (int kb = 0; kb < kblocks; kb++, used++) {
+                    const int s = used % STAGES;
+                    if (!(ok = mbar_wait(bar(full[s]), (used / STAGES) & 1, err, 52))) break;
+                    tc_fence_after();
+                    const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        umma_pair<FP8>(acc, smem_desc(sa + kk * 32, 1024, SWZ_128B),
+                                       smem_desc(sb + kk * 32, 1024, SWZ_128B), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit_pair(bar(empty[s]));
+                }
+                if (ok) tc_commit_pair(bar(acc_full[ab]));
+            }
+            tc_commit_pair(bar(done));  // (the peer's copy of `done` is not waited on)
+            mbar_wait(bar(done), 0, err, 53, false);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ epilogue, one thread per row
+        const int r = tid - 128;
+        const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+        bool ok = true;
+        for (int t = pair, it = 0; t < ntiles && ok; t += npairs, it++) {
+            const int ab = it & 1;
+            const int m0 = tile_m0(t), n0 = tile_n0(t);
+            const int row = m0 + (int)rank * BM + r;
+            if (!(ok = warp_all_wait(bar(acc_full[ab]), (it >> 1) & 1, err, 54))) break;
+            tc_fence_after();
+            const uint32_t acc = tmem + lane_off + ab * BN;
+            const int bb = row / g.tokens, tok = row % g.tokens;
+            const float xs = FP8 && x_scale && row < g.m ? __ldg(x_scale + row) : 1.0f;
+            const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
+#pragma unroll 1
+            for (int hh = 0; hh < BN / D; hh++) {
+                const int c0 = n0 + hh * D;
+                int part, head;
+                if (c0 < g.hq * D) {
+                    part = 0;
+                    head = c0 / D;
+                } else if (c0 < (g.hq + g.hkv) * D) {
+                    part = 1;
+                    head = (c0 - g.hq * D) / D;
+                } else {
+                    part = 2;
+                    head = (c0 - (g.hq + g.hkv) * D) / D;
+                }
+                float x[D];
+#pragma unroll
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(acc + hh * D + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        float y = __uint_as_float(v[e]);
+                        if (FP8) {
+                            y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                            y = __fmul_rn(__fmul_rn(y, xs), w_scale ? __ldg(w_scale + c0 + c + e) : 1.0f);
+                            if (bias) y = __fadd_rn(y, __uint_as_float((uint32_t)bias[c0 + c + e] << 16));
+                            x[c + e] = y;
+                        } else {
+                            if (bias) y += __uint_as_float((uint32_t)bias[c0 + c + e] << 16);
+                            x[c + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                        }
+                    }
+                }
+                if (HALF && part < 2) {
+#pragma unroll
+                    for (int d = 0; d < D; d++) {
+                        if (d & HALF) continue;
+                        const int pr = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
+                        const float2 cs = __ldg(rt + pr);
+                        const float a = x[d], b = x[d | HALF];
+                        x[d] = a * cs.x - b * cs.y;
+                        x[d | HALF] = b * cs.x + a * cs.y;
+                    }
+                }
+                if (row < g.m) {
+                    uint16_t* dst = (part == 0 ? q_out : part == 1 ? k_out : v_out) +
+                                    ((long long)bb * g.tokens + tok) * (long long)(part == 0 ? g.hq : g.hkv) * D +
+                                    (long long)head * D;
+#pragma unroll
+                    for (int c = 0; c < D; c += 8) {
+                        uint4 w;
+                        w.x = pack_bf16x2(x[c], x[c + 1]);
+                        w.y = pack_bf16x2(x[c + 2], x[c + 3]);
+                        w.z = pack_bf16x2(x[c + 4], x[c + 5]);
+                        w.w = pack_bf16x2(x[c + 6], x[c + 7]);
+                        *reinterpret_cast<uint4*>(dst + c) = w;
+                    }
+                }
+                if (hh == BN / D - 1) {
+                    // this CTA's rows of accumulator ab are read: one arrival per
+                    // warp on the leader's barrier
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(map_to_rank(bar(acc_empty[ab]), 0));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the leader's MMAs have finished with both CTAs' memory
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem, 2 * BN);
+}
+
+template <int D, int HALF, bool FP8>
+static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, const float* x_scale,
+                          const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
+                          const QkvGeom& g, cudaStream_t st) {
+    auto kern = sp_qkv_gemm_2sm<D, HALF, FP8>;
+    static unsigned attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !(attr_set & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) attr_set |= 1u << dev;
+    }
+    static int sms[32] = {0};
+    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
+    const long long ntiles = (long long)(g.n / gemm2::BN) * ((g.m + 2 * gemm2::BM - 1) / (2 * gemm2::BM));
+    long long pairs = n_sm / 2;
+    if (ntiles < pairs) pairs = ntiles;
+    if (pairs < 1) pairs = 1;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(gemm2::NTHREADS);
+    cfg.dynamicSmemBytes = gemm2::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, maps.x, maps.w, bias, (const float2*)rope, x_scale, w_scale, q, k, v, err, g);
+}
+
+template <bool FP8>
+static cudaError_t qkv2_dispatch(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                 const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                 uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    const int half = rope ? g.rope_half : 0;
+    if (d == 64) {
+        if (half == 0) return qkv2_t<64, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 16) return qkv2_t<64, 16, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 32) return qkv2_t<64, 32, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        return cudaErrorInvalidValue;
+    }
+    if (half == 0) return qkv2_t<128, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    if (half == 64) return qkv2_t<128, 64, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_qkv_gemm_2sm(int d, bool fp8, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    return fp8 ? qkv2_dispatch<true>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st)
+               : qkv2_dispatch<false>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+}
+
+}  // namespace sp

@@ -105,6 +105,7 @@ struct spl_sage {
     int device;
     int sm_count;
     int reserved_sms;  // SMs the persistent kernels leave free (spl_sage_reserve_sms)
+    int gemm_pairs;    // GEMMs on SM pairs (spl_sage_gemm_pairs)
     uint32_t* err;     // device error word of the calls that run without a workspace
 };
 
@@ -198,6 +199,7 @@ int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_
     s->sm_count = 0;
     cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, dev);
     s->reserved_sms = 0;
+    s->gemm_pairs = 1;  // measured faster at C4: bf16 1.28 -> 1.20 ms, FP8 0.81 -> 0.78 ms
     s->err = errw;
     *out = s;
     return SPL_SAGE_OK;
@@ -208,6 +210,12 @@ int spl_sage_reserve_sms(spl_sage* s, int n) {
     if (n < 0 || n >= s->sm_count)
         return fail(SPL_SAGE_ERR_INVALID, "cannot leave %d of %d SMs free", n, s->sm_count);
     s->reserved_sms = n;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_gemm_pairs(spl_sage* s, int on) {
+    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_gemm_pairs: NULL engine");
+    s->gemm_pairs = on ? 1 : 0;
     return SPL_SAGE_OK;
 }
 
@@ -617,11 +625,16 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
     int rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g);
     if (rc) return rc;
     sp::QkvMaps maps;
+    const uint32_t wbox = s->gemm_pairs ? 128 : 256;  // an SM pair loads half of a 256-channel tile per CTA
     rc = make_map_bf16_2d(&maps.x, x, g.k, g.m, (uint64_t)g.k * 2, 64, 128);
-    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, g.k, g.n, (uint64_t)g.k * 2, 64, 256);
+    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, g.k, g.n, (uint64_t)g.k * 2, 64, wbox);
     if (rc != SPL_SAGE_OK) return rc;
-    cudaError_t e = sp::launch_qkv_gemm(s->head_dim, maps, (const uint16_t*)bias, rope, (uint16_t*)q, (uint16_t*)k,
-                                        (uint16_t*)v, s->err, g, s->stream);
+    cudaError_t e = s->gemm_pairs
+                        ? sp::launch_qkv_gemm_2sm(s->head_dim, false, maps, (const uint16_t*)bias, rope, nullptr,
+                                                  nullptr, (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g,
+                                                  s->stream)
+                        : sp::launch_qkv_gemm(s->head_dim, maps, (const uint16_t*)bias, rope, (uint16_t*)q,
+                                              (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
     return SPL_SAGE_OK;
 }
@@ -635,11 +648,16 @@ int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const vo
     int rc = qkv_setup(s, shape, x8, w8, rope, q, k, v, 16, &g);
     if (rc) return rc;
     sp::QkvMaps maps;
+    const uint32_t wbox = s->gemm_pairs ? 128 : 256;
     rc = make_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, x8, g.k, g.m, (uint64_t)g.k, 128, 128);
-    if (rc == SPL_SAGE_OK) rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, g.k, g.n, (uint64_t)g.k, 128, 256);
+    if (rc == SPL_SAGE_OK) rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, g.k, g.n, (uint64_t)g.k, 128, wbox);
     if (rc != SPL_SAGE_OK) return rc;
-    cudaError_t e = sp::launch_qkv_gemm_fp8(s->head_dim, maps, (const uint16_t*)bias, rope, x_scale, w_scale,
-                                            (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
+    cudaError_t e = s->gemm_pairs
+                        ? sp::launch_qkv_gemm_2sm(s->head_dim, true, maps, (const uint16_t*)bias, rope, x_scale,
+                                                  w_scale, (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g,
+                                                  s->stream)
+                        : sp::launch_qkv_gemm_fp8(s->head_dim, maps, (const uint16_t*)bias, rope, x_scale, w_scale,
+                                                  (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch fp8 qkv gemm");
     return SPL_SAGE_OK;
 }
@@ -692,10 +710,14 @@ int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const
     g.max_ctas = max_ctas(s);
     sp::QkvMaps maps;
     int rc = make_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, x8, k, m, k, 128, 128);
-    if (rc == SPL_SAGE_OK) rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, k, n, k, 128, 256);
+    if (rc == SPL_SAGE_OK)
+        rc = make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w8, k, n, k, 128, s->gemm_pairs ? 128 : 256);
     if (rc != SPL_SAGE_OK) return rc;
-    cudaError_t e = sp::launch_qkv_gemm_fp8(128, maps, (const uint16_t*)bias, nullptr, x_scale, w_scale,
-                                            (uint16_t*)y, nullptr, nullptr, s->err, g, s->stream);
+    cudaError_t e = s->gemm_pairs ? sp::launch_qkv_gemm_2sm(128, true, maps, (const uint16_t*)bias, nullptr, x_scale,
+                                                            w_scale, (uint16_t*)y, nullptr, nullptr, s->err, g,
+                                                            s->stream)
+                                  : sp::launch_qkv_gemm_fp8(128, maps, (const uint16_t*)bias, nullptr, x_scale, w_scale,
+                                                            (uint16_t*)y, nullptr, nullptr, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch fp8 gemm");
     return SPL_SAGE_OK;
 }

@@ -83,6 +83,11 @@ cudaError_t launch_qkv_gemm(int d, const QkvMaps& maps, const uint16_t* bias, co
 cudaError_t launch_qkv_gemm_fp8(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
                                 const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
                                 uint32_t* err, const QkvGeom& g, cudaStream_t st);
+// The same GEMM on SM pairs (qkv_gemm2sm.cu): W's tensor map has a box of
+// 128 rows (each CTA of a pair loads half of a 256-channel tile).
+cudaError_t launch_qkv_gemm_2sm(int d, bool fp8, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
+                                uint32_t* err, const QkvGeom& g, cudaStream_t st);
 int qkv_smem_bytes();
 
 // LayerNorm -> per-token E4M3 (layer_norm.cu): x f32 or bf16 [rows][c].

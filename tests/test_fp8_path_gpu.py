@@ -113,13 +113,15 @@ FP8_CASES = {
 }
 
 
+@pytest.mark.parametrize("pairs", [False, True], ids=["1sm", "2sm"])
 @pytest.mark.parametrize("name", list(FP8_CASES))
-def test_fp8_qkv_gemm_matches_f64_oracle(name):
+def test_fp8_qkv_gemm_matches_f64_oracle(name, pairs):
     b, t, hidden, hq, hkv, d, rk = FP8_CASES[name]
     m, n = b * t, (hq + 2 * hkv) * d
     rng = np.random.default_rng(11)
     x, xd, gamma, beta = _ln_inputs(m, hidden, seed=3)
     eng = _engine(d)
+    eng.gemm_pairs(pairs)
     q8d = torch.zeros(m, hidden, dtype=torch.uint8, device="cuda")
     xsd = torch.zeros(m, device="cuda")
     eng.layer_norm_fp8(xd, torch.from_numpy(gamma).cuda(), torch.from_numpy(beta).cuda(), 1e-6, q8d, xsd)
@@ -207,7 +209,8 @@ def test_rows_fp8_bytes_equal_the_reference_kernel(c, ld):
         assert sc[5] == 1.0
 
 
-def test_linear_fp8_matches_f64_oracle_and_defers_scales():
+@pytest.mark.parametrize("pairs", [False, True], ids=["1sm", "2sm"])
+def test_linear_fp8_matches_f64_oracle_and_defers_scales(pairs):
     m, n, k = 300, 1024, 1024
     rng = np.random.default_rng(4)
     x8 = O.f32_to_e4m3_array(rng.normal(size=(m, k)) * 40)
@@ -215,6 +218,7 @@ def test_linear_fp8_matches_f64_oracle_and_defers_scales():
     xs = rng.uniform(0.005, 0.02, size=m).astype(np.float32)
     bias = O.f32_to_bf16(rng.normal(0, 0.1, size=n))
     eng = _engine()
+    eng.gemm_pairs(pairs)
     x8d, w8d = torch.from_numpy(x8).cuda(), torch.from_numpy(w8).cuda()
     y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     eng.linear_fp8(x8d, torch.from_numpy(xs).cuda(), w8d, torch.from_numpy(ws).cuda(), _bf16_dev(bias), y)

@@ -1,5 +1,5 @@
 """The fused QKV GEMM (spl_sage_qkv_gemm: tcgen05 bf16 GEMM + bias + RoPE
-epilogue) against the f64 oracle of the reference's GEMM + QKV prologue
+epilogue; one SM per tile, and SM pairs with cta_group::2) against the f64 oracle of the reference's GEMM + QKV prologue
 (host::linear + qkv::reference), with the reference's own tolerance for its
 GEMM (src/tests.rs:652-684: rel-RMS 4e-3 against f64, here on bf16 outputs
 5e-3), and parity at the quantiser boundary: the quantised workspace equals
@@ -53,8 +53,9 @@ CASES = {
 }
 
 
+@pytest.mark.parametrize("pairs", [False, True], ids=["1sm", "2sm"])
 @pytest.mark.parametrize("name", list(CASES))
-def test_qkv_gemm_matches_f64_oracle(name):
+def test_qkv_gemm_matches_f64_oracle(name, pairs):
     b, t, hidden, hq, hkv, d, rk = CASES[name]
     rng = np.random.default_rng(5)
     m, n = b * t, (hq + 2 * hkv) * d
@@ -71,6 +72,7 @@ def test_qkv_gemm_matches_f64_oracle(name):
     elif rk == "vggt":
         rope, half, frame = vggt_table(7, 10, 5), 16, 75
     eng = st.engine(st.Case(batch=b, heads=hq, kv_heads=hkv, tokens=t, d=d))
+    eng.gemm_pairs(pairs)
     q = torch.empty(b, t, hq, d, dtype=torch.bfloat16, device="cuda")
     k = torch.empty(b, t, hkv, d, dtype=torch.bfloat16, device="cuda")
     v = torch.empty(b, t, hkv, d, dtype=torch.bfloat16, device="cuda")
