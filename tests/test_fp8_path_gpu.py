@@ -75,12 +75,16 @@ def test_layer_norm_fp8_bytes_equal_the_reference_kernel(c, xf32):
     assert ours[1][3] == np.float32(np.abs(beta).max()) / np.float32(448.0)
 
 
-@pytest.mark.parametrize("c", [512, 4096])
-def test_layer_norm_fp8_against_the_cpu_restatement(c):
-    rows = 64
-    x, xd, gamma, beta = _ln_inputs(rows, c, seed=7)
+@pytest.mark.parametrize("c,xf32", [(512, True), (3072, False), (4096, True), (4096, False)])
+def test_layer_norm_fp8_against_the_cpu_restatement(c, xf32):
+    # 63 rows: the wide rows' kernel (two warps per row, two rows per block)
+    # then has a block whose second row is past the end
+    rows = 63
+    x, xd, gamma, beta = _ln_inputs(rows, c, seed=7, xf32=xf32)
     eng = _engine()
     q8, sc, _ = _run_ln(eng, xd, gamma, beta, 1e-5, False)
+    # the restatement reduces in one-warp order; rows wider than 2048 add two
+    # warp sums instead, which moves mean and variance in the last bits
     rq8, rsc, _ = O.layer_norm_fp8(x, gamma, beta, 1e-5)
     np.testing.assert_allclose(sc, rsc, rtol=1e-6)
     # rsqrtf against 1/sqrtf: at most one E4M3 step apart, and rarely
