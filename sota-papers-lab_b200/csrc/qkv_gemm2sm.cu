@@ -237,29 +237,52 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(acc + hh * D + c, v);
                     tmem_wait_ld();
+                    // channel scales and biases 8 at a time (16-byte loads; every
+                    // lane reads the same addresses)
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        float y = __uint_as_float(v[e]);
-                        if (FP8) {
-                            y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
-                            y = __fmul_rn(__fmul_rn(y, xs), w_scale ? __ldg(w_scale + c0 + c + e) : 1.0f);
-                            if (bias) y = __fadd_rn(y, __uint_as_float((uint32_t)bias[c0 + c + e] << 16));
-                            x[c + e] = y;
+                    for (int e8 = 0; e8 < 32; e8 += 8) {
+                        float ws[8], bs[8];
+                        if (FP8 && w_scale) {
+                            const float4 a = __ldg(reinterpret_cast<const float4*>(w_scale + c0 + c + e8));
+                            const float4 b = __ldg(reinterpret_cast<const float4*>(w_scale + c0 + c + e8 + 4));
+                            ws[0] = a.x; ws[1] = a.y; ws[2] = a.z; ws[3] = a.w;
+                            ws[4] = b.x; ws[5] = b.y; ws[6] = b.z; ws[7] = b.w;
                         } else {
-                            if (bias) y += __uint_as_float((uint32_t)bias[c0 + c + e] << 16);
-                            x[c + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) ws[e] = 1.0f;
+                        }
+                        if (bias)
+                            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(bias + c0 + c + e8)), bs);
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            float y = __uint_as_float(v[e8 + e]);
+                            if (FP8) {
+                                y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                                y = __fmul_rn(__fmul_rn(y, xs), ws[e]);
+                                if (bias) y = __fadd_rn(y, bs[e]);
+                                x[c + e8 + e] = y;
+                            } else {
+                                if (bias) y += bs[e];
+                                x[c + e8 + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                            }
                         }
                     }
                 }
                 if (HALF && part < 2) {
+                    // pairs (d, d + HALF) for the lower channels d, two table
+                    // entries per 16-byte load (consecutive d share a row)
 #pragma unroll
-                    for (int d = 0; d < D; d++) {
+                    for (int d = 0; d < D; d += 2) {
                         if (d & HALF) continue;
                         const int pr = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
-                        const float2 cs = __ldg(rt + pr);
-                        const float a = x[d], b = x[d | HALF];
+                        const float4 cs = __ldg(reinterpret_cast<const float4*>(rt + pr));
+                        float a = x[d], b = x[d | HALF];
                         x[d] = a * cs.x - b * cs.y;
                         x[d | HALF] = b * cs.x + a * cs.y;
+                        a = x[d + 1];
+                        b = x[(d + 1) | HALF];
+                        x[d + 1] = a * cs.z - b * cs.w;
+                        x[(d + 1) | HALF] = b * cs.z + a * cs.w;
                     }
                 }
                 if (row < g.m) {

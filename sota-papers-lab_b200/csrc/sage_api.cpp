@@ -624,6 +624,8 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
     sp::QkvGeom g;
     int rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g);
     if (rc) return rc;
+    if (((uintptr_t)bias | (uintptr_t)rope) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: bias and RoPE table must be 16-byte aligned");
     sp::QkvMaps maps;
     const uint32_t wbox = s->gemm_pairs ? 128 : 256;  // an SM pair loads half of a 256-channel tile per CTA
     rc = make_map_bf16_2d(&maps.x, x, g.k, g.m, (uint64_t)g.k * 2, 64, 128);
@@ -647,6 +649,8 @@ int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const vo
     sp::QkvGeom g;
     int rc = qkv_setup(s, shape, x8, w8, rope, q, k, v, 16, &g);
     if (rc) return rc;
+    if (((uintptr_t)bias | (uintptr_t)rope | (uintptr_t)w_scale) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: bias, RoPE table and weight scales must be 16-byte aligned");
     sp::QkvMaps maps;
     const uint32_t wbox = s->gemm_pairs ? 128 : 256;
     rc = make_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, x8, g.k, g.m, (uint64_t)g.k, 128, 128);
@@ -693,7 +697,7 @@ int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const
                     (long long)n);
     if (k % 16 != 0) return fail(SPL_SAGE_ERR_INVALID, "gemm: k %lld must be a multiple of 16", (long long)k);
     if (!fits_i32(m) || !fits_i32(n) || !fits_i32(k)) return fail(SPL_SAGE_ERR_INVALID, "gemm: size does not fit i32");
-    if (((uintptr_t)x8 | (uintptr_t)w8 | (uintptr_t)y) % 16)
+    if (((uintptr_t)x8 | (uintptr_t)w8 | (uintptr_t)y | (uintptr_t)bias | (uintptr_t)w_scale) % 16)
         return fail(SPL_SAGE_ERR_INVALID, "gemm: buffers must be 16-byte aligned");
     // the QKV kernel with one part of n / 128 "heads" of 128 channels and no
     // RoPE writes y row-major [m][n]
