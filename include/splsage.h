@@ -191,7 +191,8 @@ int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes);
  * q and k with pairs (d, d ^ rope_half) (16 or 32 at head dim 64, 64 at 128),
  * table row = token % frame_len.  Writes q bf16 [batch][tokens][heads][D],
  * k and v bf16 [batch][tokens][kv_heads][D].  The q, k and v widths must be
- * multiples of 256 channels. */
+ * multiples of 256 channels; every buffer, bias and RoPE table included,
+ * 16-byte aligned. */
 typedef struct {
     int64_t batch;
     int64_t tokens;
@@ -213,7 +214,8 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
  * in one tcgen05 kind::f8f6f4 GEMM.  x8 E4M3 [batch*tokens][hidden] with
  * x_scale f32 [batch*tokens] (spl_sage_layer_norm_fp8 writes both); w8 E4M3
  * [(heads + 2*kv_heads)*head_dim][hidden] with w_scale f32 per output
- * channel; hidden a multiple of 16; the rest as spl_sage_qkv_gemm. */
+ * channel (16-byte aligned); hidden a multiple of 16; the rest as
+ * spl_sage_qkv_gemm. */
 int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x8, const float* x_scale,
                           const void* w8, const float* w_scale, const void* bias, const float* rope, void* q, void* k,
                           void* v);
