@@ -2,6 +2,7 @@
 the CPU (the driver runs `pytest -m "not gpu"` without a GPU)."""
 import importlib
 import os
+import shutil
 import subprocess
 import sys
 
@@ -23,7 +24,16 @@ def _ensure_oracle():
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "liboracle.so"], check=True)
 
 
+def _ensure_library():
+    """Builds libsplsage.so (nvcc cross-compiles for sm_100a without a GPU)
+    when a fresh checkout has none; the ABI tests inspect the built file."""
+    lib = os.path.join(ROOT, "sota-papers-lab_b200", "libsplsage.so")
+    if not os.path.exists(lib) and shutil.which("nvcc"):
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "sota-papers-lab_b200", "csrc")], check=True)
+
+
 _ensure_oracle()
+_ensure_library()
 
 
 @pytest.fixture(scope="session")
