@@ -9,9 +9,11 @@
 // stage barrier, which the leader arms for both halves), warp 1 owns TMEM
 // (allocated for the pair) and, in the leader (cluster rank 0), issues the
 // MMAs, whose commits arrive on the stage and accumulator barriers of both
-// CTAs; warps 4-7 read their own CTA's accumulator (rows rank * 128 + lane)
-// and run the same epilogue as qkv_gemm.cu, then tell the leader the
-// accumulator is free.  Every mbarrier wait is bounded; both CTAs always
+// CTAs; the epilogue warps (4-11 for E4M3, 4-7 for bf16) read their own
+// CTA's accumulator (rows rank * 128 + quarter * 32 + lane; with eight,
+// warps 4-7 take channels 0-127 of the tile and warps 8-11 channels 128-255)
+// and run the epilogue of qkv_gemm.cu, then tell the leader the accumulator
+// is free.  Every mbarrier wait is bounded; both CTAs always
 // reach the closing cluster barrier, after which TMEM is freed.
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
@@ -23,7 +25,14 @@ constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 6;      // per CTA: 1
 constexpr int A_BYTES = BM * BK_BYTES, B_BYTES = (BN / 2) * BK_BYTES;  // each CTA holds half of B's rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
-constexpr int NTHREADS = 256;
+// warps 0-3 load / MMA / idle, then the epilogue warps: eight for E4M3
+// (whose MMAs are fast enough for a four-warp epilogue to hold them up), four
+// for bf16 (C4: FP8 0.689 ms with eight, 0.722 with four; bf16 1.184 ms
+// with four, 1.200 with eight)
+template <bool FP8>
+constexpr int epilogue_warps() { return FP8 ? 8 : 4; }
+template <bool FP8>
+constexpr int nthreads() { return 128 + 32 * epilogue_warps<FP8>(); }
 }  // namespace gemm2
 
 namespace {
@@ -98,7 +107,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 }  // namespace
 
 template <int D, int HALF, bool FP8>
-__global__ void __launch_bounds__(gemm2::NTHREADS, 1)
+__global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
     sp_qkv_gemm_2sm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                     const uint16_t* __restrict__ bias, const float2* __restrict__ rope,
                     const float* __restrict__ x_scale, const float* __restrict__ w_scale, uint16_t* __restrict__ q_out,
@@ -131,7 +140,7 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(acc_full[i]), 1);
-            mbar_init(bar(acc_empty[i]), 8);  // four epilogue warps of each CTA (leader's barrier)
+            mbar_init(bar(acc_empty[i]), 2 * epilogue_warps<FP8>());  // epilogue warps of both CTAs
         }
         mbar_init(bar(done), 1);
         fence_barrier_init();
@@ -203,9 +212,17 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
             mbar_wait(bar(done), 0, err, 53, false);
         }
     } else if (warp >= 4) {
-        // ------------------------------------------------------------ epilogue, one thread per row
-        const int r = tid - 128;
-        const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+        // ------------------------------------------------------------ epilogue
+        // with eight epilogue warps, warps 4-7 take the tile's channels
+        // 0-127 and warps 8-11 channels 128-255 (with four, warps 4-7 take
+        // all); a warp reads its own TMEM lane quarter (warp % 4), one thread
+        // per row.  Columns go through 32 at a time, with their RoPE partners
+        // (d + HALF) when HALF >= 32, so that only 64 floats are live.
+        constexpr int EPW = epilogue_warps<FP8>();
+        constexpr int HEADS = (EPW == 8 ? BN / 2 : BN) / D;  // heads per epilogue warp
+        const int quarter = warp & 3, chalf = EPW == 8 ? (warp - 4) >> 2 : 0;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         bool ok = true;
         for (int t = pair, it = 0; t < ntiles && ok; t += npairs, it++) {
             const int ab = it & 1;
@@ -218,7 +235,7 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
             const float xs = FP8 && x_scale && row < g.m ? __ldg(x_scale + row) : 1.0f;
             const float2* rt = HALF ? rope + (long long)(tok % g.frame_len) * (D / 2) : nullptr;
 #pragma unroll 1
-            for (int hh = 0; hh < BN / D; hh++) {
+            for (int hh = chalf * HEADS; hh < (chalf + 1) * HEADS; hh++) {
                 const int c0 = n0 + hh * D;
                 int part, head;
                 if (c0 < g.hq * D) {
@@ -231,14 +248,14 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
                     part = 2;
                     head = (c0 - (g.hq + g.hkv) * D) / D;
                 }
-                float x[D];
-#pragma unroll
-                for (int c = 0; c < D; c += 32) {
+                uint16_t* dst = (part == 0 ? q_out : part == 1 ? k_out : v_out) +
+                                ((long long)bb * g.tokens + tok) * (long long)(part == 0 ? g.hq : g.hkv) * D +
+                                (long long)head * D;
+                // columns c .. c+31 of the head: GEMM output, scales, bias
+                auto load = [&](int c, float (&x)[32]) {
                     uint32_t v[32];
                     tmem_ld32(acc + hh * D + c, v);
                     tmem_wait_ld();
-                    // channel scales and biases 8 at a time (16-byte loads; every
-                    // lane reads the same addresses)
 #pragma unroll
                     for (int e8 = 0; e8 < 32; e8 += 8) {
                         float ws[8], bs[8];
@@ -260,53 +277,72 @@ __global__ void __launch_bounds__(gemm2::NTHREADS, 1)
                                 y = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
                                 y = __fmul_rn(__fmul_rn(y, xs), ws[e]);
                                 if (bias) y = __fadd_rn(y, bs[e]);
-                                x[c + e8 + e] = y;
+                                x[e8 + e] = y;
                             } else {
                                 if (bias) y += bs[e];
-                                x[c + e8 + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                                x[e8 + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
                             }
                         }
                     }
-                }
-                if (HALF && part < 2) {
-                    // pairs (d, d + HALF) for the lower channels d, two table
-                    // entries per 16-byte load (consecutive d share a row)
+                };
+                auto store = [&](int c, const float (&x)[32]) {
+                    if (row >= g.m) return;
 #pragma unroll
-                    for (int d = 0; d < D; d += 2) {
-                        if (d & HALF) continue;
-                        const int pr = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
-                        const float4 cs = __ldg(reinterpret_cast<const float4*>(rt + pr));
-                        float a = x[d], b = x[d | HALF];
-                        x[d] = a * cs.x - b * cs.y;
-                        x[d | HALF] = b * cs.x + a * cs.y;
-                        a = x[d + 1];
-                        b = x[(d + 1) | HALF];
-                        x[d + 1] = a * cs.z - b * cs.w;
-                        x[(d + 1) | HALF] = b * cs.z + a * cs.w;
-                    }
-                }
-                if (row < g.m) {
-                    uint16_t* dst = (part == 0 ? q_out : part == 1 ? k_out : v_out) +
-                                    ((long long)bb * g.tokens + tok) * (long long)(part == 0 ? g.hq : g.hkv) * D +
-                                    (long long)head * D;
-#pragma unroll
-                    for (int c = 0; c < D; c += 8) {
+                    for (int e = 0; e < 32; e += 8) {
                         uint4 w;
-                        w.x = pack_bf16x2(x[c], x[c + 1]);
-                        w.y = pack_bf16x2(x[c + 2], x[c + 3]);
-                        w.z = pack_bf16x2(x[c + 4], x[c + 5]);
-                        w.w = pack_bf16x2(x[c + 6], x[c + 7]);
-                        *reinterpret_cast<uint4*>(dst + c) = w;
+                        w.x = pack_bf16x2(x[e], x[e + 1]);
+                        w.y = pack_bf16x2(x[e + 2], x[e + 3]);
+                        w.z = pack_bf16x2(x[e + 4], x[e + 5]);
+                        w.w = pack_bf16x2(x[e + 6], x[e + 7]);
+                        *reinterpret_cast<uint4*>(dst + c + e) = w;
                     }
-                }
-                if (hh == BN / D - 1) {
-                    // this CTA's rows of accumulator ab are read: one arrival per
-                    // warp on the leader's barrier
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(map_to_rank(bar(acc_empty[ab]), 0));
+                };
+                // RoPE on (a, b) with the table entries of channels d, d + 1
+                auto rot2 = [&](int d, float& a0, float& b0, float& a1, float& b1) {
+                    const int pr = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
+                    const float4 cs = __ldg(reinterpret_cast<const float4*>(rt + pr));
+                    float a = a0, b = b0;
+                    a0 = a * cs.x - b * cs.y;
+                    b0 = b * cs.x + a * cs.y;
+                    a = a1;
+                    b = b1;
+                    a1 = a * cs.z - b * cs.w;
+                    b1 = b * cs.z + a * cs.w;
+                };
+                if (HALF >= 32) {
+                    // chunk c and its partner chunk c + HALF
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 32) {
+                        if (c & HALF) continue;
+                        float xa[32], xb[32];
+                        load(c, xa);
+                        load(c + HALF, xb);
+                        if (part < 2) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) rot2(c + i, xa[i], xb[i], xa[i + 1], xb[i + 1]);
+                        }
+                        store(c, xa);
+                        store(c + HALF, xb);
+                    }
+                } else {
+                    // no RoPE, or pairs (d, d + 16) inside each 32-channel chunk
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 32) {
+                        float xa[32];
+                        load(c, xa);
+                        if (HALF && part < 2) {
+#pragma unroll
+                            for (int i = 0; i < HALF; i += 2) rot2(c + i, xa[i], xa[i + HALF], xa[i + 1], xa[i + HALF + 1]);
+                        }
+                        store(c, xa);
+                    }
                 }
             }
+            // this CTA's rows of accumulator ab are read (this warp's half):
+            // one arrival per warp on the leader's barrier
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_rank(bar(acc_empty[ab]), 0));
         }
     }
     tc_fence_before();
@@ -340,7 +376,7 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof cfg);
     cfg.gridDim = dim3((unsigned)(2 * pairs));
-    cfg.blockDim = dim3(gemm2::NTHREADS);
+    cfg.blockDim = dim3(gemm2::nthreads<FP8>());
     cfg.dynamicSmemBytes = gemm2::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
