@@ -341,6 +341,30 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
                        int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse);
 int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out);
 
+/* The whole ring in one call, for hosts that hold their own NCCL
+ * communicator (the `spl_sage_ring_forward(..., ncclComm_t, rank, world)` of
+ * the drop-in boundary).  No counterpart in the reference.
+ * spl_sage_ring_create: this rank's state for `local` (batch, heads,
+ * kv_heads, tokens = this rank's tokens, two zig-zag chunks: chunks rank and
+ * 2*world-1-rank of 2*world; a multiple of 256), its workspace, two K/V
+ * buffers, the fp32 accumulator, a stream for the exchange; allocates.
+ * reserved_sms: SMs the attention leaves free during the ring steps for
+ * NCCL's kernel (create the communicator with ncclConfig_t.maxCTAs no larger;
+ * 1 and 1 measured best on 8 B200s).
+ * spl_sage_ring_forward: steps 1-5 above with the statistics all-reduced
+ * (sum, max) and the K/V passed to rank + 1 over `nccl_comm` (an ncclComm_t
+ * of `world` ranks, this process being `rank`; NULL when world = 1), one
+ * attention launch per ring step; q, k, v and out hold this rank's tokens.
+ * Stream-ordered on the engine's stream (the exchange runs on the ring's
+ * own stream, ordered with it by events).  NCCL is looked up in the running
+ * process, or loaded as libnccl.so.2; the library does not link it. */
+typedef struct spl_sage_ring spl_sage_ring;
+int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int world, int reserved_sms,
+                         spl_sage_ring** out);
+void spl_sage_ring_destroy(spl_sage_ring* r);
+int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                          spl_sage_tensor_mut out, const spl_sage_options* opts, void* nccl_comm);
+
 /* Tensor-core peak probe (the analog of the reference's sage_peak kernels,
  * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
  * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n

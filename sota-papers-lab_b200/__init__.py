@@ -96,7 +96,8 @@ EXPORTS = [
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
-    "spl_sage_linear_fp8", "spl_sage_gemm_pairs",
+    "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
+    "spl_sage_ring_forward",
 ]
 
 # spl_sage_cp_attend flags
@@ -122,6 +123,9 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_destroy.argtypes = [P]
         L.spl_sage_reserve_sms.argtypes = [P, I]
         L.spl_sage_gemm_pairs.argtypes = [P, I]
+        L.spl_sage_ring_create.argtypes = [P, ctypes.POINTER(_Shape), I, I, I, ctypes.POINTER(P)]
+        L.spl_sage_ring_destroy.argtypes = [P]
+        L.spl_sage_ring_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
         L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
         L.spl_sage_ws_destroy.argtypes = [P]
         L.spl_sage_ws_bytes.restype = ctypes.c_int64
@@ -544,6 +548,36 @@ class SageAttention:
         w = ctypes.c_uint32()
         _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
         return w.value
+
+
+class NativeRing:
+    """One rank of the context-parallel ring driven inside the library
+    (spl_sage_ring_create / _forward): the schedule of
+    ring.RingAttention, over a caller's NCCL communicator (an ncclComm_t as
+    an integer; 0 when world = 1)."""
+
+    def __init__(self, eng: "SageAttention", batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int,
+                 world: int, reserved_sms: int = 1):
+        cs = _Shape(batch, heads, kv_heads, local_tokens, 0, 0)
+        h = ctypes.c_void_p()
+        _check(lib().spl_sage_ring_create(eng._h, ctypes.byref(cs), rank, world, reserved_sms, ctypes.byref(h)))
+        self._h, self.eng = h, eng
+
+    def forward(self, q: Tensor, k: Tensor, v: Tensor, out: Tensor, opts: Options | None = None, comm: int = 0):
+        o = (opts or Options())._c()
+        _check(lib().spl_sage_ring_forward(self.eng._h, self._h, q._c(), k._c(), v._c(), out._c(), ctypes.byref(o),
+                                           ctypes.c_void_p(comm)))
+
+    def close(self):
+        if self._h:
+            lib().spl_sage_ring_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class KvBuffer:

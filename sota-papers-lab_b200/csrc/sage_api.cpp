@@ -3,6 +3,8 @@
 // reference's checks and error texts; all GPU work is stream-ordered.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types and prototypes only: the functions are looked up at run time
 
 #include <cmath>
 #include <cstdarg>
@@ -1025,6 +1027,235 @@ int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl
     cudaError_t e = sp::launch_cp_finish(s->head_dim, acc, g, out.data, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage context-parallel finish");
     return SPL_SAGE_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- ring attention over NCCL
+
+namespace {
+
+// The NCCL functions the ring calls, looked up in the running process (a
+// host that already loaded NCCL, e.g. through torch, shares its copy) or in
+// libnccl.so.2; the library itself does not link NCCL.
+struct NcclFns {
+    decltype(&ncclAllReduce) all_reduce;
+    decltype(&ncclSend) send;
+    decltype(&ncclRecv) recv;
+    decltype(&ncclGroupStart) group_start;
+    decltype(&ncclGroupEnd) group_end;
+    decltype(&ncclGetErrorString) error_string;
+};
+
+const NcclFns* nccl_fns() {
+    static NcclFns f;
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = RTLD_DEFAULT;
+        if (!dlsym(h, "ncclSend")) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        f.all_reduce = (decltype(f.all_reduce))dlsym(h, "ncclAllReduce");
+        f.send = (decltype(f.send))dlsym(h, "ncclSend");
+        f.recv = (decltype(f.recv))dlsym(h, "ncclRecv");
+        f.group_start = (decltype(f.group_start))dlsym(h, "ncclGroupStart");
+        f.group_end = (decltype(f.group_end))dlsym(h, "ncclGroupEnd");
+        f.error_string = (decltype(f.error_string))dlsym(h, "ncclGetErrorString");
+        ok = f.all_reduce && f.send && f.recv && f.group_start && f.group_end && f.error_string;
+    });
+    return ok ? &f : nullptr;
+}
+
+int nccl_fail(const NcclFns* f, ncclResult_t r, const char* what) {
+    return fail(SPL_SAGE_ERR_CUDA, "%s: %s", what, f->error_string(r));
+}
+
+}  // namespace
+
+struct spl_sage_ring {
+    int rank, world, reserved_sms;
+    int64_t batch, heads, kv_heads, tokens, chunk;
+    spl_sage_ws* ws;
+    spl_sage_kv* kv[2];
+    void* kv_mem[2];
+    int64_t k8_bytes, ks_bytes, v8_bytes;
+    float* acc;
+    float* lse;
+    float* raw;  // [bg][4][D], then raw_sum and raw_max after it
+    cudaStream_t comm;
+    cudaEvent_t ev_compute, ev_comm;
+};
+
+extern "C" {
+
+void spl_sage_ring_destroy(spl_sage_ring* r) {
+    if (!r) return;
+    for (int i = 0; i < 2; i++) {
+        spl_sage_kv_destroy(r->kv[i]);
+        cudaFree(r->kv_mem[i]);
+    }
+    cudaFree(r->acc);
+    cudaFree(r->lse);
+    cudaFree(r->raw);
+    if (r->comm) cudaStreamDestroy(r->comm);
+    if (r->ev_compute) cudaEventDestroy(r->ev_compute);
+    if (r->ev_comm) cudaEventDestroy(r->ev_comm);
+    spl_sage_ws_destroy(r->ws);
+    delete r;
+}
+
+int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int world, int reserved_sms,
+                         spl_sage_ring** out) {
+    if (!s || !local || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_create: NULL argument");
+    *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world)
+        return fail(SPL_SAGE_ERR_INVALID, "ring: rank %d of %d ranks", rank, world);
+    if (local->tokens <= 0 || local->tokens % 256)
+        return fail(SPL_SAGE_ERR_INVALID,
+                    "ring: each rank's %lld tokens must be two chunks of whole 128-token tiles",
+                    (long long)local->tokens);
+    if (reserved_sms < 0 || reserved_sms >= s->sm_count)
+        return fail(SPL_SAGE_ERR_INVALID, "ring: cannot leave %d of %d SMs free", reserved_sms, s->sm_count);
+    spl_sage_ring* r = new spl_sage_ring;
+    memset(r, 0, sizeof *r);
+    r->rank = rank;
+    r->world = world;
+    r->reserved_sms = world > 1 ? reserved_sms : 0;
+    spl_sage_shape sh = *local;
+    sh.causal = 0;
+    if (sh.kv_heads == 0) sh.kv_heads = sh.heads;
+    r->batch = sh.batch;
+    r->heads = sh.heads;
+    r->kv_heads = sh.kv_heads;
+    r->tokens = sh.tokens;
+    r->chunk = sh.tokens / 2;
+    int rc = spl_sage_workspace_create(s, &sh, nullptr, &r->ws);
+    if (rc) {
+        delete r;
+        return rc;
+    }
+    spl_sage_kv_bytes(r->ws, &r->k8_bytes, &r->ks_bytes, &r->v8_bytes);
+    const int64_t D = s->head_dim;
+    const size_t k8o = 0, kso = ((size_t)r->k8_bytes + 255) & ~(size_t)255;
+    const size_t v8o = (kso + (size_t)r->ks_bytes + 255) & ~(size_t)255;
+    const size_t kv_total = v8o + (size_t)r->v8_bytes;
+    const size_t acc_n = (size_t)(r->batch * r->tokens * r->heads * D);
+    const size_t lse_n = (size_t)(r->batch * r->heads * r->tokens);
+    const size_t raw_n = (size_t)(r->batch * r->kv_heads * 4 * D);
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 2 && e == cudaSuccess; i++) e = cudaMalloc(&r->kv_mem[i], kv_total);
+    if (e == cudaSuccess) e = cudaMalloc(&r->acc, acc_n * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&r->lse, lse_n * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&r->raw, 3 * raw_n * 4);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&r->comm, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_compute, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_comm, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        spl_sage_ring_destroy(r);
+        return cuda_fail(e, "allocate the ring's buffers");
+    }
+    for (int i = 0; i < 2; i++) {
+        uint8_t* m = (uint8_t*)r->kv_mem[i];
+        rc = spl_sage_kv_create(s, r->ws, m + k8o, (float*)(m + kso), m + v8o, &r->kv[i]);
+        if (rc) {
+            spl_sage_ring_destroy(r);
+            return rc;
+        }
+    }
+    *out = r;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
+                          spl_sage_tensor_mut out, const spl_sage_options* opts, void* nccl_comm) {
+    if (!s || !r) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_forward: NULL argument");
+    const NcclFns* nc = nullptr;
+    if (r->world > 1) {
+        if (!nccl_comm) return fail(SPL_SAGE_ERR_INVALID, "ring: %d ranks need an NCCL communicator", r->world);
+        if (!(nc = nccl_fns()))
+            return fail(SPL_SAGE_ERR_CUDA, "ring: NCCL is not loaded and libnccl.so.2 could not be opened");
+    }
+    ncclComm_t comm = (ncclComm_t)nccl_comm;
+    const int64_t D = s->head_dim, C = r->chunk, P = r->world, rank = r->rank;
+    const int bg = (int)(r->batch * r->kv_heads);
+    const size_t raw_n = (size_t)bg * 4 * (size_t)D;
+    // 1. this rank's Q quantised and its raw K/V statistics
+    int rc = spl_sage_cp_prepare(s, r->ws, q, k, v, opts, r->raw);
+    if (rc) return rc;
+    // 2. the statistics of the whole sequence
+    if (P > 1) {
+        float* rsum = r->raw + raw_n;
+        float* rmax = r->raw + 2 * raw_n;
+        ncclResult_t nr = nc->all_reduce(r->raw, rsum, raw_n, ncclFloat32, ncclSum, comm, s->stream);
+        if (nr == ncclSuccess) nr = nc->all_reduce(r->raw, rmax, raw_n, ncclFloat32, ncclMax, comm, s->stream);
+        if (nr != ncclSuccess) return nccl_fail(nc, nr, "ring: statistics all-reduce");
+        cudaError_t e = sp::launch_cp_merge_stats(rsum, rmax, r->raw, bg, (int)D, s->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "launch the statistics merge");
+    }
+    // 3. this rank's K/V quantised with them
+    rc = spl_sage_cp_quantize_kv(s, r->ws, k, v, opts, r->raw, r->tokens * P, r->kv[0]);
+    if (rc) return rc;
+    // 4. P steps, one segment launch each, the K/V moving one rank on meanwhile
+    const int keep = s->reserved_sms;
+    s->reserved_sms = r->reserved_sms;
+    int cur = 0;
+    const int next = (int)((rank + 1) % P), prev = (int)((rank + P - 1) % P);
+    for (int64_t step = 0; step < P && rc == SPL_SAGE_OK; step++) {
+        const int64_t src = (rank - step + P) % P;
+        const bool pass_on = step + 1 < P;
+        if (pass_on) {
+            // the buffer received into was read by the previous step
+            cudaError_t e = cudaEventRecord(r->ev_compute, s->stream);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(r->comm, r->ev_compute, 0);
+            if (e != cudaSuccess) {
+                rc = cuda_fail(e, "order the ring exchange");
+                break;
+            }
+            ncclResult_t nr = nc->group_start();
+            uint8_t* snd = (uint8_t*)r->kv_mem[cur];
+            uint8_t* rcv = (uint8_t*)r->kv_mem[1 - cur];
+            const size_t total = ((((size_t)r->k8_bytes + 255) & ~(size_t)255) + (size_t)r->ks_bytes + 255) &
+                                 ~(size_t)255;
+            const size_t bytes = total + (size_t)r->v8_bytes;  // the whole buffer: k8, k_scale, v8
+            if (nr == ncclSuccess) nr = nc->send(snd, bytes, ncclUint8, next, comm, r->comm);
+            if (nr == ncclSuccess) nr = nc->recv(rcv, bytes, ncclUint8, prev, comm, r->comm);
+            const ncclResult_t ng = nc->group_end();
+            if (nr == ncclSuccess) nr = ng;
+            if (nr != ncclSuccess) {
+                rc = nccl_fail(nc, nr, "ring: K/V exchange");
+                break;
+            }
+            e = cudaEventRecord(r->ev_comm, r->comm);
+            if (e != cudaSuccess) {
+                rc = cuda_fail(e, "record the ring exchange");
+                break;
+            }
+        }
+        // the step's chunk pairs as one segment: step 0 the rank's own tokens,
+        // causal, writing the accumulator; from a rank before this one both
+        // query chunks against its first key chunk; from a rank after it the
+        // second query chunk against both key chunks
+        int64_t qb = 0, ql = 2 * C, kb = 0, kl = 2 * C;
+        int flags = 0;
+        if (step == 0) {
+            flags = SPL_SAGE_CP_CAUSAL | SPL_SAGE_CP_FIRST;
+        } else if (src < rank) {
+            kl = C;
+        } else {
+            qb = C;
+            ql = C;
+        }
+        rc = spl_sage_cp_attend(s, r->ws, r->kv[cur], qb, ql, kb, kl, flags, r->acc, r->lse);
+        if (rc == SPL_SAGE_OK && pass_on) {
+            cudaError_t e = cudaStreamWaitEvent(s->stream, r->ev_comm, 0);
+            if (e != cudaSuccess) rc = cuda_fail(e, "wait for the ring exchange");
+            cur = 1 - cur;
+        }
+    }
+    s->reserved_sms = keep;
+    if (rc) return rc;
+    // 5. the accumulator to bf16
+    return spl_sage_cp_finish(s, r->ws, r->acc, out);
 }
 
 }  // extern "C"

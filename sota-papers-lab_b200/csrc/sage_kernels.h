@@ -116,6 +116,8 @@ cudaError_t launch_cp_prepare(int d, const void* q, const void* k, const void* v
 cudaError_t launch_cp_quant_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
                                const Geom& g, const float* raw, float total, cudaStream_t st);
 cudaError_t launch_cp_finish(int d, const float* acc, const Geom& g, void* out, cudaStream_t st);
+// raw [bg][4][D] = sums from rsum (entries 0-1), maxima from rmax (2-3).
+cudaError_t launch_cp_merge_stats(const float* rsum, const float* rmax, float* raw, int bg, int d, cudaStream_t st);
 // Segment attention merged into acc f32 (strides g.o_*) and lse f32
 // [b][h][tokens] (log2 of the row's softmax denominator) by log-sum-exp.
 cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, float* acc,

@@ -626,6 +626,22 @@ cudaError_t launch_cp_quant_kv(int d, const void* k, const void* v, const float*
                    : cp_quant_kv_d<128>(k, v, ln, buf, g, raw, total, st);
 }
 
+// raw [bg][4][D] from the ranks' combined statistics: entries 0-1 (sums)
+// from the SUM all-reduce, 2-3 (-min V, max V) from the MAX all-reduce.
+__global__ void __launch_bounds__(256) sp_cp_merge_stats(const float* __restrict__ rsum,
+                                                         const float* __restrict__ rmax, float* __restrict__ raw,
+                                                         int bg, int d) {
+    const int n = bg * 4 * d;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        raw[i] = ((i / d) & 3) < 2 ? rsum[i] : rmax[i];
+}
+
+cudaError_t launch_cp_merge_stats(const float* rsum, const float* rmax, float* raw, int bg, int d, cudaStream_t st) {
+    const int n = bg * 4 * d;
+    sp_cp_merge_stats<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, st>>>(rsum, rmax, raw, bg, d);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_cp_finish(int d, const float* acc, const Geom& g, void* out, cudaStream_t st) {
     const long long n8 = (long long)g.batch * g.tokens * g.heads * (d / 8);
     const long long want = (n8 + 255) / 256;
