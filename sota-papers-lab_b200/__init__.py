@@ -17,6 +17,7 @@ module refuses to load without the built library.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from dataclasses import dataclass, field
 
@@ -636,6 +637,73 @@ def rope_table_1d(base: float, head_dim: int, positions: int):
     out = np.empty((positions, head_dim // 2, 2), np.float32)
     _check(lib().spl_sage_rope_table_1d(base, head_dim, positions, out.ctypes.data_as(ctypes.c_void_p)))
     return out
+
+
+class RopeLayout:
+    """Which channels rotate together (qkv.rs:36-61): channel c pairs with
+    c ^ half and reads angle row pair(c) = (c / 2·half)·half + c % half.
+    VGGT: half 16 (channels 0-31 by row position, 32-63 by column); DINOv3:
+    half 32; a 1-D (Llama) table over D channels: half D/2.  The QKV GEMMs
+    take `half` as their `rope_half` argument."""
+    VGGT = 16
+    DINOV3 = 32
+
+    @staticmethod
+    def one_d(head_dim: int) -> int:
+        return head_dim // 2
+
+    @staticmethod
+    def pair(half: int, c: int) -> int:
+        return (c // (2 * half)) * half + c % half
+
+
+class RopeTable:
+    """cos / sin per (token of a frame, pair), as the QKV epilogue reads
+    them: `cos_sin` f32 [frame_len][D/2][2] (RopeTable, qkv.rs:63-131).
+    Angles are taken in f64 and their cos / sin stored as f32."""
+
+    def __init__(self, half: int, cos_sin):
+        self.half = half
+        self.cos_sin = cos_sin
+        self.frame_len = cos_sin.shape[0]
+
+    @classmethod
+    def from_angles(cls, half: int, frame_len: int, pairs: int, angle):
+        """qkv.rs:75-96: `angle(token, pair)` in radians."""
+        import numpy as np
+        a = np.array([[angle(t, p) for p in range(pairs)] for t in range(frame_len)], np.float64).reshape(
+            frame_len, pairs)
+        return cls(half, np.stack([np.cos(a), np.sin(a)], -1).astype(np.float32))
+
+    @classmethod
+    def vggt(cls, grid_h: int, grid_w: int, special: int, base: float = 100.0):
+        """qkv.rs:98-110: `special` leading tokens unrotated, then a grid at
+        positions (y + 1, x + 1); pair i of each 16-pair half at frequency
+        base^(-i/16) (D = 64)."""
+        def angle(t, p):
+            if t < special:
+                return 0.0
+            y, x = divmod(t - special, grid_w)
+            return float((y + 1) if p < 16 else (x + 1)) * base ** (-(p % 16) / 16.0)
+        return cls.from_angles(RopeLayout.VGGT, special + grid_h * grid_w, 32, angle)
+
+    @classmethod
+    def dinov3(cls, grid_h: int, grid_w: int, special: int, base: float = 100.0):
+        """qkv.rs:112-128: patch coordinates normalised to [-1, 1] per axis,
+        period base^(j/16) for pair j of each axis (D = 64)."""
+        def angle(t, p):
+            if t < special:
+                return 0.0
+            y, x = divmod(t - special, grid_w)
+            coord = (y + 0.5) / grid_h * 2.0 - 1.0 if p < 16 else (x + 0.5) / grid_w * 2.0 - 1.0
+            return 2.0 * math.pi * coord / base ** ((p % 16) / 16.0)
+        return cls.from_angles(RopeLayout.DINOV3, special + grid_h * grid_w, 32, angle)
+
+    @classmethod
+    def one_d(cls, base: float, head_dim: int, positions: int):
+        """Llama-style 1-D positions 0..positions-1, frequency
+        base^(-p/(D/2)) for pair p (spl_sage_rope_table_1d)."""
+        return cls(RopeLayout.one_d(head_dim), rope_table_1d(base, head_dim, positions))
 
 
 def flops(plan: Plan, head_dim: int) -> float:

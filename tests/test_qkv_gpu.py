@@ -4,7 +4,8 @@ epilogue; one SM per tile, and SM pairs with cta_group::2) against the f64 oracl
 GEMM (src/tests.rs:652-684: rel-RMS 4e-3 against f64, here on bf16 outputs
 5e-3), and parity at the quantiser boundary: the quantised workspace equals
 the oracle quantiser applied to the bf16 Q/K/V the GEMM wrote, bit for bit."""
-import math
+
+import importlib
 
 import numpy as np
 import pytest
@@ -14,6 +15,7 @@ import sagetest as st
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
+sage = importlib.import_module("sota-papers-lab_b200")
 
 
 def _bf16(a):
@@ -26,23 +28,6 @@ def _dev(bits):
 
 def _host(t):
     return O.bf16_to_f32(t.view(torch.int16).cpu().numpy().view(np.uint16))
-
-
-def vggt_table(grid_h, grid_w, special, base=100.0):
-    # RopeTable::vggt (qkv.rs:98-110): pairs (i, i+16) in each 32-wide half
-    rows = []
-    for t in range(special + grid_h * grid_w):
-        row = []
-        for p in range(32):
-            if t < special:
-                a = 0.0
-            else:
-                y, x = (t - special) // grid_w, (t - special) % grid_w
-                pos = (y + 1) if p < 16 else (x + 1)
-                a = pos * base ** (-(p % 16) / 16.0)
-            row.append([math.cos(a), math.sin(a)])
-        rows.append(row)
-    return np.array(rows, np.float32)
 
 
 CASES = {
@@ -66,11 +51,10 @@ def test_qkv_gemm_matches_f64_oracle(name, pairs):
     bias = _bf16(rng.normal(0, 0.1, size=n))
     rope, half, frame = None, 0, 1
     if rk == "llama":
-        import importlib
-        sage = importlib.import_module("sota-papers-lab_b200")
         rope, half, frame = sage.rope_table_1d(500000.0, d, t), d // 2, t
     elif rk == "vggt":
-        rope, half, frame = vggt_table(7, 10, 5), 16, 75
+        tab = sage.RopeTable.vggt(7, 10, 5)
+        rope, half, frame = tab.cos_sin, tab.half, tab.frame_len
     eng = st.engine(st.Case(batch=b, heads=hq, kv_heads=hkv, tokens=t, d=d))
     eng.gemm_pairs(pairs)
     q = torch.empty(b, t, hq, d, dtype=torch.bfloat16, device="cuda")
@@ -94,8 +78,6 @@ def test_qkv_gemm_quant_is_the_quantiser_on_its_own_output():
     rng = np.random.default_rng(9)
     m, n = b * t, (hq + 2 * hkv) * d
     xb, wb = _bf16(rng.normal(size=(m, hidden))), _bf16(rng.normal(0, 0.02, size=(n, hidden)))
-    import importlib
-    sage = importlib.import_module("sota-papers-lab_b200")
     rope = sage.rope_table_1d(500000.0, d, t)
     c = st.Case(batch=b, heads=hq, kv_heads=hkv, tokens=t, d=d, causal=True, packed=False)
     eng = st.engine(c)
