@@ -145,6 +145,12 @@ int spl_sage_gemm_pairs(spl_sage* s, int on);
 int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
                               spl_sage_ws** out);
 void spl_sage_ws_destroy(spl_sage_ws* ws);
+/* Plan::new (mod.rs:405-440): the padded query and key counts of a shape
+ * and key merge, with the same checks (empty shape, merge stride 2 or 4, a
+ * patch grid, a frame layout covering the sequence, i32 limits) and the
+ * same error texts; merge NULL or stride <= 1 = dense.  Host only: needs no
+ * engine and no GPU.  spl_sage_workspace_create applies it first. */
+int spl_sage_plan_new(const spl_sage_shape* shape, const spl_sage_merge* merge, spl_sage_plan* out);
 /* Workspace::bytes (mod.rs:485-494) and Workspace::plan (mod.rs:480-482). */
 int64_t spl_sage_ws_bytes(const spl_sage_ws* ws);
 int spl_sage_ws_plan(const spl_sage_ws* ws, spl_sage_plan* out);

@@ -98,7 +98,7 @@ EXPORTS = [
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
     "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
-    "spl_sage_ring_forward",
+    "spl_sage_ring_forward", "spl_sage_plan_new",
 ]
 
 # spl_sage_cp_attend flags
@@ -132,6 +132,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_ws_bytes.restype = ctypes.c_int64
         L.spl_sage_ws_bytes.argtypes = [P]
         L.spl_sage_ws_plan.argtypes = [P, ctypes.POINTER(_Plan)]
+        L.spl_sage_plan_new.argtypes = [ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(_Plan)]
         L.spl_sage_prepare.argtypes = [P, P, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options)]
         L.spl_sage_attend.argtypes = [P, P, _Tensor]
         L.spl_sage_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options)]
@@ -308,6 +309,13 @@ class Options:
         return o
 
 
+def _merge_c(merge: "KvMerge") -> _Merge:
+    if merge.stride > 1:
+        lay = merge.layout
+        return _Merge(merge.stride, 0, lay.frames, lay.special, lay.grid_h, lay.grid_w, lay.dense_frames)
+    return _Merge()
+
+
 @dataclass(frozen=True)
 class Plan:
     """mod.rs:391-454."""
@@ -316,6 +324,21 @@ class Plan:
     tq_pad: int
     tk: int
     tk_pad: int
+
+    @classmethod
+    def new(cls, shape: Shape, merge: KvMerge | None = None) -> "Plan":
+        """Plan::new (mod.rs:405-440): the sizes that follow from a shape and
+        a key merge, with the same checks (spl_sage_plan_new; host only)."""
+        merge = merge or KvMerge.dense()
+        cs = _Shape(shape.batch, shape.heads, shape.kv_heads, shape.tokens, int(shape.causal), 0)
+        cm = _merge_c(merge)
+        p = _Plan()
+        _check(lib().spl_sage_plan_new(ctypes.byref(cs), ctypes.byref(cm), ctypes.byref(p)))
+        return cls(shape, merge, p.tq_pad, p.tk, p.tk_pad)
+
+    def key_ratio(self) -> float:
+        """Keys after merging per key before (mod.rs:443-445)."""
+        return self.tk / self.shape.tokens
 
 
 @dataclass
@@ -485,10 +508,7 @@ class SageAttention:
     def workspace(self, shape: Shape, merge: KvMerge | None = None) -> Workspace:
         merge = merge or KvMerge.dense()
         cs = _Shape(shape.batch, shape.heads, shape.kv_heads, shape.tokens, int(shape.causal), 0)
-        cm = _Merge()
-        if merge.stride > 1:
-            lay = merge.layout
-            cm = _Merge(merge.stride, 0, lay.frames, lay.special, lay.grid_h, lay.grid_w, lay.dense_frames)
+        cm = _merge_c(merge)
         h = ctypes.c_void_p()
         _check(lib().spl_sage_workspace_create(self._h, ctypes.byref(cs), ctypes.byref(cm), ctypes.byref(h)))
         p = _Plan()

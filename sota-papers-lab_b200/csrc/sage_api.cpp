@@ -227,10 +227,8 @@ void spl_sage_destroy(spl_sage* s) {
     delete s;
 }
 
-int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
-                              spl_sage_ws** out) {
-    if (!s || !shape || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_workspace_create: NULL argument");
-    *out = nullptr;
+int spl_sage_plan_new(const spl_sage_shape* shape, const spl_sage_merge* merge, spl_sage_plan* out) {
+    if (!shape || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_plan_new: NULL argument");
     spl_sage_shape sh = *shape;
     if (sh.kv_heads == 0) sh.kv_heads = sh.heads;
     if (sh.batch <= 0 || sh.heads <= 0 || sh.tokens <= 0 || sh.kv_heads <= 0)
@@ -243,10 +241,6 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     spl_sage_merge mg;
     memset(&mg, 0, sizeof mg);
     if (merge) mg = *merge;
-    if (mg.stride <= 1) {
-        memset(&mg, 0, sizeof mg);
-        mg.stride = 1;
-    }
     int64_t tk = sh.tokens;
     if (mg.stride > 1) {
         if (mg.stride != 2 && mg.stride != 4)
@@ -272,6 +266,29 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     if (!fits_i32(sh.batch * sh.heads))
         return fail(SPL_SAGE_ERR_INVALID, "batch x heads = %lld does not fit in i32", (long long)(sh.batch * sh.heads));
     if (tq_pad / 128 > 65535) return fail(SPL_SAGE_ERR_INVALID, "too many query tiles (%lld)", (long long)(tq_pad / 128));
+    out->tq_pad = tq_pad;
+    out->tk = tk;
+    out->tk_pad = tk_pad;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const spl_sage_merge* merge,
+                              spl_sage_ws** out) {
+    if (!s || !shape || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_workspace_create: NULL argument");
+    *out = nullptr;
+    spl_sage_plan plan;
+    const int prc = spl_sage_plan_new(shape, merge, &plan);
+    if (prc) return prc;
+    spl_sage_shape sh = *shape;
+    if (sh.kv_heads == 0) sh.kv_heads = sh.heads;
+    spl_sage_merge mg;
+    memset(&mg, 0, sizeof mg);
+    if (merge) mg = *merge;
+    if (mg.stride <= 1) {
+        memset(&mg, 0, sizeof mg);
+        mg.stride = 1;
+    }
+    const int64_t tq_pad = plan.tq_pad, tk = plan.tk, tk_pad = plan.tk_pad;
 
     const int64_t D = s->head_dim, B = sh.batch, H = sh.heads, G = sh.kv_heads;
     const int64_t q_tiles = tq_pad / QTILE;

@@ -91,3 +91,40 @@ def test_no_gpu_fails_loudly(sage):
 def test_flops_definition(sage):
     plan = sage.Plan(sage.Shape(1, 16, 137800), sage.KvMerge.dense(), 137856, 137800, 137856)
     assert sage.flops(plan, 64) == 4.0 * 16 * 137800 * 137800 * 64
+
+
+def test_plan_rejects_bad_layouts(sage):
+    # tests.rs:174-190 (Plan::new, mod.rs:405-440), on the host: no engine, no GPU
+    lay = lambda frames: sage.FrameLayout(frames, 17, 21, 32, 0)  # noqa: E731  (tests.rs:85-93)
+    with pytest.raises(sage.SageError, match="covers 1378 tokens, the sequence has 1000"):
+        sage.Plan.new(sage.Shape(1, 2, 1000), sage.KvMerge.pool(2, lay(2)))
+    with pytest.raises(sage.SageError, match="stride must be 2 or 4, got 3"):
+        sage.Plan.new(sage.Shape(1, 2, 2 * 689), sage.KvMerge.pool(3, lay(2)))
+    p = sage.Plan.new(sage.Shape(1, 2, 2 * 689), sage.KvMerge.pool(4, lay(2)))
+    assert (p.tq_pad, p.tk, p.tk_pad) == (1408, 2 * (17 + 6 * 8), 192)
+    with pytest.raises(sage.SageError, match="empty attention shape"):
+        sage.Plan.new(sage.Shape(1, 2, 0))
+    with pytest.raises(sage.SageError, match="patch grid"):
+        sage.Plan.new(sage.Shape(1, 2, 34), sage.KvMerge.pool(2, sage.FrameLayout(2, 17, 0, 32)))
+    with pytest.raises(sage.SageError, match="multiple of kv_heads"):
+        sage.Plan.new(sage.Shape(1, 6, 128, kv_heads=4))
+    with pytest.raises(sage.SageError, match="causal attention over merged keys"):
+        sage.Plan.new(sage.Shape(1, 2, 2 * 689, causal=True), sage.KvMerge.pool(2, lay(2)))
+
+
+def test_plan_sizes(sage):
+    # the padding of mod.rs:429-434 at the BASELINE shapes (N = 1370 -> 1408 / 1408)
+    for tokens, tq_pad, tk_pad in ((1024, 1024, 1024), (1370, 1408, 1408), (8192, 8192, 8192), (1, 128, 64),
+                                   (130, 256, 192)):
+        p = sage.Plan.new(sage.Shape(8, 16, tokens))
+        assert (p.tq_pad, p.tk, p.tk_pad, p.key_ratio()) == (tq_pad, tokens, tk_pad, 1.0)
+    # a merged layout keeps its dense frames whole (tests.rs:96-133)
+    lay = sage.FrameLayout(3, 5, 7, 10, 1)
+    p = sage.Plan.new(sage.Shape(2, 3, 3 * 75), sage.KvMerge.pool(2, lay))
+    assert p.tk == lay.merged_keys(2) == 75 + 2 * (5 + 4 * 5)
+    assert p.tk_pad == 128 and 0 < p.key_ratio() < 1
+    # every index the kernels form must fit in i32 (mod.rs:435-439)
+    with pytest.raises(sage.SageError, match="does not fit in i32"):
+        sage.Plan.new(sage.Shape(1, 1, 2**31))
+    with pytest.raises(sage.SageError, match="does not fit in i32"):
+        sage.Plan.new(sage.Shape(2**16, 2**16, 128))
