@@ -272,6 +272,26 @@ int spl_sage_rope_table_1d(double base, int head_dim, int64_t positions, float* 
  * without a workspace, e.g. spl_sage_qkv_gemm).  Synchronises the stream. */
 int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word);
 
+/* The device error word: bit 0 = a bounded wait inside a kernel gave up
+ * (after 1.5 s, or 2^30 tries), bit 1 = a CTA saw the word set and left
+ * early, bits 8..15 = the wait site that gave up. */
+#define SPL_SAGE_DEVERR_TIMEOUT 0x1u
+#define SPL_SAGE_DEVERR_ABORTED 0x2u
+#define SPL_SAGE_DEVERR_SITE(word) (((word) >> 8) & 0xffu)
+#define SPL_SAGE_SELFTEST_SITE 99
+
+/* Runs the failure path of the kernels' bounded waits on purpose (no
+ * counterpart in the reference): one block whose warp 0 waits on an
+ * mbarrier that nothing arrives on until its 0.2 s limit, recording
+ * SPL_SAGE_DEVERR_TIMEOUT and site SPL_SAGE_SELFTEST_SITE in the engine's
+ * error word, while warp 1 waits on another with the kernels' own limit and
+ * leaves as soon as it sees the word set.  result (host, 4 values) =
+ * {warp 0 succeeded, warp 0's wait in ns, warp 1 succeeded, warp 1's wait in
+ * ns}.  Nothing faults and the context stays usable; the engine's word then
+ * reads back through spl_sage_engine_status (which clears it).  Refuses to
+ * run while the word is already set.  Synchronises the engine's stream. */
+int spl_sage_wait_selftest(spl_sage* s, uint64_t* result);
+
 /* Quantises q, k and v exactly like spl_sage_prepare (same bytes), for
  * callers that cannot allocate device memory: a library embedded in a host
  * application that owns all device memory through its own pool and forbids

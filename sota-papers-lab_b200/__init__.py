@@ -98,7 +98,7 @@ EXPORTS = [
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
     "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
-    "spl_sage_ring_forward", "spl_sage_plan_new",
+    "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest",
 ]
 
 # spl_sage_cp_attend flags
@@ -148,6 +148,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_qkv_gemm_quant.argtypes = [P, P, ctypes.POINTER(_QkvShape)] + [P] * 7 + [ctypes.POINTER(_Options)]
         L.spl_sage_rope_table_1d.argtypes = [ctypes.c_double, I, ctypes.c_int64, P]
         L.spl_sage_engine_status.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
+        L.spl_sage_wait_selftest.argtypes = [P, ctypes.POINTER(ctypes.c_uint64)]
         L.spl_sage_quantize_noalloc.argtypes = ([P, I, I, ctypes.POINTER(_Shape), _Tensor, _Tensor, _Tensor,
                                                  ctypes.POINTER(_Options)] + [P] * 6)
         I64P = ctypes.POINTER(ctypes.c_int64)
@@ -501,9 +502,19 @@ class SageAttention:
                                              p(k), p(v), ctypes.byref(o)))
 
     def engine_status(self) -> int:
+        """Reads (and clears) the engine's device error word; raises on a
+        kernel error."""
         w = ctypes.c_uint32()
         _check(lib().spl_sage_engine_status(self._h, ctypes.byref(w)))
         return w.value
+
+    def wait_selftest(self) -> tuple[bool, int, bool, int]:
+        """Runs a bounded wait into its timeout on purpose
+        (spl_sage_wait_selftest): (warp 0 succeeded, its wait in ns, warp 1
+        succeeded, its wait in ns).  The engine's error word is left set."""
+        r = (ctypes.c_uint64 * 4)()
+        _check(lib().spl_sage_wait_selftest(self._h, r))
+        return bool(r[0]), int(r[1]), bool(r[2]), int(r[3])
 
     def workspace(self, shape: Shape, merge: KvMerge | None = None) -> Workspace:
         merge = merge or KvMerge.dense()

@@ -879,6 +879,28 @@ int spl_sage_engine_status(spl_sage* s, uint32_t* device_error_word) {
     return SPL_SAGE_OK;
 }
 
+int spl_sage_wait_selftest(spl_sage* s, uint64_t* result) {
+    if (!s || !result) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_wait_selftest: NULL argument");
+    uint32_t w = 0;
+    cudaError_t e = cudaMemcpyAsync(&w, s->err, 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "read engine status");
+    if (w)
+        return fail(SPL_SAGE_ERR_KERNEL,
+                    "the engine's error word is already set (0x%08x): read it with spl_sage_engine_status first", w);
+    unsigned long long* out = nullptr;
+    e = cudaMalloc(&out, 4 * sizeof(unsigned long long));
+    if (e != cudaSuccess) return cuda_fail(e, "allocate the wait probe's output");
+    e = cudaMemsetAsync(out, 0xff, 4 * sizeof(unsigned long long), s->stream);
+    if (e == cudaSuccess) e = sp::launch_wait_probe(s->err, SPL_SAGE_SELFTEST_SITE, out, s->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(result, out, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    cudaFree(out);
+    if (e != cudaSuccess) return cuda_fail(e, "run the wait probe");
+    return SPL_SAGE_OK;
+}
+
 double spl_sage_flops(const spl_sage_ws* ws) {
     if (!ws) return 0.0;
     return 4.0 * (double)(ws->shape.batch * ws->shape.heads) * (double)ws->shape.tokens * (double)ws->tk *

@@ -23,8 +23,11 @@ constexpr uint32_t ERR_TIMEOUT = 1u << 0;       // a bounded mbarrier wait gave 
 constexpr uint32_t ERR_ABORTED = 1u << 1;       // a CTA saw the error word set and left early
 constexpr uint32_t ERR_SITE_SHIFT = 8;          // bits 8..15: the wait site that timed out
 
-// A wait gives up after this many nanoseconds of %globaltimer.
+// A wait gives up after this many nanoseconds of %globaltimer, or after
+// WAIT_MAX_TRIES unsuccessful try_waits (each one suspends for a while, so
+// the count is a backstop that ends the wait even if the timer stood still).
 constexpr unsigned long long WAIT_LIMIT_NS = 1500000000ull;
+constexpr uint32_t WAIT_MAX_TRIES = 1u << 30;
 
 // ---------------------------------------------------------------- formats
 
@@ -182,23 +185,30 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for phase `parity` of `bar`.  Gives up (returns false) after
-// WAIT_LIMIT_NS, recording ERR_TIMEOUT and the wait site in the device error
-// word, or, with bail_on_err, as soon as anyone has set the error word.
-// Never traps.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t site,
-                                          bool bail_on_err = true) {
+// LIMIT_NS (or WAIT_MAX_TRIES), recording ERR_TIMEOUT and the wait site in
+// the device error word, or, with bail_on_err, as soon as anyone has set the
+// error word.  Never traps.
+template <unsigned long long LIMIT_NS>
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t site,
+                                              bool bail_on_err) {
     if (mbar_try(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return true;
         if ((i & 255u) == 0) {
             if (bail_on_err && ld_volatile(err) != 0) return false;
-            if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+            if (globaltimer() - t0 > LIMIT_NS || i >= WAIT_MAX_TRIES) {
                 atomicOr(err, ERR_TIMEOUT | ((site & 0xffu) << ERR_SITE_SHIFT));
                 return false;
             }
         }
     }
+}
+
+// The kernels' wait: WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t site,
+                                          bool bail_on_err = true) {
+    return mbar_wait_for<WAIT_LIMIT_NS>(bar, parity, err, site, bail_on_err);
 }
 
 // All 32 lanes wait; the warp gives up together if any lane gave up.

@@ -126,6 +126,7 @@ cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& bu
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
                           cudaStream_t st);
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes);
+cudaError_t launch_wait_probe(uint32_t* err, uint32_t site, unsigned long long* out, cudaStream_t st);
 cudaError_t launch_peak(int kind, int n, int iters, int sms, uint32_t* err, unsigned long long* cycles,
                         cudaStream_t st);
 int attn_smem_bytes(int d);

@@ -85,4 +85,37 @@ cudaError_t launch_peak(int kind, int n, int iters, int sms, uint32_t* err, unsi
                       : peak_t<2, 256>(iters, sms, err, cycles, st);
 }
 
+// The failure path of every bounded wait, run on purpose: warp 0 waits on an
+// mbarrier that nothing arrives on and gives up after PROBE_LIMIT_NS,
+// recording ERR_TIMEOUT and `site` in the error word; warp 1 waits on a
+// second such barrier with the kernels' own limit and bail-out, so it leaves
+// as soon as it sees the word set, as the other warps and CTAs of a failed
+// launch do.  out[2w] = 1 if warp w's wait succeeded, out[2w + 1] = its
+// wait in nanoseconds.  Nothing else is in flight: no TMA, no MMA, no TMEM.
+constexpr unsigned long long PROBE_LIMIT_NS = 200000000ull;  // 0.2 s
+
+__global__ void __launch_bounds__(64, 1) sp_wait_probe(uint32_t* err, uint32_t site, unsigned long long* out) {
+    __shared__ __align__(8) uint64_t never[2];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&never[0]), 1);
+        mbar_init(smem_u32(&never[1]), 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const unsigned long long t0 = globaltimer();
+    const bool ok = warp == 0 ? mbar_wait_for<PROBE_LIMIT_NS>(smem_u32(&never[0]), 0, err, site, false)
+                              : mbar_wait(smem_u32(&never[1]), 0, err, site + 1, true);
+    const unsigned long long dt = globaltimer() - t0;
+    if (lane == 0) {
+        out[2 * warp] = ok ? 1ull : 0ull;
+        out[2 * warp + 1] = dt;
+    }
+}
+
+cudaError_t launch_wait_probe(uint32_t* err, uint32_t site, unsigned long long* out, cudaStream_t st) {
+    sp_wait_probe<<<1, 64, 0, st>>>(err, site, out);
+    return cudaGetLastError();
+}
+
 }  // namespace sp
