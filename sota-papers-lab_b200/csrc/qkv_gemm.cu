@@ -24,6 +24,8 @@
 // MMAs of the next.  Warp 0 loads, warp 1 issues the MMAs (4 x M128 N256 K16
 // per block; 4 x K32 for E4M3) and owns TMEM, warps 4-7 run the epilogue,
 // one thread per row.
+#include <atomic>
+
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
@@ -240,18 +242,22 @@ template <int D, int HALF, bool FP8>
 static cudaError_t qkv_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, const float* x_scale,
                          const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
                          const QkvGeom& g, cudaStream_t st) {
-    static unsigned attr_set = 0;
+    static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 32 || !(attr_set & (1u << dev))) {
+    if (dev >= 32 || !(attr_set.load(std::memory_order_acquire) & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(sp_qkv_gemm<D, HALF, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              gemm::SMEM);
         if (e != cudaSuccess) return e;
-        if (dev < 32) attr_set |= 1u << dev;
+        if (dev < 32) attr_set.fetch_or(1u << dev, std::memory_order_release);
     }
-    static int sms[32] = {0};  // SMs per device ordinal
-    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    static std::atomic<int> sms[32];  // SMs per device ordinal (zero until asked)
+    int n_sm = dev < 32 ? sms[dev].load(std::memory_order_relaxed) : 0;
+    if (n_sm <= 0) {
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (dev < 32 && n_sm > 0) sms[dev].store(n_sm, std::memory_order_relaxed);
+    }
+    if (n_sm <= 0) n_sm = 148;
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)(g.n / gemm::BN) * ((g.m + gemm::BM - 1) / gemm::BM);
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM

@@ -15,6 +15,8 @@
 // and run the epilogue of qkv_gemm.cu, then tell the leader the accumulator
 // is free.  Every mbarrier wait is bounded; both CTAs always
 // reach the closing cluster barrier, after which TMEM is freed.
+#include <atomic>
+
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
@@ -357,17 +359,21 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
                           const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
                           const QkvGeom& g, cudaStream_t st) {
     auto kern = sp_qkv_gemm_2sm<D, HALF, FP8>;
-    static unsigned attr_set = 0;
+    static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 32 || !(attr_set & (1u << dev))) {
+    if (dev >= 32 || !(attr_set.load(std::memory_order_acquire) & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM);
         if (e != cudaSuccess) return e;
-        if (dev < 32) attr_set |= 1u << dev;
+        if (dev < 32) attr_set.fetch_or(1u << dev, std::memory_order_release);
     }
-    static int sms[32] = {0};
-    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    static std::atomic<int> sms[32];  // SMs per device ordinal (zero until asked)
+    int n_sm = dev < 32 ? sms[dev].load(std::memory_order_relaxed) : 0;
+    if (n_sm <= 0) {
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (dev < 32 && n_sm > 0) sms[dev].store(n_sm, std::memory_order_relaxed);
+    }
+    if (n_sm <= 0) n_sm = 148;
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)(g.n / gemm2::BN) * ((g.m + 2 * gemm2::BM - 1) / (2 * gemm2::BM));
     long long pairs = n_sm / 2;

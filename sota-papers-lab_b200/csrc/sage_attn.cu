@@ -42,6 +42,8 @@
 // Every mbarrier wait is bounded (sage_dev.cuh): on a timeout the kernel
 // records it in the device error word, drains its own TMA loads and MMAs,
 // frees TMEM and returns.
+#include <atomic>
+
 #include "sage_dev.cuh"
 #include "sage_kernels.h"
 
@@ -562,18 +564,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 template <int D, bool CAUSAL, bool MERGE, bool PARTIAL>
 static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out, float* acc, float* lse,
                             int q_tiles, cudaStream_t st) {
-    static unsigned attr_set = 0;  // one bit per device ordinal
+    static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
     auto kern = sp_attn<D, CAUSAL, MERGE, PARTIAL>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 32 || !(attr_set & (1u << dev))) {
+    if (dev >= 32 || !(attr_set.load(std::memory_order_acquire) & (1u << dev))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::DYN);
         if (e != cudaSuccess) return e;
-        if (dev < 32) attr_set |= 1u << dev;
+        if (dev < 32) attr_set.fetch_or(1u << dev, std::memory_order_release);
     }
-    static int sms[32] = {0};  // SMs per device ordinal
-    if (dev < 32 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    int n_sm = dev < 32 && sms[dev] > 0 ? sms[dev] : 148;
+    static std::atomic<int> sms[32];  // SMs per device ordinal (zero until asked)
+    int n_sm = dev < 32 ? sms[dev].load(std::memory_order_relaxed) : 0;
+    if (n_sm <= 0) {
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (dev < 32 && n_sm > 0) sms[dev].store(n_sm, std::memory_order_relaxed);
+    }
+    if (n_sm <= 0) n_sm = 148;
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)g.batch * g.heads * q_tiles;
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
