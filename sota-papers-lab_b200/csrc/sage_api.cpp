@@ -112,12 +112,16 @@ struct spl_sage {
 };
 
 namespace {
-// The CTA cap of this engine's persistent kernels (0: one per SM).
-int max_ctas(const spl_sage* s) {
-    if (s->reserved_sms <= 0) return 0;
-    const int n = s->sm_count - s->reserved_sms;
+// The CTA cap of a persistent kernel that leaves `reserved` SMs free (0: one
+// CTA per SM).
+int max_ctas(const spl_sage* s, int reserved) {
+    if (reserved <= 0) return 0;
+    const int n = s->sm_count - reserved;
     return n > 1 ? n : 1;
 }
+
+// ... with the engine's own reservation (spl_sage_reserve_sms).
+int max_ctas(const spl_sage* s) { return max_ctas(s, s->reserved_sms); }
 }  // namespace
 
 struct spl_sage_ws {
@@ -1010,8 +1014,10 @@ int spl_sage_cp_quantize_kv(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor k, spl
     return SPL_SAGE_OK;
 }
 
-int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
-                       int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse) {
+// One segment with `reserved` SMs left free; the engine itself is not
+// changed, so other threads may use it meanwhile.
+static int cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
+                     int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse, int reserved) {
     if (!s || !ws || !kv || !acc || !lse) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend: NULL argument");
     if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
     if (kv->head_dim != ws->head_dim || kv->tk_pad != ws->tk_pad || kv->batch != ws->shape.batch ||
@@ -1041,7 +1047,7 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
     g.tk_pad = (int)kv->tk_pad;
     g.causal = causal ? 1 : 0;
     g.cp_first = (flags & SPL_SAGE_CP_FIRST) ? 1 : 0;
-    g.max_ctas = max_ctas(s);
+    g.max_ctas = max_ctas(s, reserved);
     g.merge = 1;
     sp::AttnMaps maps;
     maps.q = ws->maps.q;
@@ -1052,6 +1058,12 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
     cudaError_t e = sp::launch_attend_partial(s->head_dim, maps, buf, g, acc, lse, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage segment attention");
     return SPL_SAGE_OK;
+}
+
+int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv, int64_t q_begin, int64_t q_len,
+                       int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse) {
+    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend: NULL argument");
+    return cp_attend(s, ws, kv, q_begin, q_len, k_begin, k_len, flags, acc, lse, s->reserved_sms);
 }
 
 int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out) {
@@ -1234,9 +1246,8 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
     // 3. this rank's K/V quantised with them
     rc = spl_sage_cp_quantize_kv(s, r->ws, k, v, opts, r->raw, r->tokens * P, r->kv[0]);
     if (rc) return rc;
-    // 4. P steps, one segment launch each, the K/V moving one rank on meanwhile
-    const int keep = s->reserved_sms;
-    s->reserved_sms = r->reserved_sms;
+    // 4. P steps, one segment launch each, the K/V moving one rank on
+    // meanwhile; the segments leave the ring's reserved SMs to NCCL
     int cur = 0;
     const int next = (int)((rank + 1) % P), prev = (int)((rank + P - 1) % P);
     for (int64_t step = 0; step < P && rc == SPL_SAGE_OK; step++) {
@@ -1284,14 +1295,13 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
             qb = C;
             ql = C;
         }
-        rc = spl_sage_cp_attend(s, r->ws, r->kv[cur], qb, ql, kb, kl, flags, r->acc, r->lse);
+        rc = cp_attend(s, r->ws, r->kv[cur], qb, ql, kb, kl, flags, r->acc, r->lse, r->reserved_sms);
         if (rc == SPL_SAGE_OK && pass_on) {
             cudaError_t e = cudaStreamWaitEvent(s->stream, r->ev_comm, 0);
             if (e != cudaSuccess) rc = cuda_fail(e, "wait for the ring exchange");
             cur = 1 - cur;
         }
     }
-    s->reserved_sms = keep;
     if (rc) return rc;
     // 5. the accumulator to bf16
     return spl_sage_cp_finish(s, r->ws, r->acc, out);

@@ -214,6 +214,13 @@ class RingAttention:
             import torch.distributed as dist
             if dist.is_available() and dist.is_initialized() and dist.get_backend() == "nccl":
                 self.group, self._own_group = nccl_ring_group(), True
+        # the segments launch through an engine of their own on the same
+        # stream that leaves the reserved SMs free, so the caller's engine is
+        # never changed (other threads may use it meanwhile)
+        self.seg_eng = eng
+        if self.reserved_sms:
+            self.seg_eng = sage.SageAttention(eng.stream, head_dim, eng.config)
+            self.seg_eng.reserve_sms(self.reserved_sms)
         self.ws = eng.workspace(sage.Shape(batch, heads, local_tokens, kv_heads, False))
         self.kv = [sage.KvBuffer(eng, self.ws), sage.KvBuffer(eng, self.ws)]
         self.raw = torch.empty(batch * kv_heads, 4, head_dim, dtype=torch.float32, device="cuda")
@@ -237,30 +244,28 @@ class RingAttention:
         if exchange is None and P > 1:
             exchange = nccl_exchange(group)
         cur = 0
-        keep = self.eng.reserved_sms
-        self.eng.reserve_sms(self.reserved_sms)
-        try:
-            for s, (src, seg) in enumerate(ring_segments(r, P)):
-                wait = None
-                if s + 1 < P:
-                    wait = exchange(self.kv[cur].tensors(), self.kv[1 - cur].tensors())
-                self.attend_segment(self.kv[cur], seg, first=s == 0)
-                if wait is not None:
-                    wait()
-                    cur = 1 - cur
-        finally:
-            self.eng.reserve_sms(keep)
+        for s, (src, seg) in enumerate(ring_segments(r, P)):
+            wait = None
+            if s + 1 < P:
+                wait = exchange(self.kv[cur].tensors(), self.kv[1 - cur].tensors())
+            self.attend_segment(self.kv[cur], seg, first=s == 0)
+            if wait is not None:
+                wait()
+                cur = 1 - cur
         self.eng.cp_finish(self.ws, self.acc, out)
 
     def attend_segment(self, kv, seg: Segment, first: bool):
         C = self.C
-        self.eng.cp_attend(self.ws, kv, seg.q_chunk * C, seg.q_chunks * C, seg.k_chunk * C, seg.k_chunks * C,
-                           seg.causal, self.acc, self.lse, first=first)
+        self.seg_eng.cp_attend(self.ws, kv, seg.q_chunk * C, seg.q_chunks * C, seg.k_chunk * C, seg.k_chunks * C,
+                               seg.causal, self.acc, self.lse, first=first)
 
     def close(self):
         for kv in self.kv:
             kv.close()
         self.ws.close()
+        if self.seg_eng is not self.eng:
+            self.seg_eng.close()
+            self.seg_eng = self.eng
         if self._own_group:
             import torch.distributed as dist
             dist.destroy_process_group(self.group)
