@@ -186,7 +186,7 @@ int or_members(const or_geom* g, int j, int* base, int* nx) {
  * reproducible), tolerance-checked only. */
 static void dev_layernorm(float* x, const float* w, const float* bias, int d, float eps) {
     int ch = d / 8;
-    float part[16], part2[16];
+    float part[16] = {0.f}, part2[16] = {0.f};  /* d is 64 or 128: ch = 8 or 16 lanes */
     for (int c = 0; c < ch; c++) {
         float s = 0.f;
         for (int e = 0; e < 8; e++) s += x[c * 8 + e];
