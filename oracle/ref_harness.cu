@@ -15,6 +15,18 @@
 
 #include REF_SRC
 
+#include <stddef.h>
+
+// The struct the reference's Rust host passes by value (its Geom, checked by
+// src/sage/tests.rs:234-242): 12 i64 strides, 16 i32, 3 f32 and padding.
+// This harness fills it field by field, so the same layout pins that the
+// reference kernels read what the harness wrote.
+static_assert(sizeof(SgGeom) == 12 * 8 + 16 * 4 + 4 * 4, "SgGeom size");
+static_assert(offsetof(SgGeom, batch) == 96, "SgGeom.batch offset");
+static_assert(offsetof(SgGeom, flags) == 96 + 15 * 4, "SgGeom.flags offset");
+static_assert(offsetof(SgGeom, q_mul) == 96 + 16 * 4, "SgGeom.q_mul offset");
+static_assert(offsetof(SgGeom, v_range) == 96 + 18 * 4, "SgGeom.v_range offset");
+
 static int g_smem_set = 0;
 
 extern "C" int ref_head_dim(void) { return SG_D; }
