@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_tiles = g.n / BN, ntiles = n_tiles * ((g.m + BM - 1) / BM);
+    // channels from one RoPE pair row to the next (HALF = 0, no RoPE: unused)
+    constexpr int PAIR_SPAN = HALF > 0 ? 2 * HALF : 1;
     const int kblocks = (g.k + BK - 1) / BK;
     // the CTA's it-th tile; consecutive tiles share their rows of x
     auto tile_m0 = [&](int t) { return (t / n_tiles) * BM; };
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(gemm::NTHREADS, 1)
 #pragma unroll
                     for (int d = 0; d < D; d++) {
                         if (d & HALF) continue;
-                        const int pair = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
+                        const int pair = (d / PAIR_SPAN) * HALF + (d & (HALF - 1));
                         const float2 cs = __ldg(rt + pair);
                         const float a = x[d], b = x[d | HALF];
                         x[d] = a * cs.x - b * cs.y;

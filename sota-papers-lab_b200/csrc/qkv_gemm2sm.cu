@@ -117,6 +117,8 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                     const QkvGeom g) {
     using namespace gemm2;
     constexpr int TM = 2 * BM;  // rows of the pair's tile
+    // channels from one RoPE pair row to the next (HALF = 0, no RoPE: unused)
+    constexpr int PAIR_SPAN = HALF > 0 ? 2 * HALF : 1;
     constexpr uint32_t IDESC =
         FP8 ? make_idesc(C_F32, F_E4M3, F_E4M3, TM, BN) : make_idesc(C_F32, F_BF16, F_BF16, TM, BN);
     constexpr int BK = FP8 ? BK_BYTES : BK_BYTES / 2;  // K elements per ring stage
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                 };
                 // RoPE on (a, b) with the table entries of channels d, d + 1
                 auto rot2 = [&](int d, float& a0, float& b0, float& a1, float& b1) {
-                    const int pr = (d / (2 * HALF)) * HALF + (d & (HALF - 1));
+                    const int pr = (d / PAIR_SPAN) * HALF + (d & (HALF - 1));
                     const float4 cs = __ldg(reinterpret_cast<const float4*>(rt + pr));
                     float a = a0, b = b0;
                     a0 = a * cs.x - b * cs.y;
@@ -379,13 +381,12 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     long long pairs = n_sm / 2;
     if (ntiles < pairs) pairs = ntiles;
     if (pairs < 1) pairs = 1;
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof cfg);
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs));
     cfg.blockDim = dim3(gemm2::nthreads<FP8>());
     cfg.dynamicSmemBytes = gemm2::SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[1] = {};
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
