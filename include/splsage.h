@@ -388,6 +388,17 @@ typedef struct spl_sage_ring spl_sage_ring;
 int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int world, int reserved_sms,
                          spl_sage_ring** out);
 void spl_sage_ring_destroy(spl_sage_ring* r);
+
+/* The segment step `step` of rank `rank` attends (the schedule
+ * spl_sage_ring_forward follows), as arguments of spl_sage_cp_attend with
+ * chunk = each rank's tokens / 2: step 0 the rank's own two chunks, causal,
+ * first of their rows; a step holding the K/V of a rank before this one both
+ * query chunks against that rank's first key chunk; of a rank after it the
+ * second query chunk against both key chunks.  Over the steps every
+ * (query chunk, key chunk) pair of the zig-zag split with the key at or
+ * before the query is attended once.  Host only. */
+int spl_sage_ring_segment(int rank, int world, int step, int64_t chunk, int64_t* q_begin, int64_t* q_len,
+                          int64_t* k_begin, int64_t* k_len, int* flags);
 int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
                           spl_sage_tensor_mut out, const spl_sage_options* opts, void* nccl_comm);
 

@@ -98,7 +98,7 @@ EXPORTS = [
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
     "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
-    "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest",
+    "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest", "spl_sage_ring_segment",
 ]
 
 # spl_sage_cp_attend flags
@@ -127,6 +127,8 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_ring_create.argtypes = [P, ctypes.POINTER(_Shape), I, I, I, ctypes.POINTER(P)]
         L.spl_sage_ring_destroy.argtypes = [P]
         L.spl_sage_ring_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
+        L.spl_sage_ring_segment.argtypes = [I, I, I, ctypes.c_int64] + [ctypes.POINTER(ctypes.c_int64)] * 4 + [
+            ctypes.POINTER(I)]
         L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
         L.spl_sage_ws_destroy.argtypes = [P]
         L.spl_sage_ws_bytes.restype = ctypes.c_int64
@@ -580,6 +582,15 @@ class SageAttention:
         w = ctypes.c_uint32()
         _check(lib().spl_sage_status(self._h, ws._h, ctypes.byref(w)))
         return w.value
+
+
+def ring_segment(rank: int, world: int, step: int, chunk: int) -> tuple[int, int, int, int, int]:
+    """The segment the native ring attends at a step (spl_sage_ring_segment;
+    host only): (q_begin, q_len, k_begin, k_len, cp_attend flags)."""
+    v = [ctypes.c_int64() for _ in range(4)]
+    f = ctypes.c_int()
+    _check(lib().spl_sage_ring_segment(rank, world, step, chunk, *[ctypes.byref(x) for x in v], ctypes.byref(f)))
+    return v[0].value, v[1].value, v[2].value, v[3].value, f.value
 
 
 class NativeRing:

@@ -1217,6 +1217,34 @@ int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int
     return SPL_SAGE_OK;
 }
 
+int spl_sage_ring_segment(int rank, int world, int step, int64_t chunk, int64_t* q_begin, int64_t* q_len,
+                          int64_t* k_begin, int64_t* k_len, int* flags) {
+    if (!q_begin || !q_len || !k_begin || !k_len || !flags)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_segment: NULL argument");
+    if (world < 1 || rank < 0 || rank >= world || step < 0 || step >= world || chunk <= 0)
+        return fail(SPL_SAGE_ERR_INVALID, "ring: step %d of rank %d of %d ranks, chunk %lld", step, rank, world,
+                    (long long)chunk);
+    // the step's chunk pairs as one segment: step 0 the rank's own tokens,
+    // causal, writing the accumulator; from a rank before this one both
+    // query chunks against its first key chunk; from a rank after it the
+    // second query chunk against both key chunks
+    const int src = (rank - step + world) % world;
+    *q_begin = 0;
+    *q_len = 2 * chunk;
+    *k_begin = 0;
+    *k_len = 2 * chunk;
+    *flags = 0;
+    if (step == 0) {
+        *flags = SPL_SAGE_CP_CAUSAL | SPL_SAGE_CP_FIRST;
+    } else if (src < rank) {
+        *k_len = chunk;
+    } else {
+        *q_begin = chunk;
+        *q_len = chunk;
+    }
+    return SPL_SAGE_OK;
+}
+
 int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
                           spl_sage_tensor_mut out, const spl_sage_options* opts, void* nccl_comm) {
     if (!s || !r) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_forward: NULL argument");
@@ -1251,7 +1279,6 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
     int cur = 0;
     const int next = (int)((rank + 1) % P), prev = (int)((rank + P - 1) % P);
     for (int64_t step = 0; step < P && rc == SPL_SAGE_OK; step++) {
-        const int64_t src = (rank - step + P) % P;
         const bool pass_on = step + 1 < P;
         if (pass_on) {
             // the buffer received into was read by the previous step
@@ -1281,20 +1308,10 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
                 break;
             }
         }
-        // the step's chunk pairs as one segment: step 0 the rank's own tokens,
-        // causal, writing the accumulator; from a rank before this one both
-        // query chunks against its first key chunk; from a rank after it the
-        // second query chunk against both key chunks
-        int64_t qb = 0, ql = 2 * C, kb = 0, kl = 2 * C;
-        int flags = 0;
-        if (step == 0) {
-            flags = SPL_SAGE_CP_CAUSAL | SPL_SAGE_CP_FIRST;
-        } else if (src < rank) {
-            kl = C;
-        } else {
-            qb = C;
-            ql = C;
-        }
+        int64_t qb, ql, kb, kl;
+        int flags;
+        rc = spl_sage_ring_segment((int)rank, (int)P, (int)step, C, &qb, &ql, &kb, &kl, &flags);
+        if (rc) break;
         rc = cp_attend(s, r->ws, r->kv[cur], qb, ql, kb, kl, flags, r->acc, r->lse, r->reserved_sms);
         if (rc == SPL_SAGE_OK && pass_on) {
             cudaError_t e = cudaStreamWaitEvent(s->stream, r->ev_comm, 0);

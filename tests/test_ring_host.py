@@ -122,3 +122,19 @@ def test_exchange_and_statistics_over_gloo(world):
         assert raw[1] == sum(2.0 * r for r in range(world))
         assert raw[2] == max(-(5.0 - r) for r in range(world))
         assert raw[3] == max(3.0 * r for r in range(world))
+
+
+def test_native_schedule_is_the_python_schedule(sage):
+    """The ring inside the library (spl_sage_ring_segment, the schedule
+    spl_sage_ring_forward follows) attends, at every step of every rank,
+    the segment the Python ring attends, for 1 to 8 ranks."""
+    C = 384
+    for world in range(1, 9):
+        for rank in range(world):
+            for step, (src, seg) in enumerate(ring.ring_segments(rank, world)):
+                flags = (sage.CP_CAUSAL if seg.causal else 0) | (sage.CP_FIRST if step == 0 else 0)
+                want = (seg.q_chunk * C, seg.q_chunks * C, seg.k_chunk * C, seg.k_chunks * C, flags)
+                assert sage.ring_segment(rank, world, step, C) == want, (world, rank, step)
+    for bad in ((0, 0, 0, C), (2, 2, 0, C), (0, 2, 2, C), (0, 2, 0, 0), (-1, 2, 0, C)):
+        with pytest.raises(sage.SageError):
+            sage.ring_segment(*bad)
