@@ -240,6 +240,27 @@ def run_layers(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     attn_ms = a0.elapsed_time(a1) / (args.steps * Lr)
+
+    # end to end: each step's activations up from pinned host memory, the 24
+    # layers, the last layer's attention output back to the host
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    e_steps = max(1, min(args.steps, 3))
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e_steps):
+        x.copy_(xh, non_blocking=True)
+        for i in range(Lr):
+            layer(i)
+        oh.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item()) / e_steps
     word |= eng.status(ws)
     if rank != 0:
         return None
@@ -262,6 +283,10 @@ def run_layers(args, rank, world, local_rank):
                      "traffic": None, "attn_ms_per_layer": round(attn_ms, 4),
                      "layer_ms": round(step_ms / Lr, 4),
                      "peak_source": "measured in this run by the tcgen05 probe (lower of INT8, FP8 E4M3)"},
+        "e2e": {"value": round(eff / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": x.numel() * x.element_size(),
+                "d2h_bytes_per_step": out.numel() * out.element_size(),
+                "api": "qkv_gemm_quant + attend via libsplsage C ABI, 24 layers per step, pinned host buffers"},
         "gpu_launches": 5 * Lr * args.steps,
         "clocks": clk.summary(),
         "device_error_word": word,
