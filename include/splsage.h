@@ -306,7 +306,12 @@ int spl_sage_wait_selftest(spl_sage* s, uint64_t* result);
  *     ceil(tokens / 128) * 4 * head_dim <= 1,048,576; larger calls are
  *     rejected with SPL_SAGE_ERR_INVALID (use spl_sage_prepare).
  *   - The first call on a device looks the array's device address up (and
- *     caches it); make that first call before any stream capture.
+ *     caches it with the device's current context; a device reset that
+ *     re-creates the context makes the next call look it up again); make
+ *     that first call before any stream capture.
+ *   - q8, k8 and v8 must start on 16 bytes, q_scale, k_scale and stats on
+ *     4 bytes (SPL_SAGE_ERR_INVALID otherwise): the library cannot see the
+ *     outputs' sizes, so the caller sizes them as listed below.
  *   - All calls share the array and it keeps the last call's contents
  *     (each call overwrites what it reads), so calls that overlap on the
  *     GPU, on different streams, race.

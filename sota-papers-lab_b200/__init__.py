@@ -40,6 +40,9 @@ def library_path() -> str:
     return os.path.join(_HERE, "libsplsage.so")
 
 
+ERR_INVALID = 1  # SPL_SAGE_ERR_INVALID
+
+
 class SageError(RuntimeError):
     """A non-zero status from libsplsage, with its message."""
 
@@ -664,7 +667,22 @@ def quantize_noalloc(head_dim: int, shape: Shape, q: Tensor, k: Tensor, v: Tenso
     [b][h][tq_pad/16] f32, k8 [b][g][tk_pad][D] i8, k_scale [b][g][tk_pad/64]
     f32, v8 [b][g][D][tk_pad] E4M3 bytes, stats [b][g][4][D] f32.  Dense keys
     only; the library's fixed scratch bounds batch * kv_heads *
-    ceil(tokens/128) * 4 * D to 1,048,576."""
+    ceil(tokens/128) * 4 * D to 1,048,576.  The C ABI cannot see the
+    outputs' sizes, so every output is checked here (a CUDA tensor of at
+    least its layout's bytes) before the call."""
+    b, h, g, t, d = shape.batch, shape.heads, shape.kv, shape.tokens, head_dim
+    tq_pad = (t + 127) // 128 * 128
+    tk_pad = (t + 63) // 64 * 64
+    need = {"q8": b * h * tq_pad * d, "q_scale": 4 * b * h * (tq_pad // 16), "k8": b * g * tk_pad * d,
+            "k_scale": 4 * b * g * (tk_pad // 64), "v8": b * g * d * tk_pad, "stats": 4 * b * g * 4 * d}
+    for name, t_out in (("q8", q8), ("q_scale", q_scale), ("k8", k8), ("k_scale", k_scale), ("v8", v8),
+                        ("stats", stats)):
+        if not getattr(t_out, "is_cuda", False):
+            raise SageError(ERR_INVALID, f"quantize_noalloc: {name} must be a CUDA tensor")
+        have = t_out.numel() * t_out.element_size()
+        if have < need[name]:
+            raise SageError(ERR_INVALID,
+                            f"quantize_noalloc: {name} holds {have} bytes, the shape needs {need[name]}")
     sh = _Shape(shape.batch, shape.heads, shape.kv, shape.tokens, int(shape.causal), 0)
     o = (opts or Options())._c()
     ptr = (lambda t: ctypes.c_void_p(t.data_ptr()))

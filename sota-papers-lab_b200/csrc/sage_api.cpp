@@ -792,6 +792,12 @@ int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const sp
     // the fixed device array in sage_quant.cu: no cudaMalloc, no cudaFree.
     if (!shape || !q8 || !q_scale || !k8 || !k_scale || !v8 || !stats)
         return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: NULL argument");
+    // The kernels store q8, k8 and v8 16 bytes at a time and the scales and
+    // statistics as floats; a misaligned caller buffer would fault on the GPU.
+    if ((uintptr_t)q8 % 16 || (uintptr_t)k8 % 16 || (uintptr_t)v8 % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: q8, k8 and v8 must start on 16 bytes");
+    if ((uintptr_t)q_scale % 4 || (uintptr_t)k_scale % 4 || (uintptr_t)stats % 4)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quantize_noalloc: q_scale, k_scale and stats must start on 4 bytes");
     if (head_dim != 64 && head_dim != 128)
         return fail(SPL_SAGE_ERR_INVALID, "sage attention supports head dim 64 or 128, got %d", head_dim);
     if (pv_accum != SPL_SAGE_PV_F32 && pv_accum != SPL_SAGE_PV_F16)

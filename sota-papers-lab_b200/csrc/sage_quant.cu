@@ -681,22 +681,49 @@ namespace sp {
 constexpr size_t NOALLOC_PART_FLOATS = size_t(1) << 20;  // 4 MiB of per-tile statistics
 static __device__ __align__(256) float g_noalloc_part[NOALLOC_PART_FLOATS];
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The driver's cuCtxGetCurrent, looked up once through the runtime (the
+// library does not link libcuda).
+static CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (CtxGetCurrentFn)p;
+    });
+    return fn;
+}
+
 // Device address of g_noalloc_part on the current device.  In host code the
 // array's name is only a host-side stand-in, so its device address is asked
-// for once per device (with that device current) and cached.
+// for once per device (with that device current) and cached together with
+// the context it was asked in: a device reset that re-creates the context
+// (and reloads the module) makes the next call ask again.
 cudaError_t noalloc_part_buffer(float** out) {
     static std::mutex mu;
     static float* addr[64] = {nullptr};
+    static CUcontext ctx_of[64] = {nullptr};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    CtxGetCurrentFn get = ctx_get_current_fn();
+    CUcontext ctx = nullptr;
+    if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    // (a thread with no context bound yet reads NULL: look the address up,
+    // which binds the device's primary context, and then read it again)
+    if (!addr[dev] || !ctx || ctx != ctx_of[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_part);
         if (e != cudaSuccess) return e;
+        if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
         addr[dev] = (float*)p;
+        ctx_of[dev] = ctx;
     }
     *out = addr[dev];
     return cudaSuccess;

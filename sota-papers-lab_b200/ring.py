@@ -185,6 +185,17 @@ def combine_stats(raw, world: int, group=None):
     return raw
 
 
+def _torch_stream(stream):
+    """The torch stream object of an engine stream (a torch stream, a raw
+    cudaStream_t as an int, or None for the legacy default stream)."""
+    import torch
+    if stream is None:
+        return torch.cuda.default_stream()
+    if isinstance(stream, int):
+        return torch.cuda.ExternalStream(stream) if stream else torch.cuda.default_stream()
+    return stream
+
+
 class RingAttention:
     """Ring attention of one rank.  Holds the workspace (this rank's tokens),
     two K/V buffers (the one being attended, the one being received) and the
@@ -231,7 +242,17 @@ class RingAttention:
                 combine: Callable | None = None):
         """q, k, v, out: this rank's tokens (sage.Tensor views); exchange: the
         K/V transfer (default NCCL P2P over `group`, default the ring's own);
-        combine: the statistics reduction (default all-reduce over `group`)."""
+        combine: the statistics reduction (default all-reduce over `group`).
+
+        torch.distributed orders its collectives and P2P calls against
+        torch's current stream only, so the body runs with the engine's
+        stream made current: the statistics all-reduce and the K/V exchange
+        then follow the kernels that produce what they send."""
+        import torch
+        with torch.cuda.stream(_torch_stream(self.eng.stream)):
+            self._forward(q, k, v, out, exchange, group, opts, combine)
+
+    def _forward(self, q, k, v, out, exchange, group, opts, combine):
         P, r = self.world, self.rank
         if group is None:
             group = self.group

@@ -128,3 +128,55 @@ def test_plan_sizes(sage):
         sage.Plan.new(sage.Shape(1, 1, 2**31))
     with pytest.raises(sage.SageError, match="does not fit in i32"):
         sage.Plan.new(sage.Shape(2**16, 2**16, 128))
+
+
+def test_noalloc_rejects_misaligned_outputs_before_any_launch(sage):
+    # The alignment checks of spl_sage_quantize_noalloc come before any CUDA
+    # call, so fake (never dereferenced) addresses show them on the CPU.
+    L = sage.lib()
+    sh = sage._Shape(1, 2, 2, 128, 0, 0)
+    t = sage._Tensor(0x100000, 1 << 20, 0, 0, 0)
+    base, f4 = 0x200000, 0x300000
+    ok = dict(q8=base, q_scale=f4, k8=base + 0x10000, k_scale=f4 + 0x1000, v8=base + 0x20000, stats=f4 + 0x2000)
+    for name, bad in (("q8", 8), ("k8", 4), ("v8", 1), ("q_scale", 2), ("k_scale", 1), ("stats", 3)):
+        args = dict(ok)
+        args[name] += bad
+        rc = L.spl_sage_quantize_noalloc(None, 64, 0, ctypes.byref(sh), t, t, t, None,
+                                         *[ctypes.c_void_p(args[k]) for k in
+                                           ("q8", "q_scale", "k8", "k_scale", "v8", "stats")])
+        assert rc == 1, (name, rc)
+        assert b"must start on" in L.spl_sage_last_error(), name
+
+
+class _FakeCuda:
+    """Stands in for a CUDA tensor in the wrapper's host-side size checks."""
+    is_cuda = True
+
+    def __init__(self, nbytes):
+        self.n = nbytes
+
+    def numel(self):
+        return self.n
+
+    def element_size(self):
+        return 1
+
+    def data_ptr(self):
+        raise AssertionError("the wrapper must reject before it reads an address")
+
+
+def test_noalloc_wrapper_checks_output_sizes_on_the_host(sage):
+    import torch
+    b, h, g, t, d = 1, 4, 2, 200, 64  # tq_pad 256, tk_pad 256
+    need = dict(q8=b * h * 256 * d, q_scale=4 * b * h * 16, k8=b * g * 256 * d, k_scale=4 * b * g * 4,
+                v8=b * g * d * 256, stats=4 * b * g * 4 * d)
+    x = torch.zeros(8, dtype=torch.bfloat16)
+    tq = sage.Tensor(x, sage.Strides.bthd(t, h, d))
+    order = ("q8", "q_scale", "k8", "k_scale", "v8", "stats")
+    for short in order:
+        outs = [_FakeCuda(need[k] - (1 if k == short else 0)) for k in order]
+        with pytest.raises(sage.SageError, match=short):
+            sage.quantize_noalloc(d, sage.Shape(b, h, t, g), tq, tq, tq, *outs)
+    with pytest.raises(sage.SageError, match="CUDA tensor"):
+        sage.quantize_noalloc(d, sage.Shape(b, h, t, g), tq, tq, tq, torch.zeros(need["q8"], dtype=torch.int8),
+                              *[_FakeCuda(need[k]) for k in order[1:]])
