@@ -78,7 +78,7 @@ def lib():
         L.or_attention_bthd.restype = ctypes.c_int
         L.or_attention_bthd.argtypes = [P, P, P, ctypes.POINTER(Geom), ctypes.c_float, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
-        L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom), ctypes.c_int, ctypes.c_int, P]
+        L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom)] + [ctypes.c_int] * 4 + [P]
         L.or_layer_norm.argtypes = [P, P, P, ctypes.c_int, ctypes.c_float]
         L.or_qkv_reference.argtypes = [P, P, P, P] + [ctypes.c_int] * 10 + [P, P, P]
         L.or_qkv_reference_fp8.argtypes = [P] * 6 + [ctypes.c_int] * 10 + [P, P, P]
@@ -287,10 +287,14 @@ def attention_bthd(q, k, v, g: Geom, *, causal=False, rows=None, nthreads=None, 
     return out
 
 
-def sage_emulate(qt: Quant, g: Geom, *, causal=False, nthreads=None) -> np.ndarray:
+def sage_emulate(qt: Quant, g: Geom, *, causal=False, rows=None, nthreads=None) -> np.ndarray:
+    """The quantised arithmetic evaluated exactly (or_sage_emulate); only
+    `rows` (a (start, stop) range of every (b, h)) are computed."""
     out = np.zeros((g.batch, g.tokens, g.heads, g.d), np.float32)
+    r0, r1 = rows if rows is not None else (0, g.tokens)
     lib().or_sage_emulate(_p(qt.q8), _p(qt.q_scale), _p(qt.k8), _p(qt.k_scale), _p(qt.v8), _p(qt.stats),
-                          _p(qt.kbias), ctypes.byref(g), int(causal), nthreads or os.cpu_count() or 1, _p(out))
+                          _p(qt.kbias), ctypes.byref(g), int(causal), r0, r1, nthreads or os.cpu_count() or 1,
+                          _p(out))
     return out
 
 

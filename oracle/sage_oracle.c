@@ -610,6 +610,7 @@ typedef struct {
     const float* kbias;
     const or_geom* g;
     int causal;
+    int row0, row1;
     float* out;
     int64_t next;
     pthread_mutex_t mu;
@@ -641,7 +642,7 @@ static void* emu_worker(void* arg) {
             cur_kvh = kvh;
         }
         const float* st = J->stats + kvh * 4 * d;
-        for (int i = 0; i < g->tokens; i++) {
+        for (int i = J->row0; i < J->row1; i++) {
             const int8_t* qi = J->q8 + (bh * g->tq_pad + i) * d;
             double qs = J->q_scale[bh * (g->tq_pad / OR_QGROUP) + i / OR_QGROUP];
             int nk = J->causal ? (i + 1 < g->tk ? i + 1 : g->tk) : g->tk;
@@ -674,7 +675,7 @@ static void* emu_worker(void* arg) {
 
 void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
                      const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
-                     int nthreads, float* out) {
+                     int row0, int row1, int nthreads, float* out) {
     emu_job J;
     J.q8 = q8;
     J.q_scale = q_scale;
@@ -685,6 +686,8 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
     J.kbias = kbias;
     J.g = g;
     J.causal = causal;
+    J.row0 = row0 < 0 ? 0 : row0;
+    J.row1 = row1 > g->tokens ? g->tokens : row1;
     J.out = out;
     J.next = 0;
     pthread_mutex_init(&J.mu, NULL);

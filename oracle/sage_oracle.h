@@ -124,10 +124,11 @@ int or_attention_bthd(const uint16_t* q, const uint16_t* k, const uint16_t* v, c
  * without online rescaling: logits x = S * q_scale * k_scale (+ kbias, in
  * log2 units), P = e4m3(448 * 2^(x - max)), l = sum of the unrounded P,
  * O = sum P8 * V8, out = O / l * v_scale + v_mean.  Inputs in the layouts
- * or_prepare writes; out f32 [b][t][hq][d]. */
+ * or_prepare writes; out f32 [b][t][hq][d], only rows [row0, row1) of every
+ * (b, h) written. */
 void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
                      const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
-                     int nthreads, float* out);
+                     int row0, int row1, int nthreads, float* out);
 
 /* The QKV path of one block in f64: y = x w^T + bias (host::linear,
  * platform/spl-nn/src/host.rs) then the QKV prologue (qkv::reference,
