@@ -699,6 +699,149 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
     pthread_mutex_destroy(&J.mu);
 }
 
+/* ---- online-softmax emulation (the kernels' block-by-block arithmetic) ---- */
+
+/* The reference kernel's online softmax (platform/spl-nn/cuda/sage_attn.cu:
+ * 227-344, SG_FAST_EXP): keys in blocks; S read as the float 1.5 * 2^23 + S;
+ * per block m_new = max(m, max_key fmaf(x, sc, -M * sc)) with sc = q_scale *
+ * k_scale of the key's 64-key group (merged: x = fmaf(x, sc, bias - M * sc)
+ * is the log2 logit, m_new = max(m, max x)); alpha = 2^(m - m_new);
+ * p = 2^(fmaf(x, sc, (log2 448 - m_new) + (-M * sc))); l = fmaf(l, alpha,
+ * sum p); the block's P8 V8 summed from zero and folded O = fmaf(O, alpha,
+ * PV); out = fmaf(O * (1 / l), v_scale, v_mean) (:405-420).  `block` = 64 is
+ * the reference kernel's block; 128 is this library's (one max per 128 keys,
+ * two k_scale groups).  Extensions: causal keys j <= i, GQA.  exp2 is the C
+ * library's (the kernels use ex2.approx), and each block's PV is summed in
+ * double and rounded once (the tensor cores sum in FP32), so the emulation
+ * agrees with a kernel to rounding noise, not bit for bit. */
+typedef struct {
+    const int8_t* q8;
+    const float* q_scale;
+    const int8_t* k8;
+    const float* k_scale;
+    const uint8_t* v8;
+    const float* stats;
+    const float* kbias;
+    const or_geom* g;
+    int causal, block, row0, row1;
+    float* out;
+    int64_t next;
+    pthread_mutex_t mu;
+} onl_job;
+
+static void* onl_worker(void* arg) {
+    onl_job* J = (onl_job*)arg;
+    const or_geom* g = J->g;
+    const int d = g->d, group = g->heads / g->kv_heads, nkb = g->tk_pad / OR_KBLOCK, B = J->block;
+    const int merge = J->kbias && g->merge > 1;
+    const float M = 12582912.0f, L448 = 8.807354922057604f;
+    float* vdq = (float*)malloc(sizeof(float) * (size_t)g->tk_pad * d);
+    float* xf = (float*)malloc(sizeof(float) * (size_t)B);
+    double* c = (double*)malloc(sizeof(double) * d);
+    float* o = (float*)malloc(sizeof(float) * d);
+    int64_t cur_kvh = -1;
+    const int64_t total = (int64_t)g->batch * g->heads;
+    for (;;) {
+        pthread_mutex_lock(&J->mu);
+        int64_t w = J->next++;
+        pthread_mutex_unlock(&J->mu);
+        if (w >= total) break;
+        int h = (int)(w % g->heads), b = (int)(w / g->heads);
+        int64_t bh = (int64_t)b * g->heads + h, kvh = (int64_t)b * g->kv_heads + h / group;
+        if (kvh != cur_kvh) {
+            for (int j = 0; j < g->tk_pad; j++) {
+                int blk = j / OR_KBLOCK, kl = j % OR_KBLOCK, col = (kl & ~15) + or_vpos(kl & 15);
+                for (int ch = 0; ch < d; ch++)
+                    vdq[(int64_t)j * d + ch] =
+                        or_e4m3_to_f32(J->v8[((kvh * nkb + blk) * d + ch) * (int64_t)OR_KBLOCK + col]);
+            }
+            cur_kvh = kvh;
+        }
+        const float* st = J->stats + kvh * 4 * d;
+        for (int i = J->row0; i < J->row1; i++) {
+            const int8_t* qi = J->q8 + (bh * g->tq_pad + i) * d;
+            const float qs = J->q_scale[bh * (g->tq_pad / OR_QGROUP) + i / OR_QGROUP];
+            const int nk = J->causal ? (i + 1 < g->tk ? i + 1 : g->tk) : g->tk;
+            float m = -INFINITY, l = 0.f;
+            for (int ch = 0; ch < d; ch++) o[ch] = 0.f;
+            for (int k0 = 0; k0 < nk; k0 += B) {
+                float mnew = m;
+                for (int t = 0; t < B; t++) {
+                    const int j = k0 + t;
+                    if (j >= nk) {
+                        xf[t] = -INFINITY;
+                        continue;
+                    }
+                    const int8_t* kj = J->k8 + (kvh * g->tk_pad + j) * d;
+                    int32_t sacc = 0;
+                    for (int ch = 0; ch < d; ch++) sacc += (int32_t)qi[ch] * (int32_t)kj[ch];
+                    const float sc = qs * J->k_scale[kvh * nkb + j / OR_KBLOCK];
+                    const float xm = M + (float)sacc; /* exact: |S| < 2^22 */
+                    const float lg = merge ? fmaf(xm, sc, J->kbias[j] - M * sc) : fmaf(xm, sc, -(M * sc));
+                    xf[t] = merge ? lg : xm;
+                    if (lg > mnew) mnew = lg;
+                }
+                const float alpha = exp2f(m - mnew);
+                m = mnew;
+                float sum = 0.f;
+                for (int ch = 0; ch < d; ch++) c[ch] = 0.0;
+                for (int t = 0; t < B; t++) {
+                    const int j = k0 + t;
+                    if (j >= nk) continue;
+                    float p;
+                    if (merge) {
+                        p = exp2f(xf[t] + (L448 - mnew));
+                    } else {
+                        const float sc = qs * J->k_scale[kvh * nkb + j / OR_KBLOCK];
+                        p = exp2f(fmaf(xf[t], sc, (L448 - mnew) + (-(M * sc))));
+                    }
+                    sum += p;
+                    const double p8 = (double)or_e4m3_to_f32(or_f32_to_e4m3(p));
+                    if (p8 != 0.0)
+                        for (int ch = 0; ch < d; ch++) c[ch] += p8 * (double)vdq[(int64_t)j * d + ch];
+                }
+                l = fmaf(l, alpha, sum);
+                for (int ch = 0; ch < d; ch++) o[ch] = fmaf(o[ch], alpha, (float)c[ch]);
+            }
+            const float inv = 1.0f / l;
+            float* out = J->out + (((int64_t)b * g->tokens + i) * g->heads + h) * d;
+            for (int ch = 0; ch < d; ch++) out[ch] = fmaf(o[ch] * inv, st[2 * d + ch], st[d + ch]);
+        }
+    }
+    free(vdq);
+    free(xf);
+    free(c);
+    free(o);
+    return NULL;
+}
+
+void or_sage_online(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
+                    const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
+                    int block, int row0, int row1, int nthreads, float* out) {
+    onl_job J;
+    J.q8 = q8;
+    J.q_scale = q_scale;
+    J.k8 = k8;
+    J.k_scale = k_scale;
+    J.v8 = v8;
+    J.stats = stats;
+    J.kbias = kbias;
+    J.g = g;
+    J.causal = causal;
+    J.block = block;
+    J.row0 = row0 < 0 ? 0 : row0;
+    J.row1 = row1 > g->tokens ? g->tokens : row1;
+    J.out = out;
+    J.next = 0;
+    pthread_mutex_init(&J.mu, NULL);
+    if (nthreads < 1) nthreads = 1;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * nthreads);
+    for (int i = 0; i < nthreads; i++) pthread_create(&th[i], NULL, onl_worker, &J);
+    for (int i = 0; i < nthreads; i++) pthread_join(th[i], NULL);
+    free(th);
+    pthread_mutex_destroy(&J.mu);
+}
+
 /* ------------------------------------------------------------------ metrics */
 
 /* reference.rs:201-225 */

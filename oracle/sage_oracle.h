@@ -130,6 +130,15 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
                      const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
                      int row0, int row1, int nthreads, float* out);
 
+/* The kernels' online softmax, block by block: `block` 64 is the reference
+ * kernel's (platform/spl-nn/cuda/sage_attn.cu:227-420), 128 this library's.
+ * Same inputs and output layout as or_sage_emulate; rows [row0, row1) of
+ * every (b, h).  Agrees with a kernel to rounding noise (exp2f for
+ * ex2.approx, each block's PV rounded once). */
+void or_sage_online(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
+                    const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
+                    int block, int row0, int row1, int nthreads, float* out);
+
 /* The QKV path of one block in f64: y = x w^T + bias (host::linear,
  * platform/spl-nn/src/host.rs) then the QKV prologue (qkv::reference,
  * platform/spl-nn/src/qkv.rs:306-372, generalised to head dim 128 and any

@@ -41,6 +41,7 @@ def library_path() -> str:
 
 
 ERR_INVALID = 1  # SPL_SAGE_ERR_INVALID
+NOALLOC_SCRATCH_FLOATS = 1 << 20  # the fixed scratch of spl_sage_quantize_noalloc (sage_quant.cu)
 
 
 class SageError(RuntimeError):
@@ -673,6 +674,11 @@ def quantize_noalloc(head_dim: int, shape: Shape, q: Tensor, k: Tensor, v: Tenso
     b, h, g, t, d = shape.batch, shape.heads, shape.kv, shape.tokens, head_dim
     tq_pad = (t + 127) // 128 * 128
     tk_pad = (t + 63) // 64 * 64
+    part = b * g * (tq_pad // 128) * 4 * d
+    if part > NOALLOC_SCRATCH_FLOATS:  # the library's own check, made before the outputs' sizes are looked at
+        raise SageError(ERR_INVALID, f"quantize_noalloc: batch x kv_heads x ceil(tokens/128) x 4 x head_dim = {part} "
+                                     f"floats exceeds its fixed scratch of {NOALLOC_SCRATCH_FLOATS} floats; use a "
+                                     "workspace (SageAttention.prepare)")
     need = {"q8": b * h * tq_pad * d, "q_scale": 4 * b * h * (tq_pad // 16), "k8": b * g * tk_pad * d,
             "k_scale": 4 * b * g * (tk_pad // 64), "v8": b * g * d * tk_pad, "stats": 4 * b * g * 4 * d}
     for name, t_out in (("q8", q8), ("q_scale", q_scale), ("k8", k8), ("k_scale", k_scale), ("v8", v8),

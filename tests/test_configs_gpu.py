@@ -6,15 +6,22 @@ what is checked here is what the bench times.  Gates:
   * against the reference's own kernels (oracle/_ref, compiled from the
     reference's CUDA sources; non-causal, equal head counts only): the
     quantiser bit-exact, attention cos >= 0.9995 and rel-L1 <= 1e-2;
-  * where the reference kernels cannot run (causal GQA, C4), the exact
-    emulation of the quantised arithmetic (or_sage_emulate) on our own
-    quantised tensors stands in for them: cos >= 0.9999, rel-L1 <= 5e-3,
-    on seeded query-row ranges taken from the first, middle and last tiles;
-  * f64 exact attention on the same row ranges: the reference's own gate
-    (src/sage/tests.rs:699: cos > 0.999, rel-L2 < 0.04).
-The persistent kernels carry rings, double buffers and barrier phases from
-one tile to the next; the forced-few-CTA cases (spl_sage_reserve_sms) give
-every CTA 20+ tiles on shapes the oracle finishes quickly."""
+  * where the reference kernels cannot run (causal GQA: C4), the oracle's
+    restatement of the reference kernel's online arithmetic (or_sage_online
+    with its 64-key blocks, extended with the causal mask and GQA; it
+    reproduces the reference kernels' bf16 output bit for bit on the golden
+    fixtures) stands in for them, at the same gate;
+  * the same restatement with this library's 128-key blocks: our kernel's
+    own arithmetic, to rounding noise (cos >= 0.99999, rel-L1 <= 2e-3);
+  * f64 exact attention: no less accurate than the reference's arithmetic
+    on the same rows (at C3 the x20 outlier tokens take the reference's own
+    kernel past its test gate of src/sage/tests.rs:699, so that gate is
+    asserted only on the reference generator's inputs).
+Large configurations are checked on query-row ranges from the first, a
+middle and the last tile of every (batch, head).  The persistent kernels
+carry rings, double buffers and barrier phases from one tile to the next;
+the forced-few-CTA cases (spl_sage_reserve_sms) give every CTA 16+ tiles on
+shapes the oracle finishes quickly."""
 from __future__ import annotations
 
 import numpy as np
@@ -53,23 +60,42 @@ def _row_ranges(tokens: int):
     return [(0, 128), (mid + 37, mid + 101), (last, tokens)]
 
 
-def _check_rows_against_oracles(c, x, run, *, emulate=True):
+def _bf16(a: np.ndarray) -> np.ndarray:
+    return O.bf16_to_f32(O.f32_to_bf16(np.ascontiguousarray(a, np.float32)))
+
+
+def _check_arithmetic(c, x, run, rows, *, f64=True):
+    """Our output on `rows` against our own online arithmetic (128-key
+    blocks), the reference kernel's (64-key blocks) and f64 attention.
+    Returns the three error dicts."""
     g = st.geom(c)
-    worst_emu, worst_f64 = None, None
-    for r0, r1 in _row_ranges(c.tokens):
-        ours = _rows_of(run.out, r0, r1)
-        if emulate:
-            emu = _rows_of(O.sage_emulate(run.quant, g, causal=c.causal, rows=(r0, r1)), r0, r1)
-            e = O.errors(ours, emu)
-            print(f"rows {r0}-{r1} vs emulation: {e}")
-            assert e["cos"] >= 0.9999 and e["rel_l1"] <= 5e-3, (r0, e)
-            worst_emu = e if worst_emu is None or e["rel_l1"] > worst_emu["rel_l1"] else worst_emu
-        ex = _rows_of(O.attention_bthd(x.q, x.k, x.v, g, causal=c.causal, rows=(r0, r1)), r0, r1)
-        e = O.errors(ours, ex)
-        print(f"rows {r0}-{r1} vs f64: {e}")
-        assert st.reference_gate(e), (r0, e)
-        worst_f64 = e if worst_f64 is None or e["rel_l2"] > worst_f64["rel_l2"] else worst_f64
-    return worst_emu, worst_f64
+    r0, r1 = rows
+    ours = _rows_of(run.out, r0, r1)
+    own = _bf16(_rows_of(O.sage_online(run.quant, g, block=O.OUR_BLOCK, causal=c.causal, rows=rows), r0, r1))
+    e_own = O.errors(ours, own)
+    print(f"rows {r0}-{r1} vs own arithmetic: {e_own}")
+    assert e_own["cos"] >= 0.99999 and e_own["rel_l1"] <= 2e-3, (rows, e_own)
+    ref = _rows_of(O.sage_online(run.quant, g, block=O.REF_BLOCK, causal=c.causal, rows=rows), r0, r1)
+    e_ref = O.errors(ours, ref)
+    print(f"rows {r0}-{r1} vs the reference kernel's arithmetic: {e_ref}")
+    assert st.attention_gate(e_ref), (rows, e_ref)
+    e_f64 = None
+    if f64:
+        ex = _rows_of(O.attention_bthd(x.q, x.k, x.v, g, causal=c.causal, rows=rows), r0, r1)
+        e_f64, e_ref64 = O.errors(ours, ex), O.errors(ref, ex)
+        print(f"rows {r0}-{r1} vs f64: ours {e_f64}, reference arithmetic {e_ref64}")
+        assert e_f64["rel_l2"] <= 1.05 * e_ref64["rel_l2"] + 1e-3, (rows, e_f64, e_ref64)
+        assert e_f64["cos"] >= e_ref64["cos"] - 1e-4, (rows, e_f64, e_ref64)
+    return e_own, e_ref, e_f64
+
+
+def _check_rows_against_oracles(c, x, run):
+    worst = {}
+    for rows in _row_ranges(c.tokens):
+        for name, e in zip(("own", "reference", "f64"), _check_arithmetic(c, x, run, rows)):
+            if name not in worst or e["rel_l1"] > worst[name]["rel_l1"]:
+                worst[name] = e
+    return worst
 
 
 def _against_reference_kernels(c, x, run):
@@ -87,13 +113,7 @@ def test_c1_as_specified_against_reference_kernels():
     c, x = _bench_case("C1")
     run = st.run_ours(c, x)
     _against_reference_kernels(c, x, run)
-    g = st.geom(c)
-    e = O.errors(run.out, O.attention_bthd(x.q, x.k, x.v, g))
-    print(f"C1 vs f64: {e}")
-    assert st.reference_gate(e), e
-    e2 = O.errors(run.out, O.sage_emulate(run.quant, g))
-    print(f"C1 vs emulation: {e2}")
-    assert e2["cos"] >= 0.9999 and e2["rel_l1"] <= 5e-3, e2
+    _check_arithmetic(c, x, run, (0, c.tokens))
 
 
 @pytest.mark.skipif(not O.ref_available(64), reason="oracle/_ref not built")
@@ -140,14 +160,15 @@ def test_c3_full_shape_with_outliers():
 def test_c4_full_shape_causal_gqa():
     """C4 as the bench times it (B4 Hq32 Hkv8 N8192 D128, causal, 8,192
     query tiles over 148 persistent CTAs): the quantiser bit-exact against
-    the CPU oracle, attention against the emulation and f64 on row ranges of
-    the first, middle and last tiles of every (batch, head)."""
+    the CPU oracle, attention against the reference kernel's arithmetic, our
+    own and f64 on row ranges of the first, middle and last tiles of every
+    (batch, head)."""
     c, x = _bench_case("C4")
     run = st.run_ours(c, x)
     want = O.prepare(x.q, x.k, x.v, st.geom(c))
     st.assert_quant_equal(run.quant, want, kbias=False, what="C4 quantiser")
-    emu, f64 = _check_rows_against_oracles(c, x, run)
-    print(f"C4 worst: vs emulation {emu}, vs f64 {f64}")
+    worst = _check_rows_against_oracles(c, x, run)
+    print(f"C4 worst: {worst}")
 
 
 MULTI = {
@@ -189,13 +210,11 @@ def test_persistent_multi_tile_path(name):
     print(f"{name}: {tiles} query tiles on 3 CTAs")
     assert tiles >= 48
     g = st.geom(c)
-    emu = O.sage_emulate(quant, g, causal=c.causal)
-    e = O.errors(ours, emu)
-    print(f"{name} vs emulation: {e}")
-    assert e["cos"] >= 0.9999 and e["rel_l1"] <= 5e-3, e
+    run = st.Run(ours, quant, ws, eng)
+    _check_arithmetic(c, x, run, (0, c.tokens), f64=False)
     e = O.errors(ours, O.attention_bthd(x.q, x.k, x.v, g, causal=c.causal))
     print(f"{name} vs f64: {e}")
-    assert st.reference_gate(e), e
+    assert st.reference_gate(e), e  # the reference generator's inputs: its own gate applies
     if which == "ref":
         ref, ref_quant = st.run_reference_gpu(c, x)
         st.assert_quant_equal(quant, ref_quant, what=name)

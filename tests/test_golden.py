@@ -59,3 +59,19 @@ def test_oracle_attention_matches_reference_kernels(path):
     emu = O.sage_emulate(O.prepare(x.q, x.k, x.v, g, None), g, nthreads=4)
     e2 = O.errors(ref_out, emu)
     assert e2["cos"] > 0.9999 and e2["rel_l1"] < 5e-3, e2
+
+
+@pytest.mark.parametrize("path", FILES, ids=[os.path.basename(p) for p in FILES])
+def test_online_emulation_matches_reference_kernels(path):
+    """or_sage_online with the reference kernel's 64-key blocks restates that
+    kernel's online arithmetic; against its bf16 output only rounding noise
+    is left (exp2f vs ex2.approx, the PV summation order), which the bf16
+    output almost always absorbs: most fixtures match bit for bit."""
+    f, c = _case(path)
+    x = st.make_inputs(c)
+    g = st.geom(c)
+    quant = O.prepare(x.q, x.k, x.v, g, None)
+    on64 = O.bf16_to_f32(O.f32_to_bf16(O.sage_online(quant, g, block=O.REF_BLOCK, nthreads=4)))
+    e = O.errors(f["out"], on64)
+    print(os.path.basename(path), e)
+    assert e["cos"] > 0.9999999 and e["rel_l1"] < 1e-5, e
