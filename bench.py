@@ -9,9 +9,15 @@ Llama-3-8B-shaped causal prefill attention (B4, 32 query heads, 8 KV heads,
 N=8192, head dim 128).  The metric is effective attention TOPS,
 4*B*H*N^2*D / t (the non-causal count, as the metric defines it).
 
-Multi-GPU: one process per GPU (torchrun); every rank runs its own batch
-shard of the same shape (batch x head sharding, no communication), so the
-scaling is weak and `value` is the whole-job aggregate.
+Multi-GPU: one process per GPU (torchrun).  C4 is head-sharded, as the
+path's specification asks: the job is the fixed global C4 batch and its 32
+(batch, kv head) units are split over the ranks (each rank all 4 sequences
+and 8 / N kv heads with their query heads; no communication), so the
+scaling is strong.  C1 and C3 give every rank its own batch (weak scaling).
+The C4 line also carries `ring_c5`: the C5 context-parallel ring at the same
+rank count (strong scaling over NCCL), and `c4_block`: the whole block from
+the activations (fused QKV GEMM with Q quantised in its epilogue, K/V
+quantiser, attention) on the rank's heads.
 
 Rank 0 prints ONE JSON line.  `--impl reference` times the reference's CPU
 path for this op (its f64 attention plus its quantiser, as restated in
@@ -72,6 +78,12 @@ def tensor_peak(eng):
     return i8, f8
 
 
+def fp16_accumulate_rate(eng):
+    """The FP8 E4M3 rate with an FP16 accumulator (SageAttention2++'s PV,
+    PvAccum::F16) beside the FP32 one, from the same probe."""
+    return max(eng.tensor_peak(3, 128)[0] for _ in range(2))
+
+
 def effective_flops(w, batch):
     return 4.0 * batch * w["heads"] * w["tokens"] ** 2 * w["d"]
 
@@ -90,6 +102,28 @@ def load_peaks():
             m = json.load(f)
         return m, "measured"
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def shard_of(name: str, world: int):
+    """(batch, q heads, kv heads) of one rank, and whether the job is
+    head-sharded (strong scaling: C4) or batch-replicated (weak)."""
+    w = WORKLOADS[name]
+    if name == "C4":
+        if w["kv_heads"] % world:
+            raise SystemExit(f"C4 shards its {w['kv_heads']} kv heads over the ranks: {world} does not divide them")
+        return w["batch"], w["heads"] // world, w["kv_heads"] // world, True
+    return w["batch"], w["heads"], w["kv_heads"], False
+
+
+def config_of(name: str, world: int) -> dict:
+    """The `config` of a line; the same in both arms."""
+    w = WORKLOADS[name]
+    B, Hr, Gr, sharded = shard_of(name, world)
+    return {"workload": w["desc"], "global_batch": B if sharded else B * world, "seq_len": w["tokens"],
+            "q_heads": w["heads"], "kv_heads": w["kv_heads"], "head_dim": w["d"], "causal": w["causal"],
+            "parallelism": (f"head-sharded hs{world}: each rank all {B} sequences, {Gr} kv head(s) and its {Hr} "
+                            f"query heads" if sharded else f"batch-replicated dp{world}"),
+            "l2": "inputs (0.67 GB at C4) exceed the 126 MB L2; no flush"}
 
 
 # ---------------------------------------------------------------- clocks
@@ -293,17 +327,18 @@ def run_layers(args, rank, world, local_rank):
     }
 
 
-def run_ring(args, rank, world, local_rank):
-    """C5: one long causal sequence split over the ranks (zig-zag chunks),
-    K/V passed around a ring (sota-papers-lab_b200/ring.py).  Strong
-    scaling: the whole job is one sequence whatever the rank count."""
+def ring_measure(rank, world, local_rank, steps, warmup, reserve_sms=None, e2e=True):
+    """The C5 ring (sota-papers-lab_b200/ring.py) on this rank: one long
+    causal sequence split over the ranks (zig-zag chunks), K/V passed around
+    a ring.  Device time of `steps` forwards (CUDA events on the launching
+    stream, max over ranks) and, with e2e, the same through pinned host
+    buffers.  Every rank calls it together."""
     import torch
     import torch.distributed as dist
     sage = importlib.import_module("sota-papers-lab_b200")
     ring = importlib.import_module("sota-papers-lab_b200.ring")
-    w = WORKLOADS[args.workload]
+    w = WORKLOADS["C5"]
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     B, H, G, N, D = w["batch"], w["heads"], w["kv_heads"], w["tokens"], w["d"]
     T = N // world
     stream = torch.cuda.current_stream()
@@ -319,7 +354,7 @@ def run_ring(args, rank, world, local_rank):
     k = (k + torch.randn(1, 1, G, D, generator=gb, device=dev) * w["k_bias"]).to(torch.bfloat16)
     out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
     eng = sage.SageAttention(stream, D)
-    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D, reserved_sms=args.reserve_sms)
+    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D, reserved_sms=reserve_sms)
     sq, skv = sage.Strides.bthd(T, H, D), sage.Strides.bthd(T, G, D)
     tq, tk, tv, to = sage.Tensor(q, sq), sage.Tensor(k, skv), sage.Tensor(v, skv), sage.Tensor(out, sq)
 
@@ -327,8 +362,13 @@ def run_ring(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    peaks_hw = tensor_peak(eng) if rank == 0 else (0.0, 0.0)
-    for _ in range(args.warmup):
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(warmup):
         rg.forward(tq, tk, tv, to)
     torch.cuda.synchronize()
     word = eng.status(rg.ws)
@@ -337,40 +377,53 @@ def run_ring(args, rank, world, local_rank):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             rg.forward(tq, tk, tv, to)
         e1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-
-    # end to end: this rank's Q/K/V from pinned host memory, the ring, the
-    # rank's output back to the host
-    qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
-    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    e_steps = max(1, min(args.steps, 3))
-    barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(e_steps):
-        q.copy_(qh, non_blocking=True); k.copy_(kh, non_blocking=True); v.copy_(vh, non_blocking=True)
-        rg.forward(tq, tk, tv, to)
-        oh.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item()) / e_steps
+    res = {"ms_per_step": max_over_ranks(e0.elapsed_time(e1)) / steps, "clocks": clk.summary(),
+           "reserved_sms": rg.reserved_sms, "nccl_ctas": ring.NCCL_CTAS,
+           "h2d": sum(x.numel() * x.element_size() for x in (q, k, v)), "d2h": out.numel() * out.element_size()}
+    if e2e:
+        # this rank's Q/K/V from pinned host memory, the ring, the rank's
+        # output back to the host
+        qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
+        oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        e_steps = max(1, min(steps, 3))
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(e_steps):
+            q.copy_(qh, non_blocking=True); k.copy_(kh, non_blocking=True); v.copy_(vh, non_blocking=True)
+            rg.forward(tq, tk, tv, to)
+            oh.copy_(out, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        res["e2e_ms"] = max_over_ranks(e0.elapsed_time(e1)) / e_steps
     word |= eng.status(rg.ws)
+    res["device_error_word"] = word
     rg.close()
+    eng.close()
+    return res
+
+
+def run_ring(args, rank, world, local_rank):
+    """C5: one long causal sequence split over the ranks (zig-zag chunks),
+    K/V passed around a ring (sota-papers-lab_b200/ring.py).  Strong
+    scaling: the whole job is one sequence whatever the rank count."""
+    import torch
+    sage = importlib.import_module("sota-papers-lab_b200")
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, H, G, N, D = w["batch"], w["heads"], w["kv_heads"], w["tokens"], w["d"]
+    peaks_hw = tensor_peak(sage.SageAttention(torch.cuda.current_stream(), D)) if rank == 0 else (0.0, 0.0)
+    r = ring_measure(rank, world, local_rank, args.steps, args.warmup, args.reserve_sms)
     if rank != 0:
         return None
-    step_ms = ms_max / args.steps
+    step_ms, e2e_ms = r["ms_per_step"], r["e2e_ms"]
     value = effective_flops(w, B) / (step_ms * 1e-3) / 1e12
     alg_per_rank = algorithmic_flops(w, B) / world
     achieved = alg_per_rank / (step_ms * 1e-3) / 1e12
@@ -384,8 +437,8 @@ def run_ring(args, rank, world, local_rank):
         "config": {"workload": w["desc"], "global_batch": B,
                    "seq_len": N, "q_heads": H, "kv_heads": G, "head_dim": D, "causal": True,
                    "parallelism": f"cp{world}: zig-zag chunks, one attention launch per ring step, K/V ring over "
-                                  f"NCCL send/recv in a group capped at {ring.NCCL_CTAS} CTA(s), "
-                                  f"{rg.reserved_sms} SM(s) left free for it",
+                                  f"NCCL send/recv in a group capped at {r['nccl_ctas']} CTA(s), "
+                                  f"{r['reserved_sms']} SM(s) left free for it",
                    "l2": "inputs exceed the 126 MB L2; no flush"},
         "roofline": {"bound": "tensor", "kernel": "whole ring step per GPU (quantiser, segment attention, merge)",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
@@ -393,14 +446,31 @@ def run_ring(args, rank, world, local_rank):
                      "peak_source": "measured in this run by the tcgen05 probe (lower of INT8, FP8 E4M3)",
                      "algorithmic_flops_per_gpu": alg_per_rank},
         "e2e": {"value": round(effective_flops(w, B) / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
-                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (q, k, v)),
-                "d2h_bytes_per_step": out.numel() * out.element_size(),
-                "api": "RingAttention.forward via libsplsage C ABI, pinned host buffers (rank 0's bytes)"},
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": r["h2d"] * world,
+                "d2h_bytes_per_step": r["d2h"] * world,
+                "api": "RingAttention.forward via libsplsage C ABI, pinned host buffers (every rank its own chunks)"},
         # per forward: prepare 2, K/V quantiser 2, one segment per ring step, finish 1
         "gpu_launches": (5 + world) * args.steps,
-        "clocks": clk.summary(),
-        "device_error_word": word,
+        "clocks": r["clocks"],
+        "device_error_word": r["device_error_word"],
     }
+
+
+def ring_c5_summary(rank, world, local_rank, peak):
+    """The `ring_c5` object of the C4 line: the C5 ring at this rank count."""
+    w = WORKLOADS["C5"]
+    steps = 3
+    r = ring_measure(rank, world, local_rank, steps, 3, e2e=False)
+    if rank != 0:
+        return None
+    alg_per_rank = algorithmic_flops(w, w["batch"]) / world
+    return {"workload": w["desc"], "n_gpus": world, "scaling": "strong", "steps": steps, "warmup": 3,
+            "ms_per_step": round(r["ms_per_step"], 4),
+            "value": round(effective_flops(w, w["batch"]) / (r["ms_per_step"] * 1e-3) / 1e12, 2), "unit": "TOPS",
+            "roofline_frac_per_gpu": round(alg_per_rank / (r["ms_per_step"] * 1e-3) / 1e12 / peak, 4) if peak else None,
+            "parallelism": f"cp{world}: zig-zag ring over NCCL send/recv, {r['reserved_sms']} SM(s) left to NCCL",
+            "timing": "CUDA events on the launching stream, max over ranks", "clocks": r["clocks"],
+            "device_error_word": r["device_error_word"]}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -411,9 +481,11 @@ def run_ours(args, rank, world, local_rank):
     w = WORKLOADS[args.workload]
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    B, H, G, N, D = w["batch"], w["heads"], w["kv_heads"], w["tokens"], w["d"]
+    N, D = w["tokens"], w["d"]
+    B, H, G, sharded = shard_of(args.workload, world)  # this rank's share
+    wr = dict(w, heads=H, kv_heads=G)
     stream = torch.cuda.current_stream()
-    q, k, v = make_inputs(w, B, 1234 + rank, dev)
+    q, k, v = make_inputs(wr, B, 1234 + rank, dev)
     out = torch.empty(B, N, H, D, dtype=torch.bfloat16, device=dev)
     eng = sage.SageAttention(stream, D)
     ws = eng.workspace(sage.Shape(B, H, N, G, w["causal"]))
@@ -426,14 +498,21 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     peaks_hw = tensor_peak(eng) if rank == 0 else (0.0, 0.0)
+    f16acc = fp16_accumulate_rate(eng) if rank == 0 else 0.0
     for _ in range(args.warmup):
         eng.forward(ws, tq, tk, tv, to, opts)
     torch.cuda.synchronize()
     eng.status(ws)
 
     # device-timed region: K forwards, inputs resident in HBM (Q/K/V/out are
-    # 0.67 GB, larger than the 126 MB L2, so no flush is needed)
+    # 0.67 GB at C4 on one GPU, larger than the 126 MB L2, so no flush)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -450,14 +529,16 @@ def run_ours(args, rank, world, local_rank):
         stop.record(stream)
         torch.cuda.synchronize()
     barrier()
-    ms = start.elapsed_time(stop)
+    ms_max = max_over_ranks(start.elapsed_time(stop))
     prep_ms = [a.elapsed_time(b) for a, b, _ in ev]
     attn_ms = [b.elapsed_time(c) for _, b, c in ev]
     word = eng.status(ws)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+
+    # the CPU leg (one GPU only): the reference's CPU path timed on a sample
+    # of these very inputs, and this run's output checked on the sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_leg(wr, B, q, k, v, out, nthreads=os.cpu_count() or 1)
 
     # end to end through the public API with host buffers, pipelined as a
     # serving loop would run it: step i's Q/K/V go up from pinned memory on
@@ -506,25 +587,30 @@ def run_ours(args, rank, world, local_rank):
     e1.record(d2h_s)
     torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item()) / e_steps
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e_steps
     word |= eng.status(ws)
-    h2d = sum(x.numel() * x.element_size() for x in (q, k, v))
-    d2h = out.numel() * out.element_size()
+    h2d = sum(x.numel() * x.element_size() for x in (q, k, v)) * world
+    d2h = out.numel() * out.element_size() * world
+    del bufs, views, qh, kh, vh, oh
 
-    qkv = qkv_gemm_time(eng, w, dev, stream) if w.get("qkv") else None
-    qkv8 = qkv_fp8_time(eng, w, dev, stream) if w.get("qkv") else None
+    block = qkv = qkv8 = ring_sub = None
+    if w.get("qkv"):
+        block = c4_block_time(eng, wr, B, dev, stream, rank, world, max_over_ranks)
+        qkv = qkv_gemm_time(eng, w, dev, stream) if rank == 0 else None
+        qkv8 = qkv_fp8_time(eng, w, dev, stream) if rank == 0 else None
+        del q, k, v, out, ws
+        torch.cuda.empty_cache()
+        peak_sub = min(peaks_hw) if rank == 0 else 0.0
+        ring_sub = ring_c5_summary(rank, world, local_rank, peak_sub)
 
     if rank != 0:
         return None
     peaks, peak_src = load_peaks()
-    global_batch = B * world
+    cfg = config_of(args.workload, world)
     step_ms = ms_max / args.steps
-    value = effective_flops(w, global_batch) / (step_ms * 1e-3) / 1e12
+    value = effective_flops(w, cfg["global_batch"]) / (step_ms * 1e-3) / 1e12
     attn_avg = statistics.mean(attn_ms)
-    alg = algorithmic_flops(w, B)
+    alg = algorithmic_flops(wr, B)  # one attention launch: this rank's heads
     achieved = alg / (attn_avg * 1e-3) / 1e12
     # The INT8 / FP8 dense tcgen05 rates are not in MEASURED_PEAKS.json: they
     # are measured here by the library's probe (one CTA per SM issuing
@@ -537,17 +623,15 @@ def run_ours(args, rank, world, local_rank):
         qkv["peak_source"] = f"{peak_src} bf16_tflops (cuBLAS bf16 burst)"
     traffic = None
     tf = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-    if os.path.exists(tf):
+    if os.path.exists(tf) and world == 1:
         with open(tf) as f:
             traffic = json.load(f).get(args.workload)
     line = {
         "metric": metric_of(args.workload),
         "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8/e4m3 (fp32 accumulate; bf16 in/out)", "data": "synthetic (seeded torch.randn on device)",
-        "config": {"workload": w["desc"], "global_batch": global_batch, "seq_len": N, "q_heads": H, "kv_heads": G,
-                   "head_dim": D, "causal": w["causal"], "parallelism": f"batch-sharded dp{world}",
-                   "l2": "inputs (0.67 GB per rank at C4) exceed the 126 MB L2; no flush"},
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None, "dtype": "int8/e4m3 (fp32 accumulate; bf16 in/out)",
+        "data": "synthetic (seeded torch.randn on device)", "config": cfg,
         "roofline": {"bound": "tensor", "kernel": "sp_attn (tcgen05 kind::i8 QK + kind::f8f6f4 PV)",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -556,15 +640,21 @@ def run_ours(args, rank, world, local_rank):
                                     f"{2 * peaks['bf16_tflops']:.0f}",
                      "frac_of_2x_measured_bf16": round(achieved / (2 * peaks["bf16_tflops"]), 4),
                      "algorithmic_flops_per_launch": alg, "attn_ms_avg": round(attn_avg, 4),
-                     "prepare_ms_avg": round(statistics.mean(prep_ms), 4)},
-        "e2e": {"value": round(effective_flops(w, global_batch) / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
-                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                     "prepare_ms_avg": round(statistics.mean(prep_ms), 4),
+                     "fp8_rate_with_fp16_accumulator": round(f16acc, 1)},
+        "e2e": {"value": round(effective_flops(w, cfg["global_batch"]) / (e2e_ms * 1e-3) / 1e12, 2),
+                "unit": "TOPS", "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
                 "api": "SageAttention.forward via libsplsage C ABI, pinned host buffers; uploads, compute and "
-                       "downloads of consecutive steps overlapped on three streams"},
+                       "downloads of consecutive steps overlapped on three streams (every rank its own share)"},
         "gpu_launches": 4 * args.steps,
         "clocks": clk.summary(),
         "device_error_word": word,
     }
+    if cpu is not None:
+        line["cpu_baseline"], line["parity"] = cpu
+    if block is not None:
+        line["c4_block"] = block
     if qkv is not None:
         line["qkv_gemm"] = qkv
     if qkv8 is not None:
@@ -573,7 +663,78 @@ def run_ours(args, rank, world, local_rank):
         qkv8["peak_source"] = "FP8 E4M3 tcgen05 rate measured in this run by the probe"
         qkv8["ln_frac_of_hbm"] = round(qkv8["ln_gbs"] / peaks["hbm_gbs"], 4)
         line["qkv_fp8"] = qkv8
+    if ring_sub is not None:
+        line["ring_c5"] = ring_sub
     return line
+
+
+def c4_block_time(eng, wr, B, dev, stream, rank, world, max_over_ranks, iters=5):
+    """The C4 block on this rank's heads, from the activations: x [B*N][4096]
+    (LayerNorm-normalised N(0,1)) -> the fused QKV GEMM (W [(Hq+2Hkv)*128]
+    [4096] ~ N(0, 0.02^2), RoPE theta 5e5) with Q quantised in its epilogue
+    and no bf16 Q written (spl_sage_qkv_gemm_quant) -> the K/V quantiser ->
+    causal attention.  Also the same block unfused (GEMM writing bf16 Q, K, V,
+    then the whole quantiser), so the removed Q round trip shows.  CUDA
+    events, max over ranks."""
+    import torch
+    sage = importlib.import_module("sota-papers-lab_b200")
+    H, G, N, D = wr["heads"], wr["kv_heads"], wr["tokens"], wr["d"]
+    hidden = wr["qkv"]["hidden"]
+    n_out = (H + 2 * G) * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(97 + rank)
+    x = torch.randn(B * N, hidden, generator=g, device=dev)
+    x = ((x - x.mean(1, keepdim=True)) / x.std(1, keepdim=True)).to(torch.bfloat16)
+    wt = (torch.randn(n_out, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    rope = torch.from_numpy(sage.rope_table_1d(wr["qkv"]["rope_theta"], D, N)).to(dev)
+    q = torch.empty(B, N, H, D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(B, N, G, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    out = torch.empty_like(q)
+    ws = eng.workspace(sage.Shape(B, H, N, G, True))
+    sq, skv = sage.Strides.bthd(N, H, D), sage.Strides.bthd(N, G, D)
+    to = sage.Tensor(out, sq)
+
+    def fused():
+        eng.qkv_gemm_quant(ws, x, wt, None, rope, None, k, v, rope_half=D // 2, frame_len=N)
+
+    def unfused():
+        eng.qkv_gemm(x, wt, None, rope, q, k, v, batch=B, tokens=N, heads=H, kv_heads=G, rope_half=D // 2,
+                     frame_len=N)
+        eng.prepare(ws, sage.Tensor(q, sq), sage.Tensor(k, skv), sage.Tensor(v, skv))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / iters)
+
+    t_block = timed(lambda: (fused(), eng.attend(ws, to)))
+    t_fused = timed(fused)
+    t_unfused = timed(unfused)
+    word = eng.status(ws)
+    del x, wt, q, k, v, out
+    ws.close()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    full = WORKLOADS["C4"]
+    gemm_flops = 2.0 * B * N * hidden * (full["heads"] + 2 * full["kv_heads"]) * D  # whole job
+    attn_flops = algorithmic_flops(full, B)
+    return {"what": "x -> fused QKV GEMM (Q to INT8 in its epilogue, no bf16 Q) -> K/V quantiser -> causal "
+                    "attention, this rank's heads; whole-job rates",
+            "ms": round(t_block, 4),
+            "value": round(effective_flops(full, B) / (t_block * 1e-3) / 1e12, 2), "unit": "TOPS",
+            "tflops_gemm_plus_attention": round((gemm_flops + attn_flops) / (t_block * 1e-3) / 1e12, 1),
+            "gemm_quant_ms": round(t_fused, 4), "unfused_gemm_then_quantiser_ms": round(t_unfused, 4),
+            "q_round_trip_bytes_removed": B * N * full["heads"] * D * 2 // world * 2,
+            "gpu_launches_per_block": 5, "device_error_word": word}
 
 
 def qkv_gemm_time(eng, w, dev, stream, iters=10):
@@ -700,6 +861,65 @@ def cpu_sample_time(w, chunks, heads_sample, nthreads, seed=7):
     return full, desc
 
 
+def cpu_leg(w, batch, q, k, v, out, nthreads, chunks=96, heads_sample=8, parity_runs=8, seed=7):
+    """The CPU baseline on a bounded sample of the bench's own inputs, and
+    the parity of this run's output on the same sample.  The reference's CPU
+    path (the oracle port: bit-exact quantiser + f64 attention, C, all host
+    threads) runs on batch item 0 and its first `heads_sample` query heads
+    (with their kv heads): the quantiser over the whole sequence, the
+    attention on `chunks` seeded runs of 64 query rows; its time is
+    extrapolated to the whole job by (causal) key-pair and head count.  The
+    GPU output of the first `parity_runs` runs is compared with that f64
+    attention and with the oracle's restatement of the reference kernel's
+    online arithmetic (or_sage_online, 64-key blocks) on the quantised sample.
+    Returns (cpu_baseline, parity)."""
+    from oracle import oracle as O
+    N, D, H, G = w["tokens"], w["d"], w["heads"], w["kv_heads"]
+    hs = min(heads_sample, H)
+    gs = max(1, hs * G // H)
+    bits = lambda t: t.contiguous().view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+    qs, ks, vs = bits(q[0:1, :, :hs]), bits(k[0:1, :, :gs]), bits(v[0:1, :, :gs])
+    ours_all = O.bf16_to_f32(bits(out[0:1, :, :hs]))
+    g = O.make_geom(1, hs, gs, N, D, O.bthd_strides(N, hs, D), O.bthd_strides(N, gs, D), O.bthd_strides(N, gs, D))
+    t0 = time.perf_counter()
+    quant = O.prepare(qs, ks, vs, g)
+    t_quant = time.perf_counter() - t0
+    rng = np.random.default_rng(seed)
+    run = min(64, N)
+    starts = [int(r) for r in rng.choice(max(1, N - run + 1), size=chunks, replace=True)]
+    pairs_sample = 0
+    t_attn = 0.0
+    got, f64, ref = [], [], []
+    for i, r0 in enumerate(starts):
+        t0 = time.perf_counter()
+        ex = O.attention_bthd(qs, ks, vs, g, causal=w["causal"], rows=(r0, r0 + run), nthreads=nthreads)
+        t_attn += time.perf_counter() - t0
+        pairs_sample += sum((r + 1) if w["causal"] else N for r in range(r0, r0 + run))
+        if i < parity_runs:
+            got.append(ours_all[:, r0:r0 + run])
+            f64.append(ex[:, r0:r0 + run])
+            on = O.sage_online(quant, g, block=O.REF_BLOCK, causal=w["causal"], rows=(r0, r0 + run),
+                               nthreads=nthreads)
+            ref.append(on[:, r0:r0 + run])
+    pairs_full = (N * (N + 1) // 2 if w["causal"] else N * N) * batch * H
+    full = t_attn * pairs_full / (pairs_sample * hs) + t_quant * (batch * H) / hs
+    value = effective_flops(w, batch) / full / 1e12
+    desc = (f"oracle port (f64 attention + bit-exact quantiser, C -O2, {nthreads} threads) on the bench's own "
+            f"inputs: batch 0, {hs} q heads / {gs} kv heads, {chunks} seeded runs of {run} query rows for the "
+            f"attention, the full sequence for the quantiser; measured {t_attn + t_quant:.2f} s, extrapolated by "
+            f"(causal) key-pair count and head count")
+    cpu = {"value": value, "unit": "TOPS", "cores": nthreads, "kind": "port", "sample": desc}
+    got, f64, ref = (np.ascontiguousarray(np.concatenate(a, axis=1)) for a in (got, f64, ref))
+    e64, eref = O.errors(got, f64), O.errors(got, ref)
+    rnd = lambda e: {k2: round(float(e[k2]), 6) for k2 in ("cos", "rel_l1", "rel_l2")}
+    parity = {"rows": f"{len(starts[:parity_runs])} runs of {run} query rows x {hs} q heads of batch 0 of the "
+                      f"timed output",
+              "vs_f64": rnd(e64), "vs_reference_kernel_arithmetic": rnd(eref),
+              "gate": "vs the reference kernel's arithmetic: cos >= 0.9995, rel-L1 <= 1e-2",
+              "gate_ok": bool(eref["cos"] >= 0.9995 and eref["rel_l1"] <= 1e-2)}
+    return cpu, parity
+
+
 def cpu_qkv_sample_time(w, rows, nthreads, seed=7):
     """Times the CPU port of one layer's QKV GEMM + prologue (f64, the
     oracle's restatement of host::linear and qkv::reference) on `rows`
@@ -735,14 +955,19 @@ def run_reference(args, rank, world):
         if i >= args.warmup:
             times.append(full)
     t = statistics.median(times)
-    value = w.get("layers", 1) * effective_flops(w, w["batch"]) / t / 1e12
+    # the same job as our arm's line at this rank count (its config)
+    cfg = config_of(args.workload, world) if args.workload not in ("C2", "C5") else {
+        "workload": w["desc"], "global_batch": w["batch"], "seq_len": w["tokens"], "parallelism": "host cores"}
+    jobs = cfg["global_batch"] / w["batch"]
+    t *= jobs
+    value = w.get("layers", 1) * effective_flops(w, cfg["global_batch"]) / t / 1e12
+    sharded = args.workload in ("C4", "C5")
     return {
         "impl": "reference", "metric": metric_of(args.workload),
         "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f64 (reference CPU path)", "data": "synthetic (seeded numpy normal)",
-        "config": {"workload": w["desc"], "global_batch": w["batch"], "seq_len": w["tokens"],
-                   "parallelism": "host cores"},
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "vs_baseline": None, "dtype": "f64 (reference CPU path)", "data": "synthetic (seeded numpy normal)",
+        "config": cfg,
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": nthreads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -781,7 +1006,7 @@ def main():
     try:
         runner = {"C5": run_ring, "C2": run_layers}.get(args.workload, run_ours)
         line = runner(args, rank, world, local_rank)
-        if line is not None and world == 1 and not args.no_cpu_baseline:
+        if line is not None and world == 1 and not args.no_cpu_baseline and "cpu_baseline" not in line:
             full, desc = cpu_sample_time(WORKLOADS[args.workload], chunks=96, heads_sample=8,
                                          nthreads=os.cpu_count() or 1)
             v = effective_flops(WORKLOADS[args.workload], WORKLOADS[args.workload]["batch"]) / full / 1e12

@@ -255,9 +255,15 @@ int spl_sage_rows_fp8(spl_sage* s, const void* y, int64_t rows, int64_t c, int64
 int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const void* w8, const float* w_scale,
                         const void* bias, int64_t m, int64_t n, int64_t k, void* y);
 
-/* spl_sage_qkv_gemm into q, k, v (bf16 scratch the caller owns), then
- * spl_sage_prepare of ws from them: the block's whole QKV path up to the
- * quantised tensors the attention reads. */
+/* The block's whole QKV path up to the quantised tensors the attention
+ * reads: Gemm::linear_bf16 + QkvPrologue::run + SageAttention::prepare
+ * (gemm.rs:268-292, qkv.rs:228-301, mod.rs:673-836).  With the SM-pair
+ * GEMMs (the default), dense keys, no QK LayerNorm and tokens a multiple of
+ * 16, Q is quantised inside the GEMM's epilogue (INT8, one scale per 16
+ * rows, bytes equal to spl_sage_prepare's on the bf16 Q written here) and
+ * the quantiser then reads only K and V; q may then be NULL (Q is not
+ * written in bf16 at all).  Otherwise spl_sage_qkv_gemm into q, k, v (bf16
+ * scratch the caller owns), then spl_sage_prepare of ws from them. */
 int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_shape* shape, const void* x,
                             const void* w, const void* bias, const float* rope, void* q, void* k, void* v,
                             const spl_sage_options* opts);
@@ -411,7 +417,8 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
  * platform/spl-nn/cuda/sage_peak.cu, measured by src/sage/tests.rs:758-794):
  * one CTA per SM issues `iters` x 4 back-to-back tcgen05.mma of M=128, N=n
  * (64, 128 or 256), 32 bytes of K, kind 0 = i8 -> s32, 1 = f8f6f4 e4m3 -> f32,
- * 2 = f16 (bf16) -> f32.  Returns the rate over all SMs in tera-ops/s and the
+ * 2 = f16 (bf16) -> f32, 3 = f8f6f4 e4m3 -> f16 (the FP16 PV accumulator of
+ * SageAttention2++, PvAccum::F16).  Returns the rate over all SMs in tera-ops/s and the
  * cycles per instruction of SM 0.  Synchronises the engine's stream. */
 int spl_sage_tensor_peak(spl_sage* s, int kind, int n, int iters, double* tops, double* cycles_per_mma);
 

@@ -393,23 +393,29 @@ def causal_flops(batch, heads, n, d) -> float:
 
 # ---------------------------------------------------------------- reference GPU oracle
 
-_ref_libs: dict[int, ctypes.CDLL] = {}
+_ref_libs: dict[tuple, ctypes.CDLL] = {}
 
 
-def ref_available(d: int) -> bool:
-    return os.path.exists(os.path.join(HERE, "_ref", f"libsage_ref_d{d}.so"))
+def _ref_name(d: int, pv16: bool) -> str:
+    return os.path.join(HERE, "_ref", f"libsage_ref_d{d}{'_pv16' if pv16 else ''}.so")
 
 
-def ref_lib(d: int) -> ctypes.CDLL:
-    if d not in _ref_libs:
-        L = ctypes.CDLL(os.path.join(HERE, "_ref", f"libsage_ref_d{d}.so"))
+def ref_available(d: int, pv16: bool = False) -> bool:
+    return os.path.exists(_ref_name(d, pv16))
+
+
+def ref_lib(d: int, pv16: bool = False) -> ctypes.CDLL:
+    """The reference's kernels for head dim d (SG_PV16 = pv16)."""
+    key = (d, pv16)
+    if key not in _ref_libs:
+        L = ctypes.CDLL(_ref_name(d, pv16))
         P = ctypes.c_void_p
         L.ref_sage_run.restype = ctypes.c_int
         L.ref_sage_run.argtypes = [P, P, P, P, P, P, ctypes.c_float, ctypes.c_float, ctypes.c_float] + [P] * 10
         L.ref_sage_attend.restype = ctypes.c_int
         L.ref_sage_attend.argtypes = [P, P, ctypes.c_float, ctypes.c_float] + [P] * 9
-        _ref_libs[d] = L
-    return _ref_libs[d]
+        _ref_libs[key] = L
+    return _ref_libs[key]
 
 
 def ref_dims(g: Geom) -> np.ndarray:

@@ -12,8 +12,9 @@
 // CTAs; the epilogue warps (4-11 for E4M3, 4-7 for bf16) read their own
 // CTA's accumulator (rows rank * 128 + quarter * 32 + lane; with eight,
 // warps 4-7 take channels 0-127 of the tile and warps 8-11 channels 128-255)
-// and run the epilogue of qkv_gemm.cu, then tell the leader the accumulator
-// is free.  Every mbarrier wait is bounded; both CTAs always
+// and run the epilogue of qkv_gemm.cu (for spl_sage_qkv_gemm_quant also
+// quantising Q to INT8 with its 16-row scales, so that the quantiser only
+// reads K and V), then tell the leader the accumulator is free.  Every mbarrier wait is bounded; both CTAs always
 // reach the closing cluster barrier, after which TMEM is freed.
 #include <atomic>
 
@@ -108,7 +109,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 
 }  // namespace
 
-template <int D, int HALF, bool FP8>
+template <int D, int HALF, bool FP8, bool QQ>
 __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
     sp_qkv_gemm_2sm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                     const uint16_t* __restrict__ bias, const float2* __restrict__ rope,
@@ -313,7 +314,77 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                     a1 = a * cs.z - b * cs.w;
                     b1 = b * cs.z + a * cs.w;
                 };
-                if (HALF >= 32) {
+                if (QQ && part == 0) {
+                    // Q also quantised here, as sp_prep's Q role would from the
+                    // bf16 Q this epilogue writes (sage_quant.cu prep_q: one
+                    // scale per 16 rows, 127 / amax, round to nearest even,
+                    // clamp to +-127, q_scale = amax / 127 * q_mul).  The
+                    // head's bf16 values stay in registers (packed) until the
+                    // 16-row maximum is known; lanes 0-15 and 16-31 of a warp
+                    // are two groups of consecutive rows.
+                    uint32_t qp[D / 2];
+                    float qmax = 0.f;
+                    auto keep = [&](int c, const float (&x)[32]) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const uint32_t w = pack_bf16x2(x[e], x[e + 1]);
+                            qp[(c + e) / 2] = w;
+                            qmax = fmaxf(qmax, fmaxf(fabsf(__uint_as_float(w << 16)),
+                                                     fabsf(__uint_as_float(w & 0xffff0000u))));
+                        }
+                    };
+                    if (HALF >= 32) {
+#pragma unroll
+                        for (int c = 0; c < D; c += 32) {
+                            if (c & HALF) continue;
+                            float xa[32], xb[32];
+                            load(c, xa);
+                            load(c + HALF, xb);
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) rot2(c + i, xa[i], xb[i], xa[i + 1], xb[i + 1]);
+                            if (q_out) {
+                                store(c, xa);
+                                store(c + HALF, xb);
+                            }
+                            keep(c, xa);
+                            keep(c + HALF, xb);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < D; c += 32) {
+                            float xa[32];
+                            load(c, xa);
+                            if (HALF) {
+#pragma unroll
+                                for (int i = 0; i < HALF; i += 2)
+                                    rot2(c + i, xa[i], xa[i + HALF], xa[i + 1], xa[i + HALF + 1]);
+                            }
+                            if (q_out) store(c, xa);
+                            keep(c, xa);
+                        }
+                    }
+#pragma unroll
+                    for (int o = 1; o < 16; o <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
+                    const float inv = qmax > 0.f ? 127.0f / qmax : 0.f;
+                    if (row < g.m) {
+                        const long long bhq = (long long)bb * g.hq + head;
+                        int8_t* q8row = g.q8 + (bhq * g.tq_pad + tok) * D;
+                        auto lo = [](uint32_t w) { return __uint_as_float(w << 16); };
+                        auto hi = [](uint32_t w) { return __uint_as_float(w & 0xffff0000u); };
+#pragma unroll
+                        for (int i = 0; i < D / 16; i++) {
+                            const uint32_t* p = qp + 8 * i;
+                            const uint4 w = make_uint4(
+                                s8x4(lo(p[0]) * inv, hi(p[0]) * inv, lo(p[1]) * inv, hi(p[1]) * inv),
+                                s8x4(lo(p[2]) * inv, hi(p[2]) * inv, lo(p[3]) * inv, hi(p[3]) * inv),
+                                s8x4(lo(p[4]) * inv, hi(p[4]) * inv, lo(p[5]) * inv, hi(p[5]) * inv),
+                                s8x4(lo(p[6]) * inv, hi(p[6]) * inv, lo(p[7]) * inv, hi(p[7]) * inv));
+                            *reinterpret_cast<uint4*>(q8row + 16 * i) = w;
+                        }
+                        if ((lane & 15) == 0)
+                            g.q_scale[bhq * (g.tq_pad / QGROUP) + tok / QGROUP] = (qmax * (1.0f / 127.0f)) * g.q_mul;
+                    }
+                } else if (HALF >= 32) {
                     // chunk c and its partner chunk c + HALF
 #pragma unroll 1
                     for (int c = 0; c < D; c += 32) {
@@ -356,11 +427,11 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
     if (warp == 1) tmem_dealloc_pair(tmem, 2 * BN);
 }
 
-template <int D, int HALF, bool FP8>
+template <int D, int HALF, bool FP8, bool QQ>
 static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, const float* x_scale,
                           const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
                           const QkvGeom& g, cudaStream_t st) {
-    auto kern = sp_qkv_gemm_2sm<D, HALF, FP8>;
+    auto kern = sp_qkv_gemm_2sm<D, HALF, FP8, QQ>;
     static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
@@ -396,27 +467,29 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     return cudaLaunchKernelEx(&cfg, kern, maps.x, maps.w, bias, (const float2*)rope, x_scale, w_scale, q, k, v, err, g);
 }
 
-template <bool FP8>
+template <bool FP8, bool QQ>
 static cudaError_t qkv2_dispatch(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
                                  const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
                                  uint32_t* err, const QkvGeom& g, cudaStream_t st) {
     const int half = rope ? g.rope_half : 0;
     if (d == 64) {
-        if (half == 0) return qkv2_t<64, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-        if (half == 16) return qkv2_t<64, 16, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-        if (half == 32) return qkv2_t<64, 32, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 0) return qkv2_t<64, 0, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 16) return qkv2_t<64, 16, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 32) return qkv2_t<64, 32, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
         return cudaErrorInvalidValue;
     }
-    if (half == 0) return qkv2_t<128, 0, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-    if (half == 64) return qkv2_t<128, 64, FP8>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    if (half == 0) return qkv2_t<128, 0, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    if (half == 64) return qkv2_t<128, 64, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
     return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_qkv_gemm_2sm(int d, bool fp8, const QkvMaps& maps, const uint16_t* bias, const float* rope,
                                 const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
                                 uint32_t* err, const QkvGeom& g, cudaStream_t st) {
-    return fp8 ? qkv2_dispatch<true>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st)
-               : qkv2_dispatch<false>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    if (fp8) return qkv2_dispatch<true, false>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    // bf16: with g.q8 set, Q is quantised in the epilogue (q may then be null)
+    return g.q8 ? qkv2_dispatch<false, true>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st)
+                : qkv2_dispatch<false, false>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
 }
 
 }  // namespace sp

@@ -403,7 +403,8 @@ static int build_geom(spl_sage* s, const spl_sage_ws* ws, const spl_sage_tensor&
     const int64_t D = s->head_dim;
     const spl_sage_shape& sh = ws->shape;
     int rc;
-    if ((rc = check_tensor("Q", q.data, q.len, q.batch, q.token, q.head, sh, sh.heads, D))) return rc;
+    // (a null Q: quantised elsewhere, by the QKV GEMM's epilogue)
+    if (q.data && (rc = check_tensor("Q", q.data, q.len, q.batch, q.token, q.head, sh, sh.heads, D))) return rc;
     if ((rc = check_tensor("K", k.data, k.len, k.batch, k.token, k.head, sh, sh.kv_heads, D))) return rc;
     if ((rc = check_tensor("V", v.data, v.len, v.batch, v.token, v.head, sh, sh.kv_heads, D))) return rc;
     if (o.qk_norm_params && o.qk_norm_len < 4 * D)
@@ -548,8 +549,8 @@ int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes) {
 
 int spl_sage_tensor_peak(spl_sage* s, int kind, int n, int iters, double* tops, double* cycles_per_mma) {
     if (!s || !tops) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_tensor_peak: NULL argument");
-    if (kind < 0 || kind > 2 || !(n == 64 || n == 128 || n == 256) || iters <= 0)
-        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_tensor_peak: kind 0..2, n 64/128/256, iters > 0");
+    if (kind < 0 || kind > 3 || !(n == 64 || n == 128 || n == 256) || iters <= 0)
+        return fail(SPL_SAGE_ERR_INVALID, "spl_sage_tensor_peak: kind 0..3, n 64/128/256, iters > 0");
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, s->device);
     void* scratch = nullptr;
@@ -776,13 +777,47 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     if (ws->shape.batch != sh.batch || ws->shape.tokens != sh.tokens || ws->shape.heads != sh.heads ||
         ws->shape.kv_heads != G)
         return fail(SPL_SAGE_ERR_INVALID, "qkv: the workspace was made for another shape");
-    int rc = spl_sage_qkv_gemm(s, shape, x, w, bias, rope, q, k, v);
-    if (rc) return rc;
     const int64_t D = s->head_dim;
     spl_sage_tensor tq = {q, sh.batch * sh.tokens * sh.heads * D, sh.tokens * sh.heads * D, sh.heads * D, D};
     spl_sage_tensor tk = {k, sh.batch * sh.tokens * G * D, sh.tokens * G * D, G * D, D};
     spl_sage_tensor tv = {v, sh.batch * sh.tokens * G * D, sh.tokens * G * D, G * D, D};
-    return spl_sage_prepare(s, ws, tq, tk, tv, opts);
+    // Q quantised in the GEMM's epilogue (SM-pair kernel, dense keys, no QK
+    // LayerNorm, 16-row scale groups that never straddle two sequences); the
+    // quantiser then only reads K and V.  Otherwise: the GEMM, then the whole
+    // quantiser on its bf16 output.
+    const bool fused = s->gemm_pairs && ws->merge.stride <= 1 && !(opts && opts->qk_norm_params) &&
+                       sh.tokens % QGROUP == 0;
+    if (!fused) {
+        if (!q) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm_quant: NULL q needs the fused path");
+        int rc = spl_sage_qkv_gemm(s, shape, x, w, bias, rope, q, k, v);
+        if (rc) return rc;
+        return spl_sage_prepare(s, ws, tq, tk, tv, opts);
+    }
+    if (!x || !w || !k || !v) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm_quant: NULL argument");
+    sp::Geom ag;
+    const float* ln = nullptr;
+    int rc = build_geom(s, ws, tq, tk, tv, opts, &ag, &ln);
+    if (rc) return rc;
+    sp::QkvGeom g;
+    if ((rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g))) return rc;
+    if (((uintptr_t)bias | (uintptr_t)rope) % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "qkv: bias and RoPE table must be 16-byte aligned");
+    g.q8 = ws->buf.q8;
+    g.q_scale = ws->buf.q_scale;
+    g.tq_pad = (int)ws->tq_pad;
+    g.q_mul = ag.q_mul;
+    sp::QkvMaps maps;
+    rc = make_map_bf16_2d(&maps.x, x, g.k, g.m, (uint64_t)g.k * 2, 64, 128);
+    if (rc == SPL_SAGE_OK) rc = make_map_bf16_2d(&maps.w, w, g.k, g.n, (uint64_t)g.k * 2, 64, 128);
+    if (rc != SPL_SAGE_OK) return rc;
+    cudaError_t e = sp::launch_qkv_gemm_2sm(s->head_dim, false, maps, (const uint16_t*)bias, rope, nullptr, nullptr,
+                                            (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
+    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, ws->buf, ag, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
+    ws->geom = ag;
+    ws->prepared = true;
+    return SPL_SAGE_OK;
 }
 
 int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const spl_sage_shape* shape,

@@ -300,7 +300,7 @@ __device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc)
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt, int M, int N) {
     return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-constexpr uint32_t C_F32 = 1, C_S32 = 2;
+constexpr uint32_t C_F16 = 0, C_F32 = 1, C_S32 = 2;
 constexpr uint32_t F_E4M3 = 0, F_S8 = 1, F_BF16 = 1;
 
 // Shared-memory matrix descriptor for a K-major operand tile in the

@@ -70,6 +70,13 @@ struct QkvGeom {
     int m, n, k, tokens;
     int hq, hkv, frame_len, rope_half;
     int max_ctas;  // persistent CTAs at most (0: one per SM)
+    // Q quantised in the epilogue (spl_sage_qkv_gemm_quant; nullptr: not):
+    // q8 i8 [b][hq][tq_pad][D] and q_scale f32 [b][hq][tq_pad/16], the
+    // workspace layouts, from the bf16-rounded Q exactly as sp_prep would.
+    int8_t* q8;
+    float* q_scale;
+    int tq_pad;
+    float q_mul;
 };
 
 struct QkvMaps {
@@ -102,6 +109,10 @@ cudaError_t launch_rows_fp8(const uint16_t* y, long long ld, long long c, int ro
 cudaError_t noalloc_part_buffer(float** out);
 size_t noalloc_part_capacity();
 
+// The quantiser without its Q role (Q already quantised by the QKV GEMM's
+// epilogue): K/V statistics, finalize, K/V quantisation.
+cudaError_t launch_prepare_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
+                              const Geom& g, cudaStream_t st);
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                            const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);

@@ -5,7 +5,8 @@
 // roofline denominators the benchmark reports beside the datasheet figures.
 //
 // Kinds: 0 = kind::i8 (INT8 x INT8 -> S32), 1 = kind::f8f6f4 (E4M3 x E4M3 ->
-// F32), 2 = kind::f16 (BF16 x BF16 -> F32).  M = 128, N in {64, 128, 256},
+// F32), 2 = kind::f16 (BF16 x BF16 -> F32), 3 = kind::f8f6f4 (E4M3 x E4M3 ->
+// F16: the accumulator SageAttention2++'s FP16 PV uses).  M = 128, N in {64, 128, 256},
 // K = 32 bytes per instruction (32 8-bit / 16 16-bit elements), operands
 // K-major with 128-byte swizzle; the shared memory holds zeros.
 #include "sage_dev.cuh"
@@ -38,6 +39,7 @@ __global__ void __launch_bounds__(128, 1) sp_peak(int iters, uint32_t* err, unsi
     if (threadIdx.x == 0) {
         constexpr uint32_t IDESC = KIND == 0   ? make_idesc(C_S32, F_S8, F_S8, 128, N)
                                    : KIND == 1 ? make_idesc(C_F32, F_E4M3, F_E4M3, 128, N)
+                                   : KIND == 3 ? make_idesc(C_F16, F_E4M3, F_E4M3, 128, N)
                                                : make_idesc(C_F32, F_BF16, F_BF16, 128, N);
         const unsigned long long t0 = clock64();
         for (int it = 0; it < iters; it++) {
@@ -47,7 +49,7 @@ __global__ void __launch_bounds__(128, 1) sp_peak(int iters, uint32_t* err, unsi
                 const uint64_t a = smem_desc(sA + kk * 32, 1024, SWZ_128B), b = smem_desc(sB + kk * 32, 1024, SWZ_128B);
                 if (KIND == 0)
                     umma_i8(d, a, b, IDESC, kk > 0);
-                else if (KIND == 1)
+                else if (KIND == 1 || KIND == 3)
                     umma_f8(d, a, b, IDESC, kk > 0);
                 else
                     umma_bf16(d, a, b, IDESC, kk > 0);
@@ -80,6 +82,9 @@ cudaError_t launch_peak(int kind, int n, int iters, int sms, uint32_t* err, unsi
     if (kind == 1) return n == 64 ? peak_t<1, 64>(iters, sms, err, cycles, st)
                           : n == 128 ? peak_t<1, 128>(iters, sms, err, cycles, st)
                                      : peak_t<1, 256>(iters, sms, err, cycles, st);
+    if (kind == 3) return n == 64 ? peak_t<3, 64>(iters, sms, err, cycles, st)
+                          : n == 128 ? peak_t<3, 128>(iters, sms, err, cycles, st)
+                                     : peak_t<3, 256>(iters, sms, err, cycles, st);
     return n == 64 ? peak_t<2, 64>(iters, sms, err, cycles, st)
            : n == 128 ? peak_t<2, 128>(iters, sms, err, cycles, st)
                       : peak_t<2, 256>(iters, sms, err, cycles, st);

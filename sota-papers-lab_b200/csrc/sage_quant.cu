@@ -14,7 +14,9 @@
 // as two roles of one launch).
 //
 // Three launches, all HBM-bound:
-//   sp_prep      grid (q_tiles, heads + kv_heads, batch)
+//   sp_prep      grid (q_tiles, heads + kv_heads, batch); without its Q
+//                role (Q quantised in the QKV GEMM's epilogue) (q_tiles,
+//                kv_heads, batch)
 //   sp_finalize  grid (kv_heads, batch)
 //   sp_quant_kv  grid (tk_pad / 64, kv_heads, batch)
 #include <mutex>
@@ -213,12 +215,14 @@ template <int D>
 __global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
                                                const uint16_t* __restrict__ v, const float* __restrict__ ln,
                                                int8_t* __restrict__ q8, float* __restrict__ q_scale,
-                                               float* __restrict__ part, const Geom g) {
+                                               float* __restrict__ part, const Geom g, int q_role) {
+    // grid y: the q heads (Q role, when q_role) and then the kv heads
     const int tile = blockIdx.x, y = blockIdx.y, b = blockIdx.z;
-    if (y < g.heads)
+    const int nq = q_role ? g.heads : 0;
+    if (y < nq)
         prep_q<D>(q, ln, q8, q_scale, g, tile, y, b);
     else
-        prep_stats<D>(k, v, ln, part, g, tile, y - g.heads, b);
+        prep_stats<D>(k, v, ln, part, g, tile, y - nq, b);
 }
 
 // Per (kv head, batch, 32 channels): K mean, V mean, V scale and its
@@ -519,8 +523,9 @@ __global__ void __launch_bounds__(256) sp_export_v(const uint8_t* __restrict__ v
 template <int D>
 static cudaError_t prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                              const Geom& g, cudaStream_t st) {
-    sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
-        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g);
+    const int q_role = q != nullptr;
+    sp_prep<D><<<dim3(g.q_tiles, (q_role ? g.heads : 0) + g.kv_heads, g.batch), 256, 0, st>>>(
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g, q_role);
     sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
     sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
@@ -529,7 +534,13 @@ static cudaError_t prepare_d(const void* q, const void* k, const void* v, const 
 
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                            const Geom& g, cudaStream_t st) {
+    if (!q) return cudaErrorInvalidValue;
     return d == 64 ? prepare_d<64>(q, k, v, ln, buf, g, st) : prepare_d<128>(q, k, v, ln, buf, g, st);
+}
+
+cudaError_t launch_prepare_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
+                              const Geom& g, cudaStream_t st) {
+    return d == 64 ? prepare_d<64>(nullptr, k, v, ln, buf, g, st) : prepare_d<128>(nullptr, k, v, ln, buf, g, st);
 }
 
 // ---------------------------------------------------------------- context parallelism
@@ -601,7 +612,7 @@ template <int D>
 static cudaError_t cp_prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                                 const Geom& g, float* raw, cudaStream_t st) {
     sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
-        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g);
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g, 1);
     sp_cp_partial<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(buf.part, raw, g);
     return cudaGetLastError();
 }

@@ -163,7 +163,7 @@ def run_reference_gpu(c: Case, x: Inputs, *, attend=True):
     """The reference's own kernels (oracle/_ref) on the same inputs: returns
     (out f32 [b][t][h][d] or None, Quant).  Needs heads == kv_heads."""
     assert c.heads == c.kv_heads and not c.causal
-    L = O.ref_lib(c.d)
+    L = O.ref_lib(c.d, c.pv16)
     g = geom(c)
     b, h, d = c.batch, c.heads, c.d
     keep, (tq, tk, tv) = to_device(c, x)

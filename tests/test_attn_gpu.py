@@ -23,11 +23,15 @@ def _exact(c, x):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("kw", [dict(), dict(smooth=False), dict(ln=True), dict(merge=2), dict(merge=4, ln=True)],
-                         ids=["dense", "nosmooth", "ln", "merge2", "merge4_ln"])
+@pytest.mark.parametrize("kw", [dict(), dict(smooth=False), dict(ln=True), dict(merge=2), dict(merge=4, ln=True),
+                                dict(pv16=True), dict(pv16=True, merge=4)],
+                         ids=["dense", "nosmooth", "ln", "merge2", "merge4_ln", "pv16", "pv16_merge4"])
 def test_attention_matches_reference_kernels(d, kw):
+    """pv16: PvAccum::F16 against the reference's SG_PV16 kernel (FP16 PV
+    accumulation per block); ours keeps FP32 accumulation with the same
+    quantiser (V scaled to +-2.25)."""
     import sagetest as st
-    if not O.ref_available(d):
+    if not O.ref_available(d, kw.get("pv16", False)):
         pytest.skip("oracle/_ref not built")
     c = _small(st, d, **kw)
     x = st.make_inputs(c)

@@ -45,3 +45,21 @@ def test_metrics_are_one_per_workload():
     names = sorted(bench.WORKLOADS)
     assert len({bench.metric_of(n) for n in names}) == len(names)
     assert all("TOPS" in bench.metric_of(n) for n in names)
+
+
+def test_c4_is_head_sharded_strong_scaling():
+    # the fixed global C4 job; its 32 (batch, kv head) units split over the ranks
+    for world in (1, 2, 4, 8):
+        B, H, G, sharded = bench.shard_of("C4", world)
+        assert sharded and B == 4 and H * world == 32 and G * world == 8
+        cfg = bench.config_of("C4", world)
+        assert cfg["global_batch"] == 4 and f"hs{world}" in cfg["parallelism"]
+    assert bench.shard_of("C3", 4)[3] is False and bench.config_of("C3", 4)["global_batch"] == 8
+
+
+def test_reference_arm_config_matches_ours_at_two_ranks():
+    out = _run(["--impl", "reference", "--steps", "1", "--warmup", "0"], env={"WORLD_SIZE": "2", "RANK": "0",
+                                                                              "LOCAL_RANK": "0"})
+    d = json.loads(out.strip().splitlines()[-1])
+    assert d["config"] == bench.config_of("C4", 2)
+    assert d["scaling"] == "strong" and d["n_gpus"] == 2

@@ -73,39 +73,57 @@ def test_qkv_gemm_matches_f64_oracle(name, pairs):
         assert rel_rms < 5e-3 and e["max_abs"] < 0.05 * max(1.0, e["ref_max"]), (what, e)
 
 
-def test_qkv_gemm_quant_is_the_quantiser_on_its_own_output():
-    b, t, hidden, hq, hkv, d = 1, 300, 512, 4, 2, 128
+QUANT_CASES = {
+    # name: batch, tokens, hidden, heads, kv, d, rope kind, pairs (SM-pair GEMM)
+    "fused_d128_rope1d": (2, 304, 512, 4, 2, 128, "llama", True),      # Q quantised in the epilogue
+    "fused_d64_norope": (2, 256, 256, 4, 4, 64, None, True),
+    "fused_d64_vggt": (1, 3 * 80, 256, 4, 4, 64, "vggt", True),
+    "unfused_ragged": (1, 300, 512, 4, 2, 128, "llama", True),         # tokens % 16 != 0: whole quantiser
+    "unfused_1sm": (1, 304, 512, 4, 2, 128, "llama", False),
+}
+
+
+@pytest.mark.parametrize("name", list(QUANT_CASES))
+def test_qkv_gemm_quant_is_the_quantiser_on_its_own_output(name):
+    """spl_sage_qkv_gemm_quant's workspace equals, byte for byte, the oracle
+    quantiser run on the bf16 Q/K/V the same call wrote (A.7: the GEMM output
+    rounded to bf16 after the GEMM and after RoPE, then quantised), whether Q
+    is quantised in the GEMM's epilogue (fused) or by the quantiser."""
+    b, t, hidden, hq, hkv, d, rk, pairs = QUANT_CASES[name]
     rng = np.random.default_rng(9)
     m, n = b * t, (hq + 2 * hkv) * d
     xb, wb = _bf16(rng.normal(size=(m, hidden))), _bf16(rng.normal(0, 0.02, size=(n, hidden)))
-    rope = sage.rope_table_1d(500000.0, d, t)
+    bias = _bf16(rng.normal(0, 0.1, size=n))
+    rope, half, frame = None, 0, 1
+    if rk == "llama":
+        rope, half, frame = sage.rope_table_1d(500000.0, d, t), d // 2, t
+    elif rk == "vggt":
+        tab = sage.RopeTable.vggt(5, 15, 5)
+        rope, half, frame = tab.cos_sin, tab.half, tab.frame_len
     c = st.Case(batch=b, heads=hq, kv_heads=hkv, tokens=t, d=d, causal=True, packed=False)
     eng = st.engine(c)
+    eng.gemm_pairs(pairs)
     ws = eng.workspace(sage.Shape(b, hq, t, hkv, True))
     q = torch.empty(b, t, hq, d, dtype=torch.bfloat16, device="cuda")
     k = torch.empty(b, t, hkv, d, dtype=torch.bfloat16, device="cuda")
     v = torch.empty(b, t, hkv, d, dtype=torch.bfloat16, device="cuda")
-    eng.qkv_gemm_quant(ws, _dev(xb), _dev(wb), None, torch.from_numpy(rope).cuda(), q, k, v, rope_half=64,
-                       frame_len=t)
-    p = ws.plan
-    got = O.Quant(q8=None, q_scale=None, k8=None, k_scale=None, v8=None, stats=None, kbias=None, part=None)
-    bufs = dict(q8=torch.zeros(b * hq * p.tq_pad * d, dtype=torch.int8, device="cuda"),
-                q_scale=torch.zeros(b * hq * p.tq_pad // 16, device="cuda"),
-                k8=torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.int8, device="cuda"),
-                k_scale=torch.zeros(b * hkv * p.tk_pad // 64, device="cuda"),
-                v8=torch.zeros(b * hkv * p.tk_pad * d, dtype=torch.uint8, device="cuda"),
-                stats=torch.zeros(b * hkv * 4 * d, device="cuda"), kbias=torch.zeros(p.tk_pad, device="cuda"))
-    eng.export_reference_layout(ws, **bufs)
-    torch.cuda.synchronize()
+    rd = None if rope is None else torch.from_numpy(rope).cuda()
+    eng.qkv_gemm_quant(ws, _dev(xb), _dev(wb), _dev(bias), rd, q, k, v, rope_half=half, frame_len=frame)
+    assert eng.status(ws) == 0
+    got = st.export_quant(eng, ws, c)
     qb = q.view(torch.int16).cpu().numpy().view(np.uint16)
     kb = k.view(torch.int16).cpu().numpy().view(np.uint16)
     vb = v.view(torch.int16).cpu().numpy().view(np.uint16)
     want = O.prepare(qb, kb, vb, st.geom(c))
-    got.q8 = bufs["q8"].cpu().numpy().reshape(want.q8.shape)
-    got.q_scale = bufs["q_scale"].cpu().numpy().reshape(want.q_scale.shape)
-    got.k8 = bufs["k8"].cpu().numpy().reshape(want.k8.shape)
-    got.k_scale = bufs["k_scale"].cpu().numpy().reshape(want.k_scale.shape)
-    got.v8 = bufs["v8"].cpu().numpy().reshape(want.v8.shape)
-    got.stats = bufs["stats"].cpu().numpy().reshape(want.stats.shape)
-    got.kbias = bufs["kbias"].cpu().numpy()
-    st.assert_quant_equal(got, want, kbias=False, what="qkv_gemm_quant")
+    st.assert_quant_equal(got, want, kbias=False, what=f"qkv_gemm_quant {name}")
+    # the bf16 outputs are the GEMM's own (unchanged by the fusion)
+    ref = O.qkv_reference(xb, wb, bias, rope, tokens=t, hq=hq, hkv=hkv, d=d, rope_half=half, frame_len=frame)
+    for got_t, r, what in zip((q, k, v), ref, "qkv"):
+        e = O.errors(_host(got_t).reshape(r.shape), r)
+        assert e["rel_l2"] < 5e-3, (what, e)
+    if name.startswith("fused"):
+        # with q NULL the fused path writes no bf16 Q and the same bytes
+        ws2 = eng.workspace(sage.Shape(b, hq, t, hkv, True))
+        eng.qkv_gemm_quant(ws2, _dev(xb), _dev(wb), _dev(bias), rd, None, k, v, rope_half=half, frame_len=frame)
+        got2 = st.export_quant(eng, ws2, c)
+        st.assert_quant_equal(got2, got, kbias=False, what=f"qkv_gemm_quant {name} without bf16 Q")
