@@ -629,6 +629,7 @@ static int qkv_setup(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x
         if (sh.frame_len <= 0) return fail(SPL_SAGE_ERR_INVALID, "qkv: RoPE frame length is 0");
     }
     sp::QkvGeom& g = *out;
+    g = sp::QkvGeom{};  // every field zero: no epilogue quantisation unless the caller sets q8
     g.m = (int)m;
     g.n = (int)n;
     g.k = (int)kd;
@@ -645,7 +646,7 @@ int spl_sage_qkv_gemm(spl_sage* s, const spl_sage_qkv_shape* shape, const void* 
                       const float* rope, void* q, void* k, void* v) {
     if (!s || !shape || !x || !w || !q || !k || !v)
         return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm: NULL argument");
-    sp::QkvGeom g;
+    sp::QkvGeom g{};
     int rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g);
     if (rc) return rc;
     if (((uintptr_t)bias | (uintptr_t)rope) % 16)
@@ -670,7 +671,7 @@ int spl_sage_qkv_gemm_fp8(spl_sage* s, const spl_sage_qkv_shape* shape, const vo
                           void* v) {
     if (!s || !shape || !x8 || !x_scale || !w8 || !w_scale || !q || !k || !v)
         return fail(SPL_SAGE_ERR_INVALID, "spl_sage_qkv_gemm_fp8: NULL argument");
-    sp::QkvGeom g;
+    sp::QkvGeom g{};
     int rc = qkv_setup(s, shape, x8, w8, rope, q, k, v, 16, &g);
     if (rc) return rc;
     if (((uintptr_t)bias | (uintptr_t)rope | (uintptr_t)w_scale) % 16)
@@ -725,7 +726,7 @@ int spl_sage_linear_fp8(spl_sage* s, const void* x8, const float* x_scale, const
         return fail(SPL_SAGE_ERR_INVALID, "gemm: buffers must be 16-byte aligned");
     // the QKV kernel with one part of n / 128 "heads" of 128 channels and no
     // RoPE writes y row-major [m][n]
-    sp::QkvGeom g;
+    sp::QkvGeom g{};
     memset(&g, 0, sizeof g);
     g.m = (int)m;
     g.n = (int)n;
@@ -798,7 +799,7 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     const float* ln = nullptr;
     int rc = build_geom(s, ws, tq, tk, tv, opts, &ag, &ln);
     if (rc) return rc;
-    sp::QkvGeom g;
+    sp::QkvGeom g{};
     if ((rc = qkv_setup(s, shape, x, w, rope, q, k, v, 8, &g))) return rc;
     if (((uintptr_t)bias | (uintptr_t)rope) % 16)
         return fail(SPL_SAGE_ERR_INVALID, "qkv: bias and RoPE table must be 16-byte aligned");
