@@ -378,6 +378,26 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
                        int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse);
 int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out);
 
+/* Context parallelism by all-gather instead of the ring's steps (no
+ * counterpart in the reference): after steps 1-3 above, the quantised K/V of
+ * all ranks are gathered (e.g. ncclAllGather over NVSwitch) into one K/V
+ * buffer of the whole sequence in key order, and each rank attends its two
+ * query chunks to it in ONE causal launch: no per-step merge, no per-step
+ * launch tail, and the zig-zag split gives every rank the same work.
+ * spl_sage_kv_create_gathered: TMA descriptors over such a buffer of
+ * `tokens` keys (a multiple of 128) with ws's batch, kv heads and head dim:
+ * k8 i8 [b][g][tokens][D], k_scale f32 [b][g][tokens/64], v8 E4M3
+ * [b][g][D][tokens] (the layouts of spl_sage_kv_bytes).
+ * spl_sage_cp_attend_gathered: this rank's local query rows [0, C) sit at
+ * global rows q_off0.., rows [C, 2C) at q_off1.. (C = the workspace's
+ * tokens / 2, whole 128-row tiles); local row i attends the gathered keys 0
+ * .. its global row; bf16 into out, with the statistics of
+ * spl_sage_cp_quantize_kv. */
+int spl_sage_kv_create_gathered(spl_sage* s, const spl_sage_ws* ws, int64_t tokens, void* k8, float* k_scale,
+                                void* v8, spl_sage_kv** out);
+int spl_sage_cp_attend_gathered(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv_all, int64_t q_off0,
+                                int64_t q_off1, spl_sage_tensor_mut out);
+
 /* The whole ring in one call, for hosts that hold their own NCCL
  * communicator (the `spl_sage_ring_forward(..., ncclComm_t, rank, world)` of
  * the drop-in boundary).  No counterpart in the reference.

@@ -103,6 +103,7 @@ EXPORTS = [
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
     "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
     "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest", "spl_sage_ring_segment",
+    "spl_sage_kv_create_gathered", "spl_sage_cp_attend_gathered",
 ]
 
 # spl_sage_cp_attend flags
@@ -131,6 +132,8 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_ring_create.argtypes = [P, ctypes.POINTER(_Shape), I, I, I, ctypes.POINTER(P)]
         L.spl_sage_ring_destroy.argtypes = [P]
         L.spl_sage_ring_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
+        L.spl_sage_kv_create_gathered.argtypes = [P, P, ctypes.c_int64, P, P, P, ctypes.POINTER(P)]
+        L.spl_sage_cp_attend_gathered.argtypes = [P, P, P, ctypes.c_int64, ctypes.c_int64, _Tensor]
         L.spl_sage_ring_segment.argtypes = [I, I, I, ctypes.c_int64] + [ctypes.POINTER(ctypes.c_int64)] * 4 + [
             ctypes.POINTER(I)]
         L.spl_sage_workspace_create.argtypes = [P, ctypes.POINTER(_Shape), ctypes.POINTER(_Merge), ctypes.POINTER(P)]
@@ -578,6 +581,12 @@ class SageAttention:
         _check(lib().spl_sage_cp_attend(self._h, ws._h, kv._h, q_begin, q_len, k_begin, k_len, flags,
                                         ctypes.c_void_p(acc.data_ptr()), ctypes.c_void_p(lse.data_ptr())))
 
+    def cp_attend_gathered(self, ws: Workspace, kv_all: "KvBuffer", q_off0: int, q_off1: int, out: Tensor):
+        """This rank's two query chunks (local rows [0, C) at global rows
+        q_off0.., [C, 2C) at q_off1..) against the gathered keys of the whole
+        sequence in one causal launch, bf16 into out."""
+        _check(lib().spl_sage_cp_attend_gathered(self._h, ws._h, kv_all._h, q_off0, q_off1, out._c()))
+
     def cp_finish(self, ws: Workspace, acc, out: Tensor):
         _check(lib().spl_sage_cp_finish(self._h, ws._h, ctypes.c_void_p(acc.data_ptr()), out._c()))
 
@@ -632,17 +641,29 @@ class KvBuffer:
     NCCL can send and receive) with the TMA descriptors the attention kernel
     reads them through (spl_sage_kv_create)."""
 
-    def __init__(self, eng: "SageAttention", ws: Workspace):
+    def __init__(self, eng: "SageAttention", ws: Workspace, tokens: int | None = None):
+        """tokens None: ws's own keys (spl_sage_kv_create); otherwise a
+        buffer of `tokens` gathered keys, the whole sequence of a
+        context-parallel job (spl_sage_kv_create_gathered)."""
         import torch
-        n = [ctypes.c_int64() for _ in range(3)]
-        _check(lib().spl_sage_kv_bytes(ws._h, *[ctypes.byref(x) for x in n]))
-        self.k8 = torch.empty(n[0].value, dtype=torch.uint8, device="cuda")
-        self.k_scale = torch.empty(n[1].value // 4, dtype=torch.float32, device="cuda")
-        self.v8 = torch.empty(n[2].value, dtype=torch.uint8, device="cuda")
+        if tokens is None:
+            n = [ctypes.c_int64() for _ in range(3)]
+            _check(lib().spl_sage_kv_bytes(ws._h, *[ctypes.byref(x) for x in n]))
+            sizes = [x.value for x in n]
+        else:
+            s = ws.plan.shape
+            kb = s.batch * s.kv * tokens * ws.head_dim
+            sizes = [kb, 4 * s.batch * s.kv * (tokens // KBLOCK), kb]
+        self.tokens = tokens
+        self.k8 = torch.empty(sizes[0], dtype=torch.uint8, device="cuda")
+        self.k_scale = torch.empty(sizes[1] // 4, dtype=torch.float32, device="cuda")
+        self.v8 = torch.empty(sizes[2], dtype=torch.uint8, device="cuda")
         h = ctypes.c_void_p()
-        _check(lib().spl_sage_kv_create(eng._h, ws._h, ctypes.c_void_p(self.k8.data_ptr()),
-                                        ctypes.c_void_p(self.k_scale.data_ptr()), ctypes.c_void_p(self.v8.data_ptr()),
-                                        ctypes.byref(h)))
+        ptrs = [ctypes.c_void_p(t.data_ptr()) for t in (self.k8, self.k_scale, self.v8)]
+        if tokens is None:
+            _check(lib().spl_sage_kv_create(eng._h, ws._h, *ptrs, ctypes.byref(h)))
+        else:
+            _check(lib().spl_sage_kv_create_gathered(eng._h, ws._h, tokens, *ptrs, ctypes.byref(h)))
         self._h = h
 
     def tensors(self):

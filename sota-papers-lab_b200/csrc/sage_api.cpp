@@ -1008,6 +1008,41 @@ int spl_sage_kv_create(spl_sage* s, const spl_sage_ws* ws, void* k8, float* k_sc
     return SPL_SAGE_OK;
 }
 
+int spl_sage_kv_create_gathered(spl_sage* s, const spl_sage_ws* ws, int64_t tokens, void* k8, float* k_scale,
+                                void* v8, spl_sage_kv** out) {
+    if (!s || !ws || !out) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_kv_create_gathered: NULL argument");
+    if (!k8 || !k_scale || !v8) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_kv_create_gathered: NULL buffer");
+    if ((uintptr_t)k8 % 128 || (uintptr_t)v8 % 128 || (uintptr_t)k_scale % 16)
+        return fail(SPL_SAGE_ERR_INVALID, "K/V buffers must be 128-byte aligned, k_scale 16-byte aligned");
+    if (ws->head_dim != s->head_dim)
+        return fail(SPL_SAGE_ERR_INVALID, "workspace was made for head dim %d, kernels are %d", ws->head_dim,
+                    s->head_dim);
+    if (ws->merge.stride > 1) return fail(SPL_SAGE_ERR_INVALID, "context parallelism takes dense keys only");
+    if (tokens <= 0 || tokens % BLK || !fits_i32(tokens))
+        return fail(SPL_SAGE_ERR_INVALID, "gathered keys: %lld tokens must be a positive multiple of 128",
+                    (long long)tokens);
+    const int64_t D = ws->head_dim, B = ws->shape.batch, G = ws->shape.kv_heads, T = tokens;
+    spl_sage_kv* kv = new spl_sage_kv;
+    memset(kv, 0, sizeof *kv);
+    kv->head_dim = (int)D;
+    kv->batch = B;
+    kv->kv_heads = G;
+    kv->tk_pad = T;
+    kv->k8 = (int8_t*)k8;
+    kv->k_scale = k_scale;
+    kv->v8 = (uint8_t*)v8;
+    const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    int rc = make_map(&kv->map_k, k8, D, T, B * G, D, T * D, (uint32_t)D, 128, swz);
+    if (rc == SPL_SAGE_OK)
+        rc = make_map(&kv->map_v, v8, T, D, B * G, T, T * D, 128, (uint32_t)D, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != SPL_SAGE_OK) {
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return SPL_SAGE_OK;
+}
+
 void spl_sage_kv_destroy(spl_sage_kv* kv) { delete kv; }
 
 int spl_sage_cp_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
@@ -1106,6 +1141,49 @@ int spl_sage_cp_attend(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv
                        int64_t k_begin, int64_t k_len, int flags, float* acc, float* lse) {
     if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend: NULL argument");
     return cp_attend(s, ws, kv, q_begin, q_len, k_begin, k_len, flags, acc, lse, s->reserved_sms);
+}
+
+int spl_sage_cp_attend_gathered(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv_all, int64_t q_off0,
+                                int64_t q_off1, spl_sage_tensor_mut out) {
+    if (!s || !ws || !kv_all) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_cp_attend_gathered: NULL argument");
+    if (!ws->prepared) return fail(SPL_SAGE_ERR_STATE, "sage workspace has not been prepared");
+    if (kv_all->head_dim != ws->head_dim || kv_all->batch != ws->shape.batch ||
+        kv_all->kv_heads != ws->shape.kv_heads)
+        return fail(SPL_SAGE_ERR_INVALID, "the gathered K/V buffer was made for another batch or kv head count");
+    const int64_t T = ws->shape.tokens, C = T / 2, N = kv_all->tk_pad;
+    if (T % (2 * QTILE))
+        return fail(SPL_SAGE_ERR_INVALID, "this rank's %lld tokens must be two chunks of whole 128-row tiles",
+                    (long long)T);
+    if (q_off0 < 0 || q_off1 < 0 || q_off0 % QTILE || q_off1 % QTILE || q_off0 + C > N || q_off1 + C > N)
+        return fail(SPL_SAGE_ERR_INVALID, "query chunks at %lld and %lld (of %lld rows) must be whole tiles "
+                    "within the %lld gathered keys", (long long)q_off0, (long long)q_off1, (long long)C,
+                    (long long)N);
+    int rc = check_tensor("output", out.data, out.len, out.batch, out.token, out.head, ws->shape, ws->shape.heads,
+                          s->head_dim);
+    if (rc) return rc;
+    sp::Geom g = ws->geom;
+    g.o_sb = out.batch;
+    g.o_st = out.token;
+    g.o_sh = out.head;
+    g.tk = (int)N;
+    g.tk_pad = (int)N;
+    g.causal = 1;
+    g.merge = 1;
+    g.q_tile0 = 0;
+    g.k_key0 = 0;
+    g.q_split = (int)C;
+    g.q_goff0 = (int)q_off0;
+    g.q_goff1 = (int)q_off1;
+    g.max_ctas = max_ctas(s);
+    sp::AttnMaps maps;
+    maps.q = ws->maps.q;
+    maps.k = kv_all->map_k;
+    maps.v = kv_all->map_v;
+    sp::Buffers buf = ws->buf;
+    buf.k_scale = kv_all->k_scale;
+    cudaError_t e = sp::launch_attend(s->head_dim, maps, buf, g, out.data, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sage gathered attention");
+    return SPL_SAGE_OK;
 }
 
 int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl_sage_tensor_mut out) {

@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         return it * (int)gridDim.x + c;
     };
     struct Tile {
-        int bh_q, b, h, bh_kv, qt, nb;
+        int bh_q, b, h, bh_kv, qt, nb, g0;
     };
     auto tile_of = [&](int t) {
         Tile x;
@@ -156,7 +156,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         x.h = x.bh_q % g.heads;
         x.bh_kv = x.b * g.kv_heads + x.h / group;
         x.qt = CAUSAL ? n_qt - 1 - qi : qi;  // tile within the segment
-        x.nb = CAUSAL ? min(nkb, x.qt + 1) : nkb;
+        // key position of the tile's first query row (causal over gathered
+        // keys: its global row; otherwise its row in the segment)
+        const int r0 = x.qt * 128;
+        x.g0 = (!PARTIAL && g.q_split) ? (r0 < g.q_split ? g.q_goff0 + r0 : g.q_goff1 + (r0 - g.q_split)) : r0;
+        x.nb = CAUSAL ? min(nkb, x.g0 / BLK + 1) : nkb;
         return x;
     };
 
@@ -359,8 +363,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
         const Tile tl = tile_of(t);
         const int bh_q = tl.bh_q, bh_kv = tl.bh_kv, qt = tl.qt, nb = tl.nb;
-        const int qrow = qt * 128 + r;                          // within the segment (masking)
-        const int qrow_ws = PARTIAL ? (q_tile0 + qt) * 128 + r : qrow;  // within the workspace
+        const int qrow = tl.g0 + r;                             // key position of this row (masking)
+        const int qrow_ws = (PARTIAL ? q_tile0 + qt : qt) * 128 + r;  // within the workspace
         const float qs =
             PREFETCH ? qs_next : __ldg(q_scale + (long long)bh_q * (g.tq_pad / QGROUP) + qrow_ws / QGROUP);
         const float* ksc = k_scale + (long long)bh_kv * nkb64 + k_key0 / KBLOCK;
@@ -430,7 +434,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int c = 0; c < 64; c++) x[c] = __uint_as_float(sr[c]);
             }
-            if (j * BLK + BLK > g.tk || (CAUSAL && j * BLK + BLK > qt * 128)) {
+            if (j * BLK + BLK > g.tk || (CAUSAL && j * BLK + BLK > tl.g0)) {
 #pragma unroll
                 for (int c = 0; c < 64; c++) {
                     const int key = key0 + c;

@@ -30,6 +30,13 @@ struct Geom {
     int q_tile0, k_key0, cp_first;
     // Persistent kernels launch at most this many CTAs (0: one per SM).
     int max_ctas;
+    // Causal attention over gathered keys (context parallelism by
+    // all-gather): the keys are the whole sequence in order and the
+    // workspace's query rows are two chunks of it, local rows [0, q_split)
+    // at global rows q_goff0 + i and rows [q_split, tokens) at q_goff1 +
+    // (i - q_split); local row i sees global keys 0 .. its global row.
+    // q_split = 0: queries and keys share positions (the plain causal mask).
+    int q_split, q_goff0, q_goff1;
 };
 
 // Device buffers of one workspace.  Layouts (b = batch, h = q head,
@@ -134,6 +141,8 @@ cudaError_t launch_cp_merge_stats(const float* rsum, const float* rmax, float* r
 cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, float* acc,
                                   float* lse, cudaStream_t st);
 
+// launch_attend with g.q_split set: causal attention of the workspace's two
+// query chunks over gathered keys (their maps in `maps`, k_scale in buf).
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,
                           cudaStream_t st);
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes);

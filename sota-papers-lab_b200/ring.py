@@ -31,6 +31,15 @@ work).  Its Q, K and V are those 2C tokens, chunk r first.
 3. The accumulator is converted to bf16.
 
 With P = 1 this is one GPU attending the whole sequence in two chunks.
+
+schedule="gather" replaces step 2: the ranks all-gather their quantised K/V
+(about 2 * C * Hkv * D bytes each) into a buffer of the whole sequence in
+key order, and each rank attends its two query chunks to it in ONE causal
+launch (spl_sage_cp_attend_gathered): no per-step merge into an fp32
+accumulator, no per-step launch tail, and the zig-zag split still gives
+every rank the same work.  The transfer is not overlapped with attention
+(the launch needs every key), but on NVSwitch it takes well under a
+millisecond against a step of tens.
 """
 from __future__ import annotations
 
@@ -185,6 +194,44 @@ def combine_stats(raw, world: int, group=None):
     return raw
 
 
+def gather_kv(local, whole, staging, world: int, batch: int, kv_heads: int, chunk: int, head_dim: int,
+              group=None):
+    """All-gather every rank's quantised K/V buffer `local` (its chunks r and
+    2P-1-r, local order) and lay the result out in `whole` in global key
+    order.  staging: three flat CUDA tensors of world x the local sizes (or
+    None at world 1)."""
+    if world > 1:
+        import torch.distributed as dist
+        for dst, src in zip(staging, local.tensors()):
+            dist.all_gather_into_tensor(dst, src, group=group)
+        parts = staging
+    else:
+        parts = local.tensors()
+    layout_gathered(parts, whole, world, batch, kv_heads, chunk, head_dim)
+
+
+def layout_gathered(parts, whole, world: int, batch: int, kv_heads: int, chunk: int, head_dim: int):
+    """The gathered buffers `parts` (every rank's k8, k_scale, v8 one after
+    the other, rank order) copied into `whole` in global key order: rank s's
+    local chunk 0 is global chunk s, its chunk 1 global chunk 2P-1-s.
+    Layouts: k8 [b][g][t][D], k_scale [b][g][t/64], v8 [b][g][D][t], t the
+    buffer's keys."""
+    import torch
+    B, G, C, D, P = batch, kv_heads, chunk, head_dim, world
+    dev = parts[0].device
+    first = torch.arange(P, device=dev)                 # rank s's chunk s
+    second = 2 * P - 1 - torch.arange(P, device=dev)    # rank s's chunk 2P-1-s
+    # per tensor: the gathered view [P][b][g]..[2][C].., whole's view, the
+    # dimension of the local chunk index in the first, of the chunk in the second
+    views = (((P, B, G, 2, C, D), (B, G, 2 * P, C, D), 3, 2),
+             ((P, B, G, 2, C // 64), (B, G, 2 * P, C // 64), 3, 2),
+             ((P, B, G, D, 2, C), (B, G, D, 2 * P, C), 4, 3))
+    for src, dst, (sv, dv, cdim, gdim) in zip(parts, whole.tensors(), views):
+        x, y = src.view(*sv), dst.view(*dv)
+        for c, idx in ((0, first), (1, second)):
+            y.index_copy_(gdim, idx, x.select(cdim, c).movedim(0, gdim))
+
+
 def _torch_stream(stream):
     """The torch stream object of an engine stream (a torch stream, a raw
     cudaStream_t as an int, or None for the legacy default stream)."""
@@ -209,19 +256,24 @@ class RingAttention:
     of the group's NCCL kernels."""
 
     def __init__(self, eng, batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int, world: int,
-                 head_dim: int, reserved_sms: int | None = None, group=None):
+                 head_dim: int, reserved_sms: int | None = None, group=None, schedule: str = "ring"):
         import torch
         sage = importlib.import_module("sota-papers-lab_b200")
         if local_tokens % 256:
             raise sage.SageError(1, "each rank's tokens must be two chunks of whole 128-token tiles")
+        if schedule not in ("ring", "gather"):
+            raise sage.SageError(1, f"unknown context-parallel schedule {schedule!r}")
         self.sage, self.eng = sage, eng
+        self.schedule = schedule
         self.rank, self.world = rank, world
         self.B, self.H, self.G, self.T, self.D = batch, heads, kv_heads, local_tokens, head_dim
         self.C = local_tokens // 2
-        # SMs left free during the ring steps (none without a transfer)
-        self.reserved_sms = (RESERVED_SMS if world > 1 else 0) if reserved_sms is None else reserved_sms
+        # SMs left free during the ring steps (none without a transfer
+        # overlapping the attention)
+        default_reserved = RESERVED_SMS if world > 1 and schedule == "ring" else 0
+        self.reserved_sms = default_reserved if reserved_sms is None else reserved_sms
         self.group, self._own_group = group, False
-        if group is None and world > 1:
+        if group is None and world > 1 and schedule == "ring":
             import torch.distributed as dist
             if dist.is_available() and dist.is_initialized() and dist.get_backend() == "nccl":
                 self.group, self._own_group = nccl_ring_group(), True
@@ -233,7 +285,13 @@ class RingAttention:
             self.seg_eng = sage.SageAttention(eng.stream, head_dim, eng.config)
             self.seg_eng.reserve_sms(self.reserved_sms)
         self.ws = eng.workspace(sage.Shape(batch, heads, local_tokens, kv_heads, False))
-        self.kv = [sage.KvBuffer(eng, self.ws), sage.KvBuffer(eng, self.ws)]
+        self.kv = [sage.KvBuffer(eng, self.ws)] + ([sage.KvBuffer(eng, self.ws)] if schedule == "ring" else [])
+        self.kv_all, self.staging = None, None
+        if schedule == "gather":
+            self.kv_all = sage.KvBuffer(eng, self.ws, tokens=local_tokens * world)
+            if world > 1:
+                self.staging = [torch.empty(t.numel() * world, dtype=t.dtype, device=t.device)
+                                for t in self.kv[0].tensors()]
         self.raw = torch.empty(batch * kv_heads, 4, head_dim, dtype=torch.float32, device="cuda")
         self.acc = torch.empty(batch, local_tokens, heads, head_dim, dtype=torch.float32, device="cuda")
         self.lse = torch.empty(batch, heads, local_tokens, dtype=torch.float32, device="cuda")
@@ -253,6 +311,8 @@ class RingAttention:
             self._forward(q, k, v, out, exchange, group, opts, combine)
 
     def _forward(self, q, k, v, out, exchange, group, opts, combine):
+        if self.schedule == "gather":
+            return self._forward_gather(q, k, v, out, group, opts, combine)
         P, r = self.world, self.rank
         if group is None:
             group = self.group
@@ -275,6 +335,21 @@ class RingAttention:
                 cur = 1 - cur
         self.eng.cp_finish(self.ws, self.acc, out)
 
+    def _forward_gather(self, q, k, v, out, group, opts, combine):
+        P, r = self.world, self.rank
+        self.eng.cp_prepare(self.ws, q, k, v, self.raw, opts)
+        if combine is not None:
+            combine(self.raw)
+        else:
+            combine_stats(self.raw, P, group)
+        self.eng.cp_quantize_kv(self.ws, k, v, self.raw, self.T * P, self.kv[0], opts)
+        gather_kv(self.kv[0], self.kv_all, self.staging, P, self.B, self.G, self.C, self.D, group)
+        self.attend_gathered(out)
+
+    def attend_gathered(self, out):
+        a, b = zigzag_chunks(self.rank, self.world)
+        self.eng.cp_attend_gathered(self.ws, self.kv_all, a * self.C, b * self.C, out)
+
     def attend_segment(self, kv, seg: Segment, first: bool):
         C = self.C
         self.seg_eng.cp_attend(self.ws, kv, seg.q_chunk * C, seg.q_chunks * C, seg.k_chunk * C, seg.k_chunks * C,
@@ -283,6 +358,9 @@ class RingAttention:
     def close(self):
         for kv in self.kv:
             kv.close()
+        if self.kv_all is not None:
+            self.kv_all.close()
+            self.kv_all = None
         self.ws.close()
         if self.seg_eng is not self.eng:
             self.seg_eng.close()
@@ -310,3 +388,23 @@ def emulate_ring(rings: Sequence[RingAttention], qs, ks, vs, outs, opts=None):
         for s, (src, seg) in enumerate(ring_segments(i, P)):
             rg.attend_segment(rings[src].kv[0], seg, first=s == 0)
         rg.eng.cp_finish(rg.ws, rg.acc, outs[i])
+
+
+def emulate_gather(rings: Sequence[RingAttention], qs, ks, vs, outs, opts=None):
+    """All ranks of a gather-schedule job in one process on one GPU (for
+    tests): the statistics combined and the quantised K/V "all-gathered" by
+    a concatenation (what all_gather_into_tensor leaves on every rank), laid
+    out in every rank's whole-sequence buffer, then each rank's one launch."""
+    import torch
+    P = len(rings)
+    for i, rg in enumerate(rings):
+        rg.eng.cp_prepare(rg.ws, qs[i], ks[i], vs[i], rg.raw, opts)
+    total = torch.stack([rg.raw for rg in rings])
+    comb = torch.cat([total[:, :, :2].sum(0), total[:, :, 2:].amax(0)], dim=1)
+    for i, rg in enumerate(rings):
+        rg.raw.copy_(comb)
+        rg.eng.cp_quantize_kv(rg.ws, ks[i], vs[i], rg.raw, rg.T * P, rg.kv[0], opts)
+    staging = [torch.cat([rings[s].kv[0].tensors()[j] for s in range(P)]) for j in range(3)]
+    for i, rg in enumerate(rings):
+        layout_gathered(staging, rg.kv_all, P, rg.B, rg.G, rg.C, rg.D)
+        rg.attend_gathered(outs[i])
