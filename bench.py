@@ -327,7 +327,7 @@ def run_layers(args, rank, world, local_rank):
     }
 
 
-def ring_measure(rank, world, local_rank, steps, warmup, reserve_sms=None, e2e=True):
+def ring_measure(rank, world, local_rank, steps, warmup, reserve_sms=None, e2e=True, schedule="gather"):
     """The C5 ring (sota-papers-lab_b200/ring.py) on this rank: one long
     causal sequence split over the ranks (zig-zag chunks), K/V passed around
     a ring.  Device time of `steps` forwards (CUDA events on the launching
@@ -354,7 +354,7 @@ def ring_measure(rank, world, local_rank, steps, warmup, reserve_sms=None, e2e=T
     k = (k + torch.randn(1, 1, G, D, generator=gb, device=dev) * w["k_bias"]).to(torch.bfloat16)
     out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
     eng = sage.SageAttention(stream, D)
-    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D, reserved_sms=reserve_sms)
+    rg = ring.RingAttention(eng, B, H, G, T, rank, world, D, reserved_sms=reserve_sms, schedule=schedule)
     sq, skv = sage.Strides.bthd(T, H, D), sage.Strides.bthd(T, G, D)
     tq, tk, tv, to = sage.Tensor(q, sq), sage.Tensor(k, skv), sage.Tensor(v, skv), sage.Tensor(out, sq)
 
@@ -383,7 +383,7 @@ def ring_measure(rank, world, local_rank, steps, warmup, reserve_sms=None, e2e=T
         torch.cuda.synchronize()
     barrier()
     res = {"ms_per_step": max_over_ranks(e0.elapsed_time(e1)) / steps, "clocks": clk.summary(),
-           "reserved_sms": rg.reserved_sms, "nccl_ctas": ring.NCCL_CTAS,
+           "reserved_sms": rg.reserved_sms, "nccl_ctas": ring.NCCL_CTAS, "schedule": schedule,
            "h2d": sum(x.numel() * x.element_size() for x in (q, k, v)), "d2h": out.numel() * out.element_size()}
     if e2e:
         # this rank's Q/K/V from pinned host memory, the ring, the rank's
@@ -420,7 +420,7 @@ def run_ring(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     B, H, G, N, D = w["batch"], w["heads"], w["kv_heads"], w["tokens"], w["d"]
     peaks_hw = tensor_peak(sage.SageAttention(torch.cuda.current_stream(), D)) if rank == 0 else (0.0, 0.0)
-    r = ring_measure(rank, world, local_rank, args.steps, args.warmup, args.reserve_sms)
+    r = ring_measure(rank, world, local_rank, args.steps, args.warmup, args.reserve_sms, schedule=args.cp_schedule)
     if rank != 0:
         return None
     step_ms, e2e_ms = r["ms_per_step"], r["e2e_ms"]
@@ -436,9 +436,7 @@ def run_ring(args, rank, world, local_rank):
         "dtype": "int8/e4m3 (fp32 accumulate; bf16 in/out)", "data": "synthetic (seeded torch.randn on device)",
         "config": {"workload": w["desc"], "global_batch": B,
                    "seq_len": N, "q_heads": H, "kv_heads": G, "head_dim": D, "causal": True,
-                   "parallelism": f"cp{world}: zig-zag chunks, one attention launch per ring step, K/V ring over "
-                                  f"NCCL send/recv in a group capped at {r['nccl_ctas']} CTA(s), "
-                                  f"{r['reserved_sms']} SM(s) left free for it",
+                   "parallelism": cp_description(world, r),
                    "l2": "inputs exceed the 126 MB L2; no flush"},
         "roofline": {"bound": "tensor", "kernel": "whole ring step per GPU (quantiser, segment attention, merge)",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
@@ -456,19 +454,34 @@ def run_ring(args, rank, world, local_rank):
     }
 
 
+def cp_description(world, r):
+    if r["schedule"] == "gather":
+        return (f"cp{world}: zig-zag chunks; the quantised K/V of all ranks all-gathered over NCCL into the whole "
+                f"sequence, then one causal attention launch per rank over it")
+    return (f"cp{world}: zig-zag chunks, one attention launch per ring step, K/V ring over NCCL send/recv in a "
+            f"group capped at {r['nccl_ctas']} CTA(s), {r['reserved_sms']} SM(s) left free for it")
+
+
 def ring_c5_summary(rank, world, local_rank, peak):
-    """The `ring_c5` object of the C4 line: the C5 ring at this rank count."""
+    """The `ring_c5` object of the C4 line: the C5 context-parallel job at
+    this rank count, with both schedules (all-gather, the default, and the
+    send/recv ring)."""
     w = WORKLOADS["C5"]
     steps = 3
-    r = ring_measure(rank, world, local_rank, steps, 3, e2e=False)
+    runs = {sch: ring_measure(rank, world, local_rank, steps, 3, e2e=False, schedule=sch)
+            for sch in ("gather", "ring")}
     if rank != 0:
         return None
     alg_per_rank = algorithmic_flops(w, w["batch"]) / world
+    r = runs["gather"]
+    tops = lambda x: round(effective_flops(w, w["batch"]) / (x["ms_per_step"] * 1e-3) / 1e12, 2)
     return {"workload": w["desc"], "n_gpus": world, "scaling": "strong", "steps": steps, "warmup": 3,
-            "ms_per_step": round(r["ms_per_step"], 4),
-            "value": round(effective_flops(w, w["batch"]) / (r["ms_per_step"] * 1e-3) / 1e12, 2), "unit": "TOPS",
+            "ms_per_step": round(r["ms_per_step"], 4), "value": tops(r), "unit": "TOPS",
             "roofline_frac_per_gpu": round(alg_per_rank / (r["ms_per_step"] * 1e-3) / 1e12 / peak, 4) if peak else None,
-            "parallelism": f"cp{world}: zig-zag ring over NCCL send/recv, {r['reserved_sms']} SM(s) left to NCCL",
+            "parallelism": cp_description(world, r),
+            "send_recv_ring": {"ms_per_step": round(runs["ring"]["ms_per_step"], 4), "value": tops(runs["ring"]),
+                               "parallelism": cp_description(world, runs["ring"]),
+                               "device_error_word": runs["ring"]["device_error_word"]},
             "timing": "CUDA events on the launching stream, max over ranks", "clocks": r["clocks"],
             "device_error_word": r["device_error_word"]}
 
@@ -981,6 +994,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="C4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cp-schedule", default="gather", choices=["gather", "ring"],
+                    help="C5: all-gather the quantised K/V (default) or pass it around a send/recv ring")
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="C5: SMs the attention leaves to NCCL during ring steps (default: the ring's own)")
     args = ap.parse_args()

@@ -155,3 +155,65 @@ def test_segment_arguments_are_checked():
     with pytest.raises(sage.SageError):  # not prepared
         eng.cp_attend(rg.ws, rg.kv[0], 0, 256, 0, 256, True, acc, lse)
     rg.close()
+
+
+@pytest.mark.parametrize("world,d,heads,kv_heads,tokens", [(2, 128, 4, 2, 2048), (4, 64, 4, 4, 2048),
+                                                           (8, 128, 4, 1, 4096)])
+def test_emulated_gather_matches_single_gpu_causal(world, d, heads, kv_heads, tokens):
+    """The gather schedule (all ranks' quantised K/V gathered into the whole
+    sequence, one causal launch per rank over it): single-GPU causal
+    attention within the gate, f64 within the reference's gate, and equal to
+    the ring schedule within the gate."""
+    c = st.Case(batch=2, heads=heads, kv_heads=kv_heads, tokens=tokens, d=d, causal=True, packed=False, seed=19)
+    x, q, k, v = _inputs(c)
+    single = st.run_ours(c, x, export=False).out
+    eng = st.engine(c)
+    T = tokens // world
+    sq, skv = sage.Strides.bthd(T, heads, d), sage.Strides.bthd(T, kv_heads, d)
+    shards = [(ring.shard_zigzag(q, r, world), ring.shard_zigzag(k, r, world), ring.shard_zigzag(v, r, world))
+              for r in range(world)]
+    views = ([sage.Tensor(a, sq) for a, _, _ in shards], [sage.Tensor(b, skv) for _, b, _ in shards],
+             [sage.Tensor(cc, skv) for _, _, cc in shards])
+    results = {}
+    for schedule, emulate in (("gather", ring.emulate_gather), ("ring", ring.emulate_ring)):
+        rings = [ring.RingAttention(eng, 2, heads, kv_heads, T, r, world, d, schedule=schedule) for r in range(world)]
+        outs = [torch.zeros(2, T, heads, d, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+        emulate(rings, *views, [sage.Tensor(o, sq) for o in outs])
+        torch.cuda.synchronize()
+        for rg in rings:
+            assert eng.status(rg.ws) == 0
+            rg.close()
+        full = ring.unshard_zigzag(outs, world, dim=1)
+        results[schedule] = O.bf16_to_f32(full.view(torch.int16).cpu().numpy().view(np.uint16)).reshape(single.shape)
+    ours = results["gather"]
+    e = O.errors(ours, single)
+    print(f"gather P={world} vs single GPU: {e}")
+    assert st.attention_gate(e), e
+    e = O.errors(ours, results["ring"])
+    assert st.attention_gate(e), e
+    for r0 in (0, tokens // 2 - 64, tokens - 128):
+        rows = (r0, r0 + 128)
+        ef = O.errors(ours[:, rows[0]:rows[1]], _f64_rows(c, x, rows))
+        assert st.reference_gate(ef), (rows, ef)
+
+
+def test_gather_single_rank_path():
+    """RingAttention.forward with the gather schedule at P = 1 (the code the
+    multi-GPU run executes, without the collective)."""
+    c = st.Case(batch=2, heads=8, kv_heads=2, tokens=1024, d=128, causal=True, packed=False, seed=29)
+    x, q, k, v = _inputs(c)
+    single = st.run_ours(c, x, export=False).out
+    eng = st.engine(c)
+    rg = ring.RingAttention(eng, 2, 8, 2, 1024, 0, 1, 128, schedule="gather")
+    out = torch.zeros(2, 1024, 8, 128, dtype=torch.bfloat16, device="cuda")
+    sq, skv = sage.Strides.bthd(1024, 8, 128), sage.Strides.bthd(1024, 2, 128)
+    rg.forward(sage.Tensor(q.contiguous(), sq), sage.Tensor(k.contiguous(), skv), sage.Tensor(v.contiguous(), skv),
+               sage.Tensor(out, sq))
+    torch.cuda.synchronize()
+    assert eng.status(rg.ws) == 0
+    ours = O.bf16_to_f32(out.view(torch.int16).cpu().numpy().view(np.uint16)).reshape(single.shape)
+    e = O.errors(ours, single)
+    assert st.attention_gate(e), e
+    with pytest.raises(sage.SageError):  # query chunks past the gathered keys
+        eng.cp_attend_gathered(rg.ws, rg.kv_all, 0, 1024, sage.Tensor(out, sq))
+    rg.close()

@@ -138,3 +138,81 @@ def test_native_schedule_is_the_python_schedule(sage):
     for bad in ((0, 0, 0, C), (2, 2, 0, C), (0, 2, 2, C), (0, 2, 0, 0), (-1, 2, 0, C)):
         with pytest.raises(sage.SageError):
             sage.ring_segment(*bad)
+
+
+class _Buf:
+    def __init__(self, tensors):
+        self._t = tensors
+
+    def tensors(self):
+        return self._t
+
+
+def _local_kv(rank, world, B, G, C, D):
+    """A rank's local K/V buffers whose every key carries its global position
+    (k8 and v8 bytes = position % 251, k_scale = global 64-key group)."""
+    pos = torch.cat([torch.arange(c * C, (c + 1) * C) for c in ring.zigzag_chunks(rank, world)])  # [2C]
+    k8 = (pos % 251).to(torch.uint8).view(1, 1, 2 * C, 1).expand(B, G, 2 * C, D).contiguous()
+    v8 = (pos % 251).to(torch.uint8).view(1, 1, 1, 2 * C).expand(B, G, D, 2 * C).contiguous()
+    ks = (pos[::64] // 64).to(torch.float32).view(1, 1, 2 * C // 64).expand(B, G, 2 * C // 64).contiguous()
+    return [k8.flatten(), ks.flatten(), v8.flatten()]
+
+
+def _check_whole(whole, world, B, G, C, D):
+    n = 2 * world * C
+    pos = torch.arange(n)
+    k8, ks, v8 = whole
+    assert torch.equal(k8.view(B, G, n, D), (pos % 251).to(torch.uint8).view(1, 1, n, 1).expand(B, G, n, D))
+    assert torch.equal(v8.view(B, G, D, n), (pos % 251).to(torch.uint8).view(1, 1, 1, n).expand(B, G, D, n))
+    assert torch.equal(ks.view(B, G, n // 64), (pos[::64] // 64).to(torch.float32).view(1, 1, -1).expand(B, G, -1))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_gathered_layout_is_global_key_order(world):
+    """layout_gathered puts every rank's two zig-zag chunks at their global
+    key positions in the whole-sequence K/V buffer (k8, k_scale, v8)."""
+    B, G, C, D = 2, 3, 128, 16
+    parts = [torch.cat([_local_kv(r, world, B, G, C, D)[j] for r in range(world)]) for j in range(3)]
+    n = 2 * world * C
+    whole = [torch.zeros(B * G * n * D, dtype=torch.uint8), torch.zeros(B * G * n // 64),
+             torch.zeros(B * G * D * n, dtype=torch.uint8)]
+    ring.layout_gathered(parts, _Buf(whole), world, B, G, C, D)
+    _check_whole(whole, world, B, G, C, D)
+
+
+def _gather_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        r = importlib.import_module("sota-papers-lab_b200.ring")
+        B, G, C, D = 1, 2, 128, 8
+        local = _local_kv(rank, world, B, G, C, D)
+        staging = [torch.empty(t.numel() * world, dtype=t.dtype) for t in local]
+        n = 2 * world * C
+        whole = [torch.zeros(B * G * n * D, dtype=torch.uint8), torch.zeros(B * G * n // 64),
+                 torch.zeros(B * G * D * n, dtype=torch.uint8)]
+        r.gather_kv(_Buf(local), _Buf(whole), staging, world, B, G, C, D)
+        _check_whole(whole, world, B, G, C, D)
+        q.put((rank, True))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_kv_over_gloo(world):
+    """The all-gather of the gather schedule with real ranks (gloo): every
+    rank ends with the whole sequence's K/V in key order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(v is True for v in got.values()), got

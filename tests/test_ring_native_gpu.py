@@ -129,3 +129,63 @@ def test_native_ring_two_ranks_over_nccl():
     single = _single_gpu(sage.SageAttention(torch.cuda.current_stream(), d), q, k, v)
     e = O.errors(_f32(full), _f32(single))
     assert st.attention_gate(e), e
+
+
+def _py_rank(rank, world, port, res_q, shape, schedule):
+    import datetime
+
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        b, t_all, h, g, d = shape
+        t = t_all // world
+        q, k, v = _qkv(b, t_all, h, g, d, seed=13)
+        qs, ks, vs = (ring.shard_zigzag(x, rank, world).cuda() for x in (q, k, v))
+        eng = sage.SageAttention(torch.cuda.current_stream(), d)
+        rg = ring.RingAttention(eng, b, h, g, t, rank, world, d, schedule=schedule)
+        out = torch.zeros(b, t, h, d, dtype=torch.bfloat16, device="cuda")
+        sq, skv = sage.Strides.bthd(t, h, d), sage.Strides.bthd(t, g, d)
+        for _ in range(2):
+            rg.forward(sage.Tensor(qs, sq), sage.Tensor(ks, skv), sage.Tensor(vs, skv), sage.Tensor(out, sq))
+        torch.cuda.synchronize()
+        assert eng.status(rg.ws) == 0
+        rg.close()
+        res_q.put((rank, out.view(torch.int16).cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("schedule", ["gather", "ring"])
+def test_python_cp_two_ranks_over_nccl(schedule):
+    """RingAttention over torch.distributed NCCL on two GPUs, both schedules:
+    the zig-zag shards put back together against single-GPU causal
+    attention."""
+    import socket
+    world, shape = 2, (1, 4096, 8, 2, 128)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    res_q = ctx.Queue()
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    procs = [ctx.Process(target=_py_rank, args=(r, world, port, res_q, shape, schedule)) for r in range(world)]
+    for p in procs:
+        p.start()
+    outs = {}
+    for _ in range(world):
+        r, o = res_q.get(timeout=300)
+        outs[r] = torch.from_numpy(o).view(torch.bfloat16)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    full = ring.unshard_zigzag([outs[r] for r in range(world)], world, dim=1)
+    b, t, h, g, d = shape
+    q, k, v = _qkv(b, t, h, g, d, seed=13)
+    single = _single_gpu(sage.SageAttention(torch.cuda.current_stream(), d), q, k, v)
+    e = O.errors(_f32(full), _f32(single))
+    print(f"{schedule} at two ranks vs single GPU: {e}")
+    assert st.attention_gate(e), e
