@@ -54,19 +54,12 @@ constexpr int VST = 3;   // V ring depth
 #ifndef SP_EXP_POLY
 #define SP_EXP_POLY 4
 #endif
-constexpr int EXP_POLY = SP_EXP_POLY;
-#ifndef SP_SOFTMAX_WARPS
-#define SP_SOFTMAX_WARPS 8
-#endif  // of every 16 exponentials, how many run on the FMA pipe
-// NS softmax warps (8: half a row per lane; 16: a quarter row per lane),
-// then one service thread per SM sub-partition (warp % 4), so that no group
-// of softmax warps carries more issue load than another: K loads (and Q),
+constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
+constexpr int NTHREADS = 384;
+// One service thread per SM sub-partition (warp % 4), so that no pair of
+// softmax warps carries more issue load than another: K loads (and Q),
 // V loads, the QK^T MMAs, the PV MMAs.
-template <int NS>
-struct Roles {
-    static constexpr int THREADS = 32 * (NS + 4);
-    static constexpr int K_WARP = NS, V_WARP = NS + 1, QK_WARP = NS + 2, PV_WARP = NS + 3;
-};
+constexpr int K_WARP = 8, V_WARP = 9, QK_WARP = 10, PV_WARP = 11, NSOFTMAX_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MAGIC_I = 0x4B400000u;    // bits of 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;       // 1.5 * 2^23
@@ -94,7 +87,6 @@ struct Bars {
     uint64_t s_full[2];
     uint64_t p_full[2], p_free[2];
     uint64_t qk_done, pv_done;
-    uint64_t xpair[8];  // 16 softmax warps: the two warps of each row set meet here once per exchange
 };
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -112,17 +104,16 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_
 // the K/V buffer (CAUSAL then means key i is seen by query i and later of
 // the segment); the result is merged into the fp32 accumulator acc and the
 // per-row log2 softmax denominator lse by log-sum-exp instead of written.
-template <int D, bool CAUSAL, bool MERGE, bool PARTIAL, int NS>
-__global__ void __launch_bounds__(32 * (NS + 4), 1)
+// GQ (causal, not PARTIAL): the queries are two chunks of a longer
+// sequence whose keys are all gathered (g.q_split, g.q_goff0, g.q_goff1).
+template <int D, bool CAUSAL, bool MERGE, bool PARTIAL, bool GQ = false>
+__global__ void __launch_bounds__(NTHREADS, 1)
     sp_attn(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
             const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q_scale,
             const float* __restrict__ k_scale, const float* __restrict__ stats, const float* __restrict__ kbias,
             uint16_t* __restrict__ out, float* __restrict__ acc, float* __restrict__ lse, uint32_t* __restrict__ err,
             const Geom g) {
     using L = AttnSmem<D>;
-    using R = Roles<NS>;
-    constexpr int NTHREADS = R::THREADS, NSOFTMAX_WARPS = NS;
-    constexpr int K_WARP = R::K_WARP, V_WARP = R::V_WARP, QK_WARP = R::QK_WARP, PV_WARP = R::PV_WARP;
     constexpr int DH = D / 2;
     constexpr uint32_t SWZ = D == 128 ? SWZ_128B : SWZ_64B;
     constexpr uint32_t QK_SBO = 8 * D;  // 8 rows of D bytes
@@ -134,10 +125,6 @@ __global__ void __launch_bounds__(32 * (NS + 4), 1)
     __shared__ Bars bars;
     __shared__ uint32_t tmem_base_s;
     __shared__ uint32_t abort_s;
-    // NS = 16: row maxima (per block parity) and row sums (per tile) passed
-    // between the two warps that hold the two key halves of the same rows
-    __shared__ float xmax[NS == 16 ? 2 : 1][8][2][16];
-    __shared__ float xsum[8][2][16];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Persistent: each CTA takes one tile of every round of gridDim.x tiles
@@ -174,7 +161,7 @@ __global__ void __launch_bounds__(32 * (NS + 4), 1)
         // key position of the tile's first query row (causal over gathered
         // keys: its global row; otherwise its row in the segment)
         const int r0 = x.qt * 128;
-        x.g0 = (!PARTIAL && g.q_split) ? (r0 < g.q_split ? g.q_goff0 + r0 : g.q_goff1 + (r0 - g.q_split)) : r0;
+        x.g0 = GQ ? (r0 < g.q_split ? g.q_goff0 + r0 : g.q_goff1 + (r0 - g.q_split)) : r0;
         x.nb = CAUSAL ? min(nkb, x.g0 / BLK + 1) : nkb;
         return x;
     };
@@ -208,7 +195,6 @@ __global__ void __launch_bounds__(32 * (NS + 4), 1)
         }
         mbar_init(bar(bars.qk_done), 1);
         mbar_init(bar(bars.pv_done), 1);
-        for (int i = 0; i < 8; i++) mbar_init(bar(bars.xpair[i]), 2);
         fence_barrier_init();
     }
     __syncthreads();
@@ -350,243 +336,6 @@ __global__ void __launch_bounds__(32 * (NS + 4), 1)
             tc_commit(bar(bars.pv_done));
             mbar_wait(bar(bars.pv_done), 0, err, 16, false);
         }
-    } else if constexpr (NS == 16) {
-        // ------------------------------------------------------------ softmax + correction, quarter rows
-        // Warp w: TMEM lane quarter q = w % 4 (its SM sub-partition), rows
-        // 32q + 16s + (0..15) with s = (w / 4) % 2, key half kh = w / 8 of
-        // every 128-key block (one k_scale group) and output columns
-        // [kh D/2, kh D/2 + D/2).  Lane t < 16 takes keys kh*64 + 0..31 and
-        // columns kh D/2 + 0..D/4-1 of row t, lane t + 16 keys kh*64 +
-        // 32..63 and the next D/4 columns of the same row.  The two warps of
-        // a row set (kh 0 and 1) exchange their block maxima and, per tile,
-        // their row sums through shared memory and a named barrier.
-        constexpr int DQ = D / 4;
-        const int quarter = warp & 3, sub = (warp >> 2) & 1, kh = warp >> 3;
-        const int half = lane >> 4;
-        const int r = quarter * 32 + sub * 16 + (lane & 15);
-        const int pair = quarter * 2 + sub;  // row set
-        // The two warps of the row set meet on bars.xpair[pair] (two
-        // arrivals per phase, a bounded wait): every exchange is one phase,
-        // in the same order in both warps.
-        uint32_t xr = 0;
-        auto pair_sync = [&](uint32_t site) -> bool {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(bars.xpair[pair]));
-            const bool met = warp_wait(bar(bars.xpair[pair]), xr & 1, err, site);
-            xr++;
-            return met;
-        };
-        const uint32_t lane_base = (uint32_t)(quarter * 32 + sub * 16) << 16;
-        const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
-        int J = 0;
-        bool ok = true;
-        auto first_scales = [&](int t, float& q_s, float& k_s) {
-            if (t >= ntiles) return;
-            const Tile x = tile_of(t);
-            const int row_ws = (PARTIAL ? q_tile0 * 128 : 0) + x.qt * 128 + r;
-            q_s = __ldg(q_scale + (long long)x.bh_q * (g.tq_pad / QGROUP) + row_ws / QGROUP);
-            const int i0 = kh < nkb64_seg ? kh : 0;
-            k_s = __ldg(k_scale + (long long)x.bh_kv * nkb64 + k_key0 / KBLOCK + i0);
-        };
-        constexpr bool PREFETCH = CAUSAL != PARTIAL;
-        float qs_next = 0.f, ks_next = 0.f;
-        if (PREFETCH) first_scales(tile_at(0), qs_next, ks_next);
-        for (int it = 0, t = tile_at(0); t < ntiles && ok; t = tile_at(++it)) {
-        const Tile tl = tile_of(t);
-        const int bh_q = tl.bh_q, bh_kv = tl.bh_kv, qt = tl.qt, nb = tl.nb;
-        const int qrow = tl.g0 + r;
-        const int qrow_ws = (PARTIAL ? q_tile0 + qt : qt) * 128 + r;
-        const float qs =
-            PREFETCH ? qs_next : __ldg(q_scale + (long long)bh_q * (g.tq_pad / QGROUP) + qrow_ws / QGROUP);
-        const float* ksc = k_scale + (long long)bh_kv * nkb64 + k_key0 / KBLOCK;
-        float o[DQ];
-#pragma unroll
-        for (int c = 0; c < DQ; c++) o[c] = 0.f;
-        float m = -1.0e30f, l = 0.f, alpha_prev = 0.f;
-        auto kscale = [&](int jb) {
-            const int i = 2 * jb + kh;
-            return __ldg(ksc + (i < nkb64_seg ? i : 2 * jb));
-        };
-        float ks = PREFETCH ? ks_next : kscale(0);
-        // O = O * a + PV[block jj] for this lane's D/4 columns
-        auto correct = [&](int jj, float a) -> bool {
-            const int pb = jj & 1;
-            if (!warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31)) return false;
-            tc_fence_after();
-            const uint64_t a2 = pk2(a, a);
-            const uint32_t ta = tmem + lane_base + (pb ? TM_PV1 : TM_PV0) + kh * DH;
-            uint32_t pv[DQ];
-            if constexpr (DQ == 32)
-                tmem_ld16x2<DQ>(ta, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
-            else
-                tmem_ld16x2_16<DQ>(ta, *reinterpret_cast<uint32_t(*)[16]>(&pv[0]));
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < DQ; e += 2)
-                upk2(fma2(pk2(o[e], o[e + 1]), a2, pk2(__uint_as_float(pv[e]), __uint_as_float(pv[e + 1]))), o[e],
-                     o[e + 1]);
-            return true;
-        };
-        for (int j = 0; j < nb; j++, J++) {
-            const int sb = J & 1;
-            const float sc = qs * ks;
-            if (j + 1 < nb) ks = kscale(j + 1);
-            if (!warp_wait(bar(bars.s_full[sb]), (J >> 1) & 1, err, 20)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[32];
-            tmem_ld16x2<32>(tmem + lane_base + (sb ? TM_S1 : TM_S0) + kh * 64, sr);
-            tmem_wait_ld();
-            float x[32];
-            const int key0 = j * BLK + kh * 64 + half * 32;
-            if (MERGE) {
-                const float c0 = -MAGIC_F * sc;
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const int key = key0 + c;
-                    const float kb = key < g.tk_pad ? __ldg(kbias + key) : __int_as_float(0xff800000);
-                    x[c] = fmaf(__uint_as_float(sr[c]), sc, kb + c0);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 32; c++) x[c] = __uint_as_float(sr[c]);
-            }
-            if (j * BLK + BLK > g.tk || (CAUSAL && j * BLK + BLK > tl.g0)) {
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const int key = key0 + c;
-                    if (key >= g.tk || (CAUSAL && key > qrow)) x[c] = __int_as_float(0xff800000);
-                }
-            }
-            float ma = x[0], mb = x[1];
-#pragma unroll
-            for (int c = 2; c < 30; c += 4) {
-                ma = fmax3(ma, x[c], x[c + 1]);
-                mb = fmax3(mb, x[c + 2], x[c + 3]);
-            }
-            float pm = fmax3(ma, mb, fmaxf(x[30], x[31]));
-            if (!MERGE) pm = fmaf(pm, sc, -MAGIC_F * sc);  // -inf stays -inf
-            pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
-            // the other key half's maximum of the same rows
-            if (lane < 16) xmax[sb][pair][kh][lane] = pm;
-            if (!pair_sync(32)) {
-                ok = false;
-                break;
-            }
-            const float mnew = fmax3(m, pm, xmax[sb][pair][kh ^ 1][lane & 15]);
-            const float alpha = ex2(m - mnew);
-            m = mnew;
-            const uint32_t prow_addr = sP + sb * L::P_BYTES + prow;
-            const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
-            const uint64_t sc2 = pk2(MERGE ? 1.0f : sc, MERGE ? 1.0f : sc), off2 = pk2(off, off);
-            uint64_t sum2a = pk2(0.f, 0.f), sum2b = sum2a;
-#pragma unroll
-            for (int c16 = 0; c16 < 2; c16++) {
-                float p[16];
-#pragma unroll
-                for (int e = 0; e < 16; e += 2) {
-                    float y0, y1;
-                    upk2(fma2(pk2(x[c16 * 16 + e], x[c16 * 16 + e + 1]), sc2, off2), y0, y1);
-                    if (e < EXP_POLY) {
-                        exp2_poly2(y0, y1, p[e], p[e + 1]);
-                    } else {
-                        p[e] = ex2(y0);
-                        p[e + 1] = ex2(y1);
-                    }
-                    if ((e >> 1) & 1)
-                        sum2b = add2(sum2b, pk2(p[e], p[e + 1]));
-                    else
-                        sum2a = add2(sum2a, pk2(p[e], p[e + 1]));
-                }
-                uint32_t w[4];
-#pragma unroll
-                for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
-                const int chunk = kh * 4 + half * 2 + c16;
-                const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
-                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                             "r"(w[3])
-                             : "memory");
-            }
-            float s0, s1, s2, s3;
-            upk2(sum2a, s0, s1);
-            upk2(sum2b, s2, s3);
-            l = fmaf(l, alpha, (s0 + s1) + (s2 + s3));
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(bars.p_full[sb]));  // one arrival per warp
-            if (j >= 1 && !correct(J - 1, alpha_prev)) {
-                ok = false;
-                break;
-            }
-            alpha_prev = alpha;
-        }
-        if (ok) ok = correct(J - 1, alpha_prev);
-        if (!ok) break;
-        if (PREFETCH) first_scales(tile_at(it + 1), qs_next, ks_next);
-        // the row's sum: this lane pair, then the other key half's warp (both
-        // warps add the same two numbers, so both hold the same sum)
-        float lt = l + __shfl_xor_sync(0xffffffffu, l, 16);
-        if (lane < 16) xsum[pair][kh][lane] = lt;
-        if (!(ok = pair_sync(33))) break;
-        lt += xsum[pair][kh ^ 1][lane & 15];
-        // (the next write of xsum comes after the next tile's first block
-        // exchange, by which the other warp has read this one)
-        const int c0 = kh * DH + half * DQ;  // this lane's first output column
-        if (ok && !PARTIAL) {
-            const float inv = 1.0f / lt;
-            const float* vmean = stats + (long long)bh_kv * 4 * D + D + c0;
-            const float* vscale = vmean + D;
-            uint16_t* orow = out + (long long)(bh_q / g.heads) * g.o_sb + (long long)qrow_ws * g.o_st +
-                             (long long)(bh_q % g.heads) * g.o_sh + c0;
-            if (qrow_ws < g.tokens) {
-#pragma unroll
-                for (int c = 0; c < DQ; c += 8) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e2 = 0; e2 < 4; e2++) {
-                        const int d = c + 2 * e2;
-                        const float y0 = fmaf(o[d] * inv, __ldg(vscale + d), __ldg(vmean + d));
-                        const float y1 = fmaf(o[d + 1] * inv, __ldg(vscale + d + 1), __ldg(vmean + d + 1));
-                        w[e2] = pack_bf16x2(y0, y1);
-                    }
-                    *reinterpret_cast<uint4*>(orow + c) = make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-        }
-        if (ok && PARTIAL) {
-            const float inv = 1.0f / lt;
-            const float lse_new = m + log2f(lt) - LOG2_448;
-            float* lrow = lse + (long long)bh_q * g.tokens + qrow_ws;
-            const float lse_old = g.cp_first ? __int_as_float(0xff800000) : *lrow;
-            const float mx = fmaxf(lse_old, lse_new);
-            const float w_old = lse_old == __int_as_float(0xff800000) ? 0.f : exp2f(lse_old - mx);
-            const float w_new = exp2f(lse_new - mx);
-            const float s_inv = 1.0f / (w_old + w_new);
-            const float a_old = w_old * s_inv, a_new = w_new * inv * s_inv;
-            const float* vmean = stats + (long long)bh_kv * 4 * D + D + c0;
-            const float* vscale = vmean + D;
-            float* arow = acc + (long long)(bh_q / g.heads) * g.o_sb + (long long)qrow_ws * g.o_st +
-                          (long long)(bh_q % g.heads) * g.o_sh + c0;
-            if (qrow_ws < g.tokens) {
-#pragma unroll
-                for (int c = 0; c < DQ; c += 4) {
-                    float4 x = w_old > 0.f ? *reinterpret_cast<const float4*>(arow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    x.x = fmaf(x.x, a_old, fmaf(o[c] * a_new, __ldg(vscale + c), __ldg(vmean + c) * w_new * s_inv));
-                    x.y = fmaf(x.y, a_old, fmaf(o[c + 1] * a_new, __ldg(vscale + c + 1), __ldg(vmean + c + 1) * w_new * s_inv));
-                    x.z = fmaf(x.z, a_old, fmaf(o[c + 2] * a_new, __ldg(vscale + c + 2), __ldg(vmean + c + 2) * w_new * s_inv));
-                    x.w = fmaf(x.w, a_old, fmaf(o[c + 3] * a_new, __ldg(vscale + c + 3), __ldg(vmean + c + 3) * w_new * s_inv));
-                    *reinterpret_cast<float4*>(arow + c) = x;
-                }
-            }
-            // every reader of lse (all four threads of the row) has read it
-            // before the one writer replaces it
-            if (!(ok = pair_sync(34))) break;
-            if (half == 0 && kh == 0 && qrow_ws < g.tokens) *lrow = mx + log2f(w_old + w_new);
-        }
-        }  // tiles
     } else {
         // ------------------------------------------------------------ softmax + correction
         const int quarter = warp & 3, sub = warp >> 2;
@@ -818,11 +567,11 @@ __global__ void __launch_bounds__(32 * (NS + 4), 1)
     if (warp == QK_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-template <int D, bool CAUSAL, bool MERGE, bool PARTIAL, int NS = SP_SOFTMAX_WARPS>
+template <int D, bool CAUSAL, bool MERGE, bool PARTIAL, bool GQ = false>
 static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out, float* acc, float* lse,
                             int q_tiles, cudaStream_t st) {
     static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
-    auto kern = sp_attn<D, CAUSAL, MERGE, PARTIAL, NS>;
+    auto kern = sp_attn<D, CAUSAL, MERGE, PARTIAL, GQ>;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 32 || !(attr_set.load(std::memory_order_acquire) & (1u << dev))) {
@@ -840,7 +589,7 @@ static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)g.batch * g.heads * q_tiles;
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
-    kern<<<grid, Roles<NS>::THREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,
+    kern<<<grid, NTHREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,
                                                    buf.kbias, (uint16_t*)out, acc, lse, buf.err, g);
     return cudaGetLastError();
 }
@@ -849,6 +598,11 @@ cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const
                           cudaStream_t st) {
     const bool merge = g.merge > 1, causal = g.causal != 0;
     const int qt = g.tq_pad / 128;
+    if (g.q_split) {  // causal over gathered keys (context parallelism by all-gather)
+        if (!causal || merge) return cudaErrorInvalidValue;
+        return d == 64 ? attend_t<64, true, false, false, true>(maps, buf, g, out, nullptr, nullptr, qt, st)
+                       : attend_t<128, true, false, false, true>(maps, buf, g, out, nullptr, nullptr, qt, st);
+    }
     if (d == 64) {
         if (merge) return attend_t<64, false, true, false>(maps, buf, g, out, nullptr, nullptr, qt, st);
         return causal ? attend_t<64, true, false, false>(maps, buf, g, out, nullptr, nullptr, qt, st)
@@ -872,11 +626,10 @@ cudaError_t launch_attend_partial(int d, const AttnMaps& maps, const Buffers& bu
 
 cudaError_t attn_func_attributes(int d, int merge, int* regs, int* local_bytes) {
     cudaFuncAttributes a;
-    constexpr int NS = SP_SOFTMAX_WARPS;
-    cudaError_t e = d == 64 ? (merge ? cudaFuncGetAttributes(&a, sp_attn<64, false, true, false, NS>)
-                                     : cudaFuncGetAttributes(&a, sp_attn<64, false, false, false, NS>))
-                            : (merge ? cudaFuncGetAttributes(&a, sp_attn<128, false, true, false, NS>)
-                                     : cudaFuncGetAttributes(&a, sp_attn<128, false, false, false, NS>));
+    cudaError_t e = d == 64 ? (merge ? cudaFuncGetAttributes(&a, sp_attn<64, false, true, false>)
+                                     : cudaFuncGetAttributes(&a, sp_attn<64, false, false, false>))
+                            : (merge ? cudaFuncGetAttributes(&a, sp_attn<128, false, true, false>)
+                                     : cudaFuncGetAttributes(&a, sp_attn<128, false, false, false>));
     if (e != cudaSuccess) return e;
     *regs = a.numRegs;
     *local_bytes = (int)a.localSizeBytes;
