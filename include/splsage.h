@@ -393,6 +393,9 @@ int spl_sage_cp_finish(spl_sage* s, const spl_sage_ws* ws, const float* acc, spl
  * tokens / 2, whole 128-row tiles); local row i attends the gathered keys 0
  * .. its global row; bf16 into out, with the statistics of
  * spl_sage_cp_quantize_kv. */
+/* Context-parallel schedules (spl_sage_ring_schedule). */
+#define SPL_SAGE_CP_RING 0   /* send/recv ring, one segment launch per step (default) */
+#define SPL_SAGE_CP_GATHER 1 /* all-gather, one causal launch over the whole sequence */
 int spl_sage_kv_create_gathered(spl_sage* s, const spl_sage_ws* ws, int64_t tokens, void* k8, float* k_scale,
                                 void* v8, spl_sage_kv** out);
 int spl_sage_cp_attend_gathered(spl_sage* s, const spl_sage_ws* ws, const spl_sage_kv* kv_all, int64_t q_off0,
@@ -419,6 +422,13 @@ typedef struct spl_sage_ring spl_sage_ring;
 int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int world, int reserved_sms,
                          spl_sage_ring** out);
 void spl_sage_ring_destroy(spl_sage_ring* r);
+/* The schedule of spl_sage_ring_forward: SPL_SAGE_CP_RING (default) or
+ * SPL_SAGE_CP_GATHER: after step 3 the K/V buffers of all ranks are
+ * gathered with ncclAllGather into a staging area, laid out in global key
+ * order by strided device copies, and attended in one causal launch per
+ * rank (spl_sage_cp_attend_gathered); the whole sequence's K/V buffer and
+ * the staging area are allocated by the first such forward. */
+int spl_sage_ring_schedule(spl_sage_ring* r, int schedule);
 
 /* The segment step `step` of rank `rank` attends (the schedule
  * spl_sage_ring_forward follows), as arguments of spl_sage_cp_attend with

@@ -103,12 +103,14 @@ EXPORTS = [
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
     "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
     "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest", "spl_sage_ring_segment",
-    "spl_sage_kv_create_gathered", "spl_sage_cp_attend_gathered",
+    "spl_sage_kv_create_gathered", "spl_sage_cp_attend_gathered", "spl_sage_ring_schedule",
 ]
 
 # spl_sage_cp_attend flags
 CP_CAUSAL = 1
 CP_FIRST = 2
+# spl_sage_ring_schedule
+CP_SCHEDULES = {"ring": 0, "gather": 1}
 
 _lib = None
 
@@ -132,6 +134,7 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_ring_create.argtypes = [P, ctypes.POINTER(_Shape), I, I, I, ctypes.POINTER(P)]
         L.spl_sage_ring_destroy.argtypes = [P]
         L.spl_sage_ring_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
+        L.spl_sage_ring_schedule.argtypes = [P, I]
         L.spl_sage_kv_create_gathered.argtypes = [P, P, ctypes.c_int64, P, P, P, ctypes.POINTER(P)]
         L.spl_sage_cp_attend_gathered.argtypes = [P, P, P, ctypes.c_int64, ctypes.c_int64, _Tensor]
         L.spl_sage_ring_segment.argtypes = [I, I, I, ctypes.c_int64] + [ctypes.POINTER(ctypes.c_int64)] * 4 + [
@@ -613,11 +616,15 @@ class NativeRing:
     an integer; 0 when world = 1)."""
 
     def __init__(self, eng: "SageAttention", batch: int, heads: int, kv_heads: int, local_tokens: int, rank: int,
-                 world: int, reserved_sms: int = 1):
+                 world: int, reserved_sms: int = 1, schedule: str = "ring"):
         cs = _Shape(batch, heads, kv_heads, local_tokens, 0, 0)
         h = ctypes.c_void_p()
         _check(lib().spl_sage_ring_create(eng._h, ctypes.byref(cs), rank, world, reserved_sms, ctypes.byref(h)))
         self._h, self.eng = h, eng
+        if schedule not in CP_SCHEDULES:
+            self.close()
+            raise SageError(ERR_INVALID, f"unknown context-parallel schedule {schedule!r}")
+        _check(lib().spl_sage_ring_schedule(self._h, CP_SCHEDULES[schedule]))
 
     def forward(self, q: Tensor, k: Tensor, v: Tensor, out: Tensor, opts: Options | None = None, comm: int = 0):
         o = (opts or Options())._c()

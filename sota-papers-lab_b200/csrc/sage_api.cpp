@@ -1211,6 +1211,7 @@ namespace {
 // libnccl.so.2; the library itself does not link NCCL.
 struct NcclFns {
     decltype(&ncclAllReduce) all_reduce;
+    decltype(&ncclAllGather) all_gather;
     decltype(&ncclSend) send;
     decltype(&ncclRecv) recv;
     decltype(&ncclGroupStart) group_start;
@@ -1227,12 +1228,13 @@ const NcclFns* nccl_fns() {
         if (!dlsym(h, "ncclSend")) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (!h) return;
         f.all_reduce = (decltype(f.all_reduce))dlsym(h, "ncclAllReduce");
+        f.all_gather = (decltype(f.all_gather))dlsym(h, "ncclAllGather");
         f.send = (decltype(f.send))dlsym(h, "ncclSend");
         f.recv = (decltype(f.recv))dlsym(h, "ncclRecv");
         f.group_start = (decltype(f.group_start))dlsym(h, "ncclGroupStart");
         f.group_end = (decltype(f.group_end))dlsym(h, "ncclGroupEnd");
         f.error_string = (decltype(f.error_string))dlsym(h, "ncclGetErrorString");
-        ok = f.all_reduce && f.send && f.recv && f.group_start && f.group_end && f.error_string;
+        ok = f.all_reduce && f.all_gather && f.send && f.recv && f.group_start && f.group_end && f.error_string;
     });
     return ok ? &f : nullptr;
 }
@@ -1255,6 +1257,13 @@ struct spl_sage_ring {
     float* raw;  // [bg][4][D], then raw_sum and raw_max after it
     cudaStream_t comm;
     cudaEvent_t ev_compute, ev_comm;
+    // schedule 1 (gather): every rank's K/V buffer gathered (staging, world
+    // x the buffer) and laid out in key order in kv_all (allocated on first use)
+    int schedule;
+    size_t kv_total, kso, v8o;
+    void* staging;
+    void* all_mem;
+    spl_sage_kv* kv_all;
 };
 
 extern "C" {
@@ -1268,6 +1277,9 @@ void spl_sage_ring_destroy(spl_sage_ring* r) {
     cudaFree(r->acc);
     cudaFree(r->lse);
     cudaFree(r->raw);
+    spl_sage_kv_destroy(r->kv_all);
+    cudaFree(r->staging);
+    cudaFree(r->all_mem);
     if (r->comm) cudaStreamDestroy(r->comm);
     if (r->ev_compute) cudaEventDestroy(r->ev_compute);
     if (r->ev_comm) cudaEventDestroy(r->ev_comm);
@@ -1310,6 +1322,9 @@ int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int
     const size_t k8o = 0, kso = ((size_t)r->k8_bytes + 255) & ~(size_t)255;
     const size_t v8o = (kso + (size_t)r->ks_bytes + 255) & ~(size_t)255;
     const size_t kv_total = v8o + (size_t)r->v8_bytes;
+    r->kv_total = kv_total;
+    r->kso = kso;
+    r->v8o = v8o;
     const size_t acc_n = (size_t)(r->batch * r->tokens * r->heads * D);
     const size_t lse_n = (size_t)(r->batch * r->heads * r->tokens);
     const size_t raw_n = (size_t)(r->batch * r->kv_heads * 4 * D);
@@ -1334,6 +1349,14 @@ int spl_sage_ring_create(spl_sage* s, const spl_sage_shape* local, int rank, int
         }
     }
     *out = r;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_ring_schedule(spl_sage_ring* r, int schedule) {
+    if (!r) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_schedule: NULL ring");
+    if (schedule != SPL_SAGE_CP_RING && schedule != SPL_SAGE_CP_GATHER)
+        return fail(SPL_SAGE_ERR_INVALID, "unknown context-parallel schedule %d", schedule);
+    r->schedule = schedule;
     return SPL_SAGE_OK;
 }
 
@@ -1365,6 +1388,55 @@ int spl_sage_ring_segment(int rank, int world, int step, int64_t chunk, int64_t*
     return SPL_SAGE_OK;
 }
 
+}  // extern "C"
+
+// The gather schedule after step 3: every rank's K/V buffer all-gathered,
+// laid out in global key order (rank s's local chunks 0 and 1 are global
+// chunks s and 2P-1-s), then one causal launch over it.
+static int ring_gather(spl_sage* s, spl_sage_ring* r, spl_sage_tensor_mut out, const NcclFns* nc, ncclComm_t comm) {
+    const int64_t D = s->head_dim, C = r->chunk, P = r->world, T = r->tokens, N = T * P;
+    const int64_t BG = r->batch * r->kv_heads;
+    if (!r->kv_all) {  // first use: the whole sequence's buffer (and the staging area)
+        int64_t k8b = BG * N * D, ksb = BG * (N / KBLOCK) * 4, v8b = BG * D * N;
+        const size_t kso = ((size_t)k8b + 255) & ~(size_t)255, v8o = (kso + (size_t)ksb + 255) & ~(size_t)255;
+        cudaError_t e = cudaMalloc(&r->all_mem, v8o + (size_t)v8b);
+        if (e == cudaSuccess && P > 1) e = cudaMalloc(&r->staging, r->kv_total * (size_t)P);
+        if (e != cudaSuccess) return cuda_fail(e, "allocate the gathered K/V buffers");
+        uint8_t* m = (uint8_t*)r->all_mem;
+        int rc = spl_sage_kv_create_gathered(s, r->ws, N, m, (float*)(m + kso), m + v8o, &r->kv_all);
+        if (rc) return rc;
+    }
+    const uint8_t* parts = (const uint8_t*)r->kv_mem[0];
+    if (P > 1) {
+        ncclResult_t nr = nc->all_gather(r->kv_mem[0], r->staging, r->kv_total, ncclUint8, comm, s->stream);
+        if (nr != ncclSuccess) return nccl_fail(nc, nr, "gather: K/V all-gather");
+        parts = (const uint8_t*)r->staging;
+    }
+    // layout: k8 [bg][t][D] rows of C*D bytes, k_scale [bg][t/64] rows of
+    // C/64 floats, v8 [bg][D][t] rows of C bytes
+    spl_sage_kv* a = r->kv_all;
+    for (int64_t src = 0; src < P; src++) {
+        const uint8_t* pk = parts + (size_t)src * r->kv_total;
+        for (int c = 0; c < 2; c++) {
+            const int64_t gch = c == 0 ? src : 2 * P - 1 - src;
+            cudaError_t e = cudaMemcpy2DAsync((uint8_t*)a->k8 + gch * C * D, (size_t)(N * D), pk + c * C * D,
+                                              (size_t)(T * D), (size_t)(C * D), (size_t)BG,
+                                              cudaMemcpyDeviceToDevice, s->stream);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(a->k_scale + gch * (C / KBLOCK), (size_t)(N / KBLOCK) * 4,
+                                      pk + r->kso + c * (C / KBLOCK) * 4, (size_t)(T / KBLOCK) * 4,
+                                      (size_t)(C / KBLOCK) * 4, (size_t)BG, cudaMemcpyDeviceToDevice, s->stream);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(a->v8 + gch * C, (size_t)N, pk + r->v8o + c * C, (size_t)T, (size_t)C,
+                                      (size_t)(BG * D), cudaMemcpyDeviceToDevice, s->stream);
+            if (e != cudaSuccess) return cuda_fail(e, "lay out the gathered K/V");
+        }
+    }
+    return spl_sage_cp_attend_gathered(s, r->ws, r->kv_all, r->rank * C, (2 * P - 1 - r->rank) * C, out);
+}
+
+extern "C" {
+
 int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_sage_tensor k, spl_sage_tensor v,
                           spl_sage_tensor_mut out, const spl_sage_options* opts, void* nccl_comm) {
     if (!s || !r) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_ring_forward: NULL argument");
@@ -1394,6 +1466,7 @@ int spl_sage_ring_forward(spl_sage* s, spl_sage_ring* r, spl_sage_tensor q, spl_
     // 3. this rank's K/V quantised with them
     rc = spl_sage_cp_quantize_kv(s, r->ws, k, v, opts, r->raw, r->tokens * P, r->kv[0]);
     if (rc) return rc;
+    if (r->schedule == SPL_SAGE_CP_GATHER) return ring_gather(s, r, out, nc, comm);
     // 4. P steps, one segment launch each, the K/V moving one rank on
     // meanwhile; the segments leave the ring's reserved SMs to NCCL
     int cur = 0;

@@ -50,17 +50,18 @@ def _f32(t):
     return O.bf16_to_f32(t.view(torch.int16).cpu().numpy().view(np.uint16))
 
 
-def test_native_ring_one_rank_equals_python_ring():
+@pytest.mark.parametrize("schedule", ["ring", "gather"])
+def test_native_ring_one_rank_equals_python_ring(schedule):
     b, t, h, g, d = 2, 1024, 8, 2, 128
     q, k, v = (x.cuda() for x in _qkv(b, t, h, g, d, seed=3))
     eng = sage.SageAttention(torch.cuda.current_stream(), d)
     sq, skv = sage.Strides.bthd(t, h, d), sage.Strides.bthd(t, g, d)
     args = (sage.Tensor(q, sq), sage.Tensor(k, skv), sage.Tensor(v, skv))
-    nat = sage.NativeRing(eng, b, h, g, t, 0, 1)
+    nat = sage.NativeRing(eng, b, h, g, t, 0, 1, schedule=schedule)
     out_n = torch.zeros(b, t, h, d, dtype=torch.bfloat16, device="cuda")
     for _ in range(2):  # twice: the ring's buffers carry no state between calls
         nat.forward(*args, sage.Tensor(out_n, sq))
-    py = ring.RingAttention(eng, b, h, g, t, 0, 1, d)
+    py = ring.RingAttention(eng, b, h, g, t, 0, 1, d, schedule=schedule)
     out_p = torch.zeros_like(out_n)
     py.forward(*args, sage.Tensor(out_p, sq))
     torch.cuda.synchronize()
@@ -72,13 +73,15 @@ def test_native_ring_one_rank_equals_python_ring():
     py.close()
     with pytest.raises(sage.SageError):
         sage.NativeRing(eng, b, h, g, 1000, 0, 1)  # not two chunks of whole tiles
+    with pytest.raises(sage.SageError):
+        sage.NativeRing(eng, b, h, g, t, 0, 1, schedule="tree")
 
 
 class _UniqueId(ctypes.Structure):
     _fields_ = [("internal", ctypes.c_byte * 128)]
 
 
-def _rank(rank, world, uid_q, res_q, shape):
+def _rank(rank, world, uid_q, res_q, shape, schedule="ring"):
     torch.cuda.set_device(rank)
     nccl = ctypes.CDLL("libnccl.so.2")
     if rank == 0:
@@ -96,7 +99,7 @@ def _rank(rank, world, uid_q, res_q, shape):
     q, k, v = _qkv(b, t_all, h, g, d, seed=11)
     qs, ks, vs = (ring.shard_zigzag(x, rank, world).cuda() for x in (q, k, v))
     eng = sage.SageAttention(torch.cuda.current_stream(), d)
-    nat = sage.NativeRing(eng, b, h, g, t, rank, world)
+    nat = sage.NativeRing(eng, b, h, g, t, rank, world, schedule=schedule)
     out = torch.zeros(b, t, h, d, dtype=torch.bfloat16, device="cuda")
     sq, skv = sage.Strides.bthd(t, h, d), sage.Strides.bthd(t, g, d)
     nat.forward(sage.Tensor(qs, sq), sage.Tensor(ks, skv), sage.Tensor(vs, skv), sage.Tensor(out, sq),
@@ -108,12 +111,13 @@ def _rank(rank, world, uid_q, res_q, shape):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_native_ring_two_ranks_over_nccl():
+@pytest.mark.parametrize("schedule", ["ring", "gather"])
+def test_native_ring_two_ranks_over_nccl(schedule):
     world, shape = 2, (1, 4096, 8, 2, 128)
     ctx = mp.get_context("spawn")
     uid_q, res_q = ctx.Queue(), ctx.Queue()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    procs = [ctx.Process(target=_rank, args=(r, world, uid_q, res_q, shape)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid_q, res_q, shape, schedule)) for r in range(world)]
     for p in procs:
         p.start()
     outs = {}
