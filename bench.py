@@ -607,7 +607,7 @@ def run_ours(args, rank, world, local_rank):
     del bufs, views, qh, kh, vh, oh
 
     block = qkv = qkv8 = ring_sub = None
-    if w.get("qkv"):
+    if w.get("qkv") and not args.no_extras:
         block = c4_block_time(eng, wr, B, dev, stream, rank, world, max_over_ranks)
         qkv = qkv_gemm_time(eng, w, dev, stream) if rank == 0 else None
         qkv8 = qkv_fp8_time(eng, w, dev, stream) if rank == 0 else None
@@ -994,6 +994,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="C4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="C4: leave out the c4_block, qkv_gemm, qkv_fp8 and ring_c5 measurements (quick runs, profiling)")
     ap.add_argument("--cp-schedule", default="gather", choices=["gather", "ring"],
                     help="C5: all-gather the quantised K/V (default) or pass it around a send/recv ring")
     ap.add_argument("--reserve-sms", type=int, default=None,

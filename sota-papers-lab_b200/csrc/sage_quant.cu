@@ -239,9 +239,7 @@ __global__ void __launch_bounds__(128) sp_finalize(const float* __restrict__ par
         const float* p = part + bh * g.q_tiles * 4 * D + stat * D + d;
         float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
         float r1 = r0;
-        int t = 0;
-        for (; t + 1 < g.q_tiles; t += 2) {
-            const float x0 = p[(long long)t * 4 * D], x1 = p[(long long)(t + 1) * 4 * D];
+        auto acc2 = [&](float x0, float x1) {
             if (stat < 2) {
                 r0 += x0;
                 r1 += x1;
@@ -252,7 +250,18 @@ __global__ void __launch_bounds__(128) sp_finalize(const float* __restrict__ par
                 r0 = fmaxf(r0, x0);
                 r1 = fmaxf(r1, x1);
             }
+        };
+        int t = 0;
+        // 16 tiles' partials loaded before they are added (in tile order), so
+        // that the loads' latency is paid once per 16 tiles, not per tile
+        for (; t + 16 <= g.q_tiles; t += 16) {
+            float x[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) x[i] = p[(long long)(t + i) * 4 * D];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) acc2(x[i], x[i + 1]);
         }
+        for (; t + 1 < g.q_tiles; t += 2) acc2(p[(long long)t * 4 * D], p[(long long)(t + 1) * 4 * D]);
         if (t < g.q_tiles) {
             const float x0 = p[(long long)t * 4 * D];
             r0 = stat < 2 ? r0 + x0 : (stat == 2 ? fminf(r0, x0) : fmaxf(r0, x0));
