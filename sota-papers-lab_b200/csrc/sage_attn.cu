@@ -383,9 +383,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // level of the FP32 accumulation (each block's PV starts from zero).
         // Waiting for p_free[jj % 2] (committed after PV(jj)) also frees
         // the P buffer of block jj + 2.
+        // Barriers tested early (a try_wait issued well before its result is
+        // needed, so that its latency stays off the softmax warps' path):
+        // pv_ready for the fold's PV, s_ready for the next block's S.
+        bool pv_ready = false, s_ready = false;
         auto correct = [&](int jj, float a) -> bool {
             const int pb = jj & 1;
-            if (!warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31)) return false;
+            if (!__all_sync(0xffffffffu, pv_ready) && !warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31))
+                return false;
             tc_fence_after();
             const uint64_t a2 = pk2(a, a);
 #pragma unroll
@@ -406,10 +411,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int sb = J & 1;
             const float sc = qs * ks;
             if (j + 1 < nb) ks = kscale(j + 1);
-            if (!warp_wait(bar(bars.s_full[sb]), (J >> 1) & 1, err, 20)) {
+            if (!__all_sync(0xffffffffu, s_ready) && !warp_wait(bar(bars.s_full[sb]), (J >> 1) & 1, err, 20)) {
                 ok = false;
                 break;
             }
+            s_ready = false;
             tc_fence_after();
             uint32_t sr[64];
             {
@@ -481,6 +487,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 uint32_t w[4];
 #pragma unroll
                 for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
+                // the fold's PV (block J - 1) is usually done by now
+                if (c16 == 1 && j >= 1) pv_ready = mbar_try(bar(bars.p_free[(J - 1) & 1]), ((J - 1) >> 1) & 1);
                 const int chunk = half * 4 + c16;
                 const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
                 asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
@@ -496,10 +504,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(bars.p_full[sb]));  // one arrival per warp
             // fold the previous block's PV into O while this block's PV runs
+            // the next block's S is usually finished during this block
+            if (j + 1 < nb) s_ready = mbar_try(bar(bars.s_full[(J + 1) & 1]), ((J + 1) >> 1) & 1);
             if (j >= 1 && !correct(J - 1, alpha_prev)) {
                 ok = false;
                 break;
             }
+            pv_ready = false;
             alpha_prev = alpha;
         }
         if (ok) ok = correct(J - 1, alpha_prev);  // the tile's last block

@@ -184,6 +184,17 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of phase `parity` of `bar` (acquire when it returns true).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for phase `parity` of `bar`.  Gives up (returns false) after
 // LIMIT_NS (or WAIT_MAX_TRIES), recording ERR_TIMEOUT and the wait site in
 // the device error word, or, with bail_on_err, as soon as anyone has set the
