@@ -503,9 +503,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(bars.p_full[sb]));  // one arrival per warp
-            // fold the previous block's PV into O while this block's PV runs
             // the next block's S is usually finished during this block
             if (j + 1 < nb) s_ready = mbar_try(bar(bars.s_full[(J + 1) & 1]), ((J + 1) >> 1) & 1);
+            // fold the previous block's PV into O while this block's PV runs
             if (j >= 1 && !correct(J - 1, alpha_prev)) {
                 ok = false;
                 break;
