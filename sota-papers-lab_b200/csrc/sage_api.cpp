@@ -108,6 +108,7 @@ struct spl_sage {
     int sm_count;
     int reserved_sms;  // SMs the persistent kernels leave free (spl_sage_reserve_sms)
     int gemm_pairs;    // GEMMs on SM pairs (spl_sage_gemm_pairs)
+    int quant_one_launch;  // the quantiser as one persistent launch (spl_sage_quant_one_launch)
     uint32_t* err;     // device error word of the calls that run without a workspace
 };
 
@@ -206,6 +207,7 @@ int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_
     cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, dev);
     s->reserved_sms = 0;
     s->gemm_pairs = 1;  // measured faster at C4: bf16 1.28 -> 1.20 ms, FP8 0.81 -> 0.78 ms
+    s->quant_one_launch = 1;
     s->err = errw;
     *out = s;
     return SPL_SAGE_OK;
@@ -222,6 +224,12 @@ int spl_sage_reserve_sms(spl_sage* s, int n) {
 int spl_sage_gemm_pairs(spl_sage* s, int on) {
     if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_gemm_pairs: NULL engine");
     s->gemm_pairs = on ? 1 : 0;
+    return SPL_SAGE_OK;
+}
+
+int spl_sage_quant_one_launch(spl_sage* s, int on) {
+    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quant_one_launch: NULL engine");
+    s->quant_one_launch = on ? 1 : 0;
     return SPL_SAGE_OK;
 }
 
@@ -301,7 +309,8 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     const size_t n_k8 = up(B * G * tk_pad * D), n_ks = up(B * G * (tk_pad / KBLOCK) * 4);
     const size_t n_v8 = up(B * G * tk_pad * D), n_st = up(B * G * 4 * D * 4);
     const size_t n_kb = up(tk_pad * 4), n_part = up(B * G * q_tiles * 4 * D * 4), n_err = 256;
-    const size_t total = n_q8 + n_qs + n_k8 + n_ks + n_v8 + n_st + n_kb + n_part + n_err;
+    const size_t n_ctl = up((2 + 2 * B * G) * 4);
+    const size_t total = n_q8 + n_qs + n_k8 + n_ks + n_v8 + n_st + n_kb + n_part + n_err + n_ctl;
 
     int dev = 0;
     cudaGetDevice(&dev);
@@ -335,7 +344,8 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     ws->buf.stats = (float*)p; p += n_st;
     ws->buf.kbias = (float*)p; p += n_kb;
     ws->buf.part = (float*)p; p += n_part;
-    ws->buf.err = (uint32_t*)p;
+    ws->buf.err = (uint32_t*)p; p += n_err;
+    ws->buf.ctl = (uint32_t*)p;
 
     const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     int rc = make_map(&ws->maps.q, ws->buf.q8, D, tq_pad, B * H, D, tq_pad * D, (uint32_t)D, 128, swz);
@@ -463,7 +473,9 @@ int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_t
     const float* ln = nullptr;
     int rc = build_geom(s, ws, q, k, v, opts, &g, &ln);
     if (rc) return rc;
-    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, g, s->stream);
+    sp::Buffers buf = ws->buf;
+    if (!s->quant_one_launch) buf.ctl = nullptr;
+    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, buf, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = g;
     ws->prepared = true;
@@ -814,7 +826,9 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     cudaError_t e = sp::launch_qkv_gemm_2sm(s->head_dim, false, maps, (const uint16_t*)bias, rope, nullptr, nullptr,
                                             (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
-    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, ws->buf, ag, s->stream);
+    sp::Buffers buf = ws->buf;
+    if (!s->quant_one_launch) buf.ctl = nullptr;
+    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, buf, ag, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = ag;
     ws->prepared = true;

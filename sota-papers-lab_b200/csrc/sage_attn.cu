@@ -55,6 +55,9 @@ constexpr int VST = 3;   // V ring depth
 #define SP_EXP_POLY 4
 #endif
 constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
+#ifndef SP_EXP_F16
+#define SP_EXP_F16 0
+#endif
 constexpr int NTHREADS = 384;
 // One service thread per SM sub-partition (warp % 4), so that no pair of
 // softmax warps carries more issue load than another: K loads (and Q),
@@ -466,6 +469,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
             const uint64_t sc2 = pk2(MERGE ? 1.0f : sc, MERGE ? 1.0f : sc), off2 = pk2(off, off);
             uint64_t sum2a = pk2(0.f, 0.f), sum2b = sum2a;
+#if SP_EXP_F16
+            uint32_t hsum = 0;
+#pragma unroll
+            for (int c16 = 0; c16 < 4; c16++) {
+                uint32_t h[8];
+#pragma unroll
+                for (int e = 0; e < 16; e += 2) {
+                    float y0, y1;
+                    upk2(fma2(pk2(x[c16 * 16 + e], x[c16 * 16 + e + 1]), sc2, off2), y0, y1);
+                    h[e >> 1] = ex2_h2(h2_of(y0, y1));
+                }
+                const uint32_t t = hadd2_u(hadd2_u(hadd2_u(h[0], h[1]), hadd2_u(h[2], h[3])),
+                                           hadd2_u(hadd2_u(h[4], h[5]), hadd2_u(h[6], h[7])));
+                hsum = c16 == 0 ? t : hadd2_u(hsum, t);
+                uint32_t w[4];
+#pragma unroll
+                for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4_h(h[2 * q4], h[2 * q4 + 1]);
+                if (c16 == 1 && j >= 1) pv_ready = mbar_try(bar(bars.p_free[(J - 1) & 1]), ((J - 1) >> 1) & 1);
+                const int chunk = half * 4 + c16;
+                const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
+                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                             "r"(w[3])
+                             : "memory");
+            }
+            l = fmaf(l, alpha, h2_sum(hsum));
+            (void)sum2a;
+            (void)sum2b;
+#else
 #pragma unroll
             for (int c16 = 0; c16 < 4; c16++) {
                 float p[16];
@@ -499,6 +530,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             upk2(sum2a, s0, s1);
             upk2(sum2b, s2, s3);
             l = fmaf(l, alpha, (s0 + s1) + (s2 + s3));
+#endif
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();

@@ -61,6 +61,11 @@ struct Buffers {
     float* kbias;
     float* part;
     uint32_t* err;
+    // control words of the one-launch quantiser (sp_prep_all): a work
+    // ticket, a finished-CTA count, then per (batch, kv head) the finished
+    // statistics tiles and a ready flag; all zero between launches (the last
+    // CTA of every launch clears them).  nullptr: the three-launch path.
+    uint32_t* ctl;
 };
 
 // TMA descriptors for the attention kernel (built once per workspace).

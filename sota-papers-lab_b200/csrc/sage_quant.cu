@@ -225,9 +225,62 @@ __global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q
         prep_stats<D>(k, v, ln, part, g, tile, y - nq, b);
 }
 
+// One statistic of one channel over a (batch, kv head)'s tile partials
+// (p = the first tile's value, tiles 4 * D floats apart): the tiles summed
+// (or min / max-ed) in order as two interleaved accumulators, 16 tiles'
+// values loaded before they are combined so that the loads' latency is paid
+// once per 16 tiles.  Loads bypass L1: in the one-launch quantiser other CTAs
+// of the same launch wrote the partials.
+template <int D>
+__device__ __forceinline__ float fin_reduce(const float* p, int stat, int q_tiles) {
+    float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
+    float r1 = r0;
+    auto acc2 = [&](float x0, float x1) {
+        if (stat < 2) {
+            r0 += x0;
+            r1 += x1;
+        } else if (stat == 2) {
+            r0 = fminf(r0, x0);
+            r1 = fminf(r1, x1);
+        } else {
+            r0 = fmaxf(r0, x0);
+            r1 = fmaxf(r1, x1);
+        }
+    };
+    int t = 0;
+    for (; t + 16 <= q_tiles; t += 16) {
+        float x[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = __ldcg(p + (long long)(t + i) * 4 * D);
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) acc2(x[i], x[i + 1]);
+    }
+    for (; t + 1 < q_tiles; t += 2) acc2(__ldcg(p + (long long)t * 4 * D), __ldcg(p + (long long)(t + 1) * 4 * D));
+    if (t < q_tiles) {
+        const float x0 = __ldcg(p + (long long)t * 4 * D);
+        r0 = stat < 2 ? r0 + x0 : (stat == 2 ? fminf(r0, x0) : fmaxf(r0, x0));
+    }
+    return stat < 2 ? r0 + r1 : (stat == 2 ? fminf(r0, r1) : fmaxf(r0, r1));
+}
+
+// Channel d's K mean, V mean, V scale and its reciprocal from its four
+// reduced statistics (K sum, V sum, V min, V max).
+template <int D>
+__device__ __forceinline__ void fin_store(float* o, int d, float ksum, float vsum, float vmin, float vmax,
+                                          const Geom& g) {
+    const float n = (float)g.tokens;
+    const float mk = (g.flags & SMOOTH_K) ? ksum / n : 0.f;
+    const float mv = (g.flags & SMOOTH_V) ? vsum / n : 0.f;
+    const float amax = fmaxf(vmax - mv, mv - vmin);
+    const float scale = amax > 0.f ? amax / g.v_range : 1.0f;
+    o[d] = mk;
+    o[D + d] = mv;
+    o[2 * D + d] = scale;
+    o[3 * D + d] = 1.0f / scale;
+}
+
 // Per (kv head, batch, 32 channels): K mean, V mean, V scale and its
-// reciprocal from the tile partials, the tiles summed as two interleaved
-// accumulators.  128 threads: (statistic, channel).
+// reciprocal from the tile partials.  128 threads: (statistic, channel).
 template <int D>
 __global__ void __launch_bounds__(128) sp_finalize(const float* __restrict__ part, float* __restrict__ stats,
                                                    const Geom g) {
@@ -235,52 +288,9 @@ __global__ void __launch_bounds__(128) sp_finalize(const float* __restrict__ par
     const long long bh = (long long)b * g.kv_heads + h;
     const int stat = tid >> 5, d = blockIdx.z * 32 + (tid & 31);
     __shared__ float st[4][32];
-    {
-        const float* p = part + bh * g.q_tiles * 4 * D + stat * D + d;
-        float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
-        float r1 = r0;
-        auto acc2 = [&](float x0, float x1) {
-            if (stat < 2) {
-                r0 += x0;
-                r1 += x1;
-            } else if (stat == 2) {
-                r0 = fminf(r0, x0);
-                r1 = fminf(r1, x1);
-            } else {
-                r0 = fmaxf(r0, x0);
-                r1 = fmaxf(r1, x1);
-            }
-        };
-        int t = 0;
-        // 16 tiles' partials loaded before they are added (in tile order), so
-        // that the loads' latency is paid once per 16 tiles, not per tile
-        for (; t + 16 <= g.q_tiles; t += 16) {
-            float x[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) x[i] = p[(long long)(t + i) * 4 * D];
-#pragma unroll
-            for (int i = 0; i < 16; i += 2) acc2(x[i], x[i + 1]);
-        }
-        for (; t + 1 < g.q_tiles; t += 2) acc2(p[(long long)t * 4 * D], p[(long long)(t + 1) * 4 * D]);
-        if (t < g.q_tiles) {
-            const float x0 = p[(long long)t * 4 * D];
-            r0 = stat < 2 ? r0 + x0 : (stat == 2 ? fminf(r0, x0) : fmaxf(r0, x0));
-        }
-        st[stat][tid & 31] = stat < 2 ? r0 + r1 : (stat == 2 ? fminf(r0, r1) : fmaxf(r0, r1));
-    }
+    st[stat][tid & 31] = fin_reduce<D>(part + bh * g.q_tiles * 4 * D + stat * D + d, stat, g.q_tiles);
     __syncthreads();
-    if (tid < 32) {
-        const float n = (float)g.tokens;
-        const float mk = (g.flags & SMOOTH_K) ? st[0][tid] / n : 0.f;
-        const float mv = (g.flags & SMOOTH_V) ? st[1][tid] / n : 0.f;
-        const float amax = fmaxf(st[3][tid] - mv, mv - st[2][tid]);
-        const float scale = amax > 0.f ? amax / g.v_range : 1.0f;
-        float* o = stats + bh * 4 * D;
-        o[d] = mk;
-        o[D + d] = mv;
-        o[2 * D + d] = scale;
-        o[3 * D + d] = 1.0f / scale;
-    }
+    if (tid < 32) fin_store<D>(stats + bh * 4 * D, d, st[0][tid], st[1][tid], st[2][tid], st[3][tid], g);
 }
 
 // Members of merged key j within one batch item: the count, the first token
@@ -318,13 +328,12 @@ __device__ __forceinline__ int members(const Geom& g, int j, int& base, int& nx)
 // with one scale per block; V -> (v - mean) / scale -> E4M3, written
 // channel-major ([D][tk_pad]) through a shared-memory transpose.
 template <int D>
-__global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
-                                                   const float* __restrict__ ln, const float* __restrict__ stats,
-                                                   int8_t* __restrict__ k8, float* __restrict__ k_scale,
-                                                   uint8_t* __restrict__ v8, float* __restrict__ kbias,
-                                                   const Geom g) {
+__device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                               const float* __restrict__ ln, const float* __restrict__ stats,
+                                               int8_t* __restrict__ k8, float* __restrict__ k_scale,
+                                               uint8_t* __restrict__ v8, float* __restrict__ kbias, const Geom& g,
+                                               int blk, int h, int b) {
     constexpr int CH = D / 8, TPI = 256 / CH, NI = KBLOCK / TPI;
-    const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
     const long long bh = (long long)b * g.kv_heads + h;
     const int nblk = g.tk_pad / KBLOCK;
@@ -335,7 +344,18 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
     if (tid == 0) kmax = 0u;
     __syncthreads();
 
-    const float* st = stats + bh * 4 * D;
+    // this thread's channels' K mean, V mean and V 1/scale (read past L1:
+    // in the one-launch quantiser another CTA of the launch wrote them)
+    float mk[8], mv[8], rv[8];
+    {
+        const float* st = stats + bh * 4 * D + ch * 8;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            mk[e] = __ldcg(st + e);
+            mv[e] = __ldcg(st + D + e);
+            rv[e] = __ldcg(st + 3 * D + e);
+        }
+    }
     if (NI == 4 && g.merge == 1 && !(g.flags & LN_K)) {
         // Dense keys, D = 128: thread (m, ch) takes the 4 consecutive keys
         // 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7, so that each channel's
@@ -365,10 +385,9 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
             float vq[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                const int d = ch * 8 + e;
-                kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -st[d]) : 0.f;
+                kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
                 amx = fmaxf(amx, fabsf(kq[i][e]));
-                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -st[D + d]) * st[3 * D + d] : 0.f;
+                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
             }
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
@@ -423,11 +442,10 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
             unpack_bf16x8(vr[i], fv);
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                const int d = ch * 8 + e;
                 // 0 + x: the member sum of the general path (it maps -0 to +0)
-                kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -st[d]) : 0.f;
+                kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
                 amax = fmaxf(amax, fabsf(kv[i][e]));
-                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -st[D + d]) * st[3 * D + d] : 0.f;
+                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
             }
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
@@ -466,12 +484,11 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
         float vq[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            const int d = ch * 8 + e;
             // fmaf: the contraction nvcc applies to the reference's
             // `ksum * rc - mean` and `(vsum * rc - mv) * inv`.
-            kv[i][e] = ok ? fmaf(ksum[e], rc, -st[d]) : 0.f;
+            kv[i][e] = ok ? fmaf(ksum[e], rc, -mk[e]) : 0.f;
             amax = fmaxf(amax, fabsf(kv[i][e]));
-            vq[e] = ok ? fmaf(vsum[e], rc, -st[D + d]) * st[3 * D + d] : 0.f;
+            vq[e] = ok ? fmaf(vsum[e], rc, -mv[e]) * rv[e] : 0.f;
         }
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
@@ -510,6 +527,145 @@ __global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ 
     }
 }
 
+template <int D>
+__global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                                   const float* __restrict__ ln, const float* __restrict__ stats,
+                                                   int8_t* __restrict__ k8, float* __restrict__ k_scale,
+                                                   uint8_t* __restrict__ v8, float* __restrict__ kbias,
+                                                   const Geom g) {
+    quant_kv_block<D>(k, v, ln, stats, k8, k_scale, v8, kbias, g, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
+// ---------------------------------------------------------------- one launch
+// The three passes above as one persistent launch, so that each (batch, kv
+// head)'s K and V (2 MB at D = 128, N = 8192) are read for quantisation
+// while their statistics pass has left them in L2, instead of after all of
+// Q has streamed through it.  Work items, taken in order from a ticket
+// counter, are laid out in rounds r = 0 .. slices + lag - 1 of equal width:
+//   [ statistics tiles of slice r | a share of the Q tiles | K/V blocks of slice r - lag ]
+// (slice = one (batch, kv head); out-of-range items are empty).  The CTA that
+// finishes a slice's last statistics tile reduces the slice's partials (the
+// same tree as sp_finalize) and sets the slice's ready flag; a K/V block
+// waits for that flag.  The wait cannot deadlock: a flag waits only on
+// items taken earlier, and those are held by running CTAs that never wait
+// on statistics.  The wait is bounded (ERR_TIMEOUT, site 60).  Every value
+// is computed by the same device functions, in the same order, as the
+// three-launch path, so the bytes are the same.
+struct PrepSchedule {
+    int slices;   // batch * kv_heads
+    int ns;       // statistics tiles per slice (q_tiles)
+    int nq;       // Q tiles per round
+    int nk;       // K/V blocks per slice (tk_pad / 64)
+    int lag;      // rounds between a slice's statistics and its K/V blocks
+    int q_total;  // Q tiles in all (0: no Q role)
+    int width;    // items per round
+    int total;    // items in all
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(256, 2) sp_prep_all(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                                                   const uint16_t* __restrict__ v, const float* __restrict__ ln,
+                                                   const Buffers buf, const Geom g, const PrepSchedule ps) {
+    const int tid = threadIdx.x;
+    uint32_t* ticket = buf.ctl;
+    uint32_t* done = buf.ctl + 1;
+    uint32_t* tiles_done = buf.ctl + 2;
+    uint32_t* ready = buf.ctl + 2 + ps.slices;
+    __shared__ int s_item;
+    __shared__ int s_flag;
+    __shared__ float s_red[4][D];
+    if (tid == 0) s_item = (int)atomicAdd(ticket, 1u);
+    __syncthreads();
+    int item = s_item;
+    while (item < ps.total) {
+        int next = 0;
+        if (tid == 0) next = (int)atomicAdd(ticket, 1u);  // in flight during this item
+        const int r = item / ps.width, o = item % ps.width;
+        if (o < ps.ns) {
+            // statistics tile o of slice r
+            if (r < ps.slices) {
+                const int h = r % g.kv_heads, b = r / g.kv_heads;
+                prep_stats<D>(k, v, ln, buf.part, g, o, h, b);
+                __threadfence();
+                __syncthreads();
+                if (tid == 0) s_flag = atomicAdd(tiles_done + r, 1u) == (uint32_t)(ps.ns - 1);
+                __syncthreads();
+                if (s_flag) {
+                    // the slice's last tile: reduce its partials as sp_finalize does
+                    __threadfence();
+                    const long long bh = (long long)b * g.kv_heads + h;
+                    for (int c = tid; c < 4 * D; c += 256) {
+                        const int stat = c / D, d = c % D;
+                        s_red[stat][d] = fin_reduce<D>(buf.part + bh * g.q_tiles * 4 * D + stat * D + d, stat, g.q_tiles);
+                    }
+                    __syncthreads();
+                    for (int d = tid; d < D; d += 256)
+                        fin_store<D>(buf.stats + bh * 4 * D, d, s_red[0][d], s_red[1][d], s_red[2][d], s_red[3][d], g);
+                    __threadfence();
+                    __syncthreads();
+                    if (tid == 0) st_release_gpu(ready + r, 1u);
+                }
+            }
+        } else if (o < ps.ns + ps.nq) {
+            // a Q tile
+            const int qi = r * ps.nq + (o - ps.ns);
+            if (qi < ps.q_total) {
+                const int tile = qi % g.q_tiles, rest = qi / g.q_tiles;
+                prep_q<D>(q, ln, buf.q8, buf.q_scale, g, tile, rest % g.heads, rest / g.heads);
+            }
+        } else {
+            // K/V block of slice r - lag, once its statistics are ready
+            const int sl = r - ps.lag, blk = o - ps.ns - ps.nq;
+            if (sl >= 0 && sl < ps.slices) {
+                if (tid == 0) {
+                    int ok = 1;
+                    if (ld_acquire_gpu(ready + sl) == 0u) {
+                        const unsigned long long t0 = globaltimer();
+                        for (uint32_t i = 1;; ++i) {
+                            __nanosleep(128);
+                            if (ld_acquire_gpu(ready + sl) != 0u) break;
+                            if ((i & 63u) == 0 &&
+                                (globaltimer() - t0 > WAIT_LIMIT_NS || i >= WAIT_MAX_TRIES || ld_volatile(buf.err) != 0)) {
+                                atomicOr(buf.err, ERR_TIMEOUT | (60u << ERR_SITE_SHIFT));
+                                ok = 0;
+                                break;
+                            }
+                        }
+                    }
+                    s_flag = ok;
+                }
+                __syncthreads();
+                if (s_flag)
+                    quant_kv_block<D>(k, v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g, blk,
+                                      sl % g.kv_heads, sl / g.kv_heads);
+            }
+        }
+        __syncthreads();  // this item's shared memory is free
+        if (tid == 0) s_item = next;
+        __syncthreads();
+        item = s_item;
+    }
+    // the last CTA out clears the control words for the next launch
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            for (int i = 0; i < 2 * ps.slices; i++) tiles_done[i] = 0u;
+            *ticket = 0u;
+            *done = 0u;
+            __threadfence();
+        }
+    }
+}
+
 // The reference's V layout for the bit gate: [b][g][tk_pad/64][D][64], keys
 // permuted within each 16 by vpos (sage_common.cu:151-155).
 __device__ __forceinline__ int vpos(int k) { return ((k >> 1) & 3) * 4 + ((k >> 3) << 1) + (k & 1); }
@@ -529,10 +685,47 @@ __global__ void __launch_bounds__(256) sp_export_v(const uint8_t* __restrict__ v
     }
 }
 
+// Persistent CTAs of sp_prep_all: as many as fit on the GPU at once.
+template <int D>
+static int prep_all_ctas() {
+    static int n[2] = {0, 0};
+    static std::once_flag once;
+    std::call_once(once, [] {
+        int dev = 0, sms = 0, per = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, sp_prep_all<D>, 256, 0);
+        n[0] = sms * (per > 0 ? per : 1);
+    });
+    return n[0];
+}
+
 template <int D>
 static cudaError_t prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                              const Geom& g, cudaStream_t st) {
     const int q_role = q != nullptr;
+    if (buf.ctl) {
+        PrepSchedule ps;
+        ps.slices = g.batch * g.kv_heads;
+        ps.ns = g.q_tiles;
+        ps.nk = g.tk_pad / KBLOCK;
+        ps.q_total = q_role ? g.batch * g.heads * g.q_tiles : 0;
+        const int ctas = prep_all_ctas<D>();
+        // lag: enough rounds that a slice's statistics tiles were all taken
+        // by the time its first K/V block is, with two grids of items between
+        ps.lag = 1;
+        for (;;) {
+            const int rounds = ps.slices + ps.lag;
+            ps.nq = (ps.q_total + rounds - 1) / rounds;
+            ps.width = ps.ns + ps.nq + ps.nk;
+            if (ps.lag >= ps.slices || (long long)ps.lag * ps.width + ps.nq >= 2LL * ctas) break;
+            ps.lag++;
+        }
+        ps.total = (ps.slices + ps.lag) * ps.width;
+        sp_prep_all<D><<<ctas, 256, 0, st>>>((const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf, g,
+                                             ps);
+        return cudaGetLastError();
+    }
     sp_prep<D><<<dim3(g.q_tiles, (q_role ? g.heads : 0) + g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g, q_role);
     sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
