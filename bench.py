@@ -321,7 +321,7 @@ def run_layers(args, rank, world, local_rank):
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
                 "api": "qkv_gemm_quant + attend via libsplsage C ABI, 24 layers per step, pinned host buffers"},
-        "gpu_launches": 5 * Lr * args.steps,
+        "gpu_launches": 3 * Lr * args.steps,  # per layer: GEMM, one-launch K/V quantiser, attention
         "clocks": clk.summary(),
         "device_error_word": word,
     }
@@ -660,7 +660,7 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": d2h,
                 "api": "SageAttention.forward via libsplsage C ABI, pinned host buffers; uploads, compute and "
                        "downloads of consecutive steps overlapped on three streams (every rank its own share)"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 2 * args.steps,  # per step: the one-launch quantiser, the attention
         "clocks": clk.summary(),
         "device_error_word": word,
     }
@@ -747,7 +747,7 @@ def c4_block_time(eng, wr, B, dev, stream, rank, world, max_over_ranks, iters=5)
             "tflops_gemm_plus_attention": round((gemm_flops + attn_flops) / (t_block * 1e-3) / 1e12, 1),
             "gemm_quant_ms": round(t_fused, 4), "unfused_gemm_then_quantiser_ms": round(t_unfused, 4),
             "q_round_trip_bytes_removed": B * N * full["heads"] * D * 2 // world * 2,
-            "gpu_launches_per_block": 5, "device_error_word": word}
+            "gpu_launches_per_block": 3, "device_error_word": word}
 
 
 def qkv_gemm_time(eng, w, dev, stream, iters=10):
