@@ -79,7 +79,7 @@ def lib():
         L.or_attention_bthd.argtypes = [P, P, P, ctypes.POINTER(Geom), ctypes.c_float, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
         L.or_sage_emulate.argtypes = [P] * 7 + [ctypes.POINTER(Geom)] + [ctypes.c_int] * 4 + [P]
-        L.or_sage_online.argtypes = [P] * 7 + [ctypes.POINTER(Geom)] + [ctypes.c_int] * 6 + [P]
+        L.or_sage_online.argtypes = [P] * 7 + [ctypes.POINTER(Geom)] + [ctypes.c_int] * 5 + [P]
         L.or_layer_norm.argtypes = [P, P, P, ctypes.c_int, ctypes.c_float]
         L.or_qkv_reference.argtypes = [P, P, P, P] + [ctypes.c_int] * 10 + [P, P, P]
         L.or_qkv_reference_fp8.argtypes = [P] * 6 + [ctypes.c_int] * 10 + [P, P, P]
@@ -303,17 +303,14 @@ REF_BLOCK = 64   # keys per online-softmax block in the reference kernel (sage_a
 OUR_BLOCK = 128  # ... in this library's kernel
 
 
-def sage_online(qt: Quant, g: Geom, *, block=REF_BLOCK, causal=False, rows=None, nthreads=None,
-                exp16=False) -> np.ndarray:
+def sage_online(qt: Quant, g: Geom, *, block=REF_BLOCK, causal=False, rows=None, nthreads=None) -> np.ndarray:
     """The kernels' online softmax, block by block (or_sage_online): block
     64 restates the reference kernel's arithmetic (extended with the causal
-    mask and GQA), 128 this library's.  exp16: the exponent and the
-    probability rounded to f16 (the packed-f16 exponential).  Only `rows` of
-    every (b, h)."""
+    mask and GQA), 128 this library's.  Only `rows` of every (b, h)."""
     out = np.zeros((g.batch, g.tokens, g.heads, g.d), np.float32)
     r0, r1 = rows if rows is not None else (0, g.tokens)
     lib().or_sage_online(_p(qt.q8), _p(qt.q_scale), _p(qt.k8), _p(qt.k_scale), _p(qt.v8), _p(qt.stats),
-                         _p(qt.kbias), ctypes.byref(g), int(causal), int(block), int(exp16), r0, r1,
+                         _p(qt.kbias), ctypes.byref(g), int(causal), int(block), r0, r1,
                          nthreads or os.cpu_count() or 1, _p(out))
     return out
 

@@ -723,14 +723,11 @@ typedef struct {
     const float* stats;
     const float* kbias;
     const or_geom* g;
-    int causal, block, row0, row1, exp16;
+    int causal, block, row0, row1;
     float* out;
     int64_t next;
     pthread_mutex_t mu;
 } onl_job;
-
-/* x rounded to the nearest f16 (ties to even), as a float. */
-static float or_round_f16(float x) { return (float)(_Float16)x; }
 
 static void* onl_worker(void* arg) {
     onl_job* J = (onl_job*)arg;
@@ -791,16 +788,13 @@ static void* onl_worker(void* arg) {
                 for (int t = 0; t < B; t++) {
                     const int j = k0 + t;
                     if (j >= nk) continue;
-                    float y, p;
+                    float p;
                     if (merge) {
-                        y = xf[t] + (L448 - mnew);
+                        p = exp2f(xf[t] + (L448 - mnew));
                     } else {
                         const float sc = qs * J->k_scale[kvh * nkb + j / OR_KBLOCK];
-                        y = fmaf(xf[t], sc, (L448 - mnew) + (-(M * sc)));
+                        p = exp2f(fmaf(xf[t], sc, (L448 - mnew) + (-(M * sc))));
                     }
-                    /* exp16: the exponent and the probability in f16, as the
-                     * kernel's packed ex2.approx.f16x2 computes them */
-                    p = J->exp16 ? or_round_f16(exp2f(or_round_f16(y))) : exp2f(y);
                     sum += p;
                     const double p8 = (double)or_e4m3_to_f32(or_f32_to_e4m3(p));
                     if (p8 != 0.0)
@@ -823,9 +817,8 @@ static void* onl_worker(void* arg) {
 
 void or_sage_online(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
                     const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
-                    int block, int exp16, int row0, int row1, int nthreads, float* out) {
+                    int block, int row0, int row1, int nthreads, float* out) {
     onl_job J;
-    J.exp16 = exp16;
     J.q8 = q8;
     J.q_scale = q_scale;
     J.k8 = k8;

@@ -137,7 +137,7 @@ void or_sage_emulate(const int8_t* q8, const float* q_scale, const int8_t* k8, c
  * ex2.approx, each block's PV rounded once). */
 void or_sage_online(const int8_t* q8, const float* q_scale, const int8_t* k8, const float* k_scale,
                     const uint8_t* v8, const float* stats, const float* kbias, const or_geom* g, int causal,
-                    int block, int exp16, int row0, int row1, int nthreads, float* out);
+                    int block, int row0, int row1, int nthreads, float* out);
 
 /* The QKV path of one block in f64: y = x w^T + bias (host::linear,
  * platform/spl-nn/src/host.rs) then the QKV prologue (qkv::reference,

@@ -98,6 +98,33 @@ int make_map_bf16_2d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1,
 
 bool fits_i32(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
 
+// The one-launch quantiser's input maps: Q (when given), K, V as bf16
+// {D, heads, tokens, batch} with the tensors' own strides, box {D, 1, 64, 1},
+// zero fill past the last token.  false when TMA cannot address a tensor
+// (base or a stride not a multiple of 16 bytes); the three launches run then.
+bool prep_maps(sp::PrepMaps* pm, int64_t D, const sp::Geom& g, const void* q, const void* k, const void* v) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    memset(pm, 0, sizeof *pm);
+    auto one = [&](CUtensorMap* m, const void* base, int64_t heads, int64_t sb, int64_t st, int64_t sh) {
+        if ((uintptr_t)base % 16) return false;
+        // a dimension of extent 1 is never stepped over: any valid pitch will do
+        const int64_t pb = g.batch > 1 ? sb * 2 : ((int64_t)g.tokens * st * 2 + 15) / 16 * 16;
+        const int64_t ph = heads > 1 ? sh * 2 : D * 2;
+        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)g.tokens, (cuuint64_t)g.batch};
+        cuuint64_t strides[3] = {(cuuint64_t)ph, (cuuint64_t)(st * 2), (cuuint64_t)pb};
+        for (cuuint64_t x : strides)
+            if (x == 0 || x % 16) return false;
+        cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
+        cuuint32_t elem[4] = {1, 1, 1, 1};
+        return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    if (q && !one(&pm->q, q, g.heads, g.q_sb, g.q_st, g.q_sh)) return false;
+    return one(&pm->k, k, g.kv_heads, g.k_sb, g.k_st, g.k_sh) && one(&pm->v, v, g.kv_heads, g.v_sb, g.v_st, g.v_sh);
+}
+
 }  // namespace
 
 struct spl_sage {
@@ -473,9 +500,10 @@ int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_t
     const float* ln = nullptr;
     int rc = build_geom(s, ws, q, k, v, opts, &g, &ln);
     if (rc) return rc;
-    sp::Buffers buf = ws->buf;
-    if (!s->quant_one_launch) buf.ctl = nullptr;
-    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, buf, g, s->stream);
+    sp::PrepMaps pm;
+    const bool one = s->quant_one_launch && prep_maps(&pm, s->head_dim, g, q.data, k.data, v.data);
+    cudaError_t e =
+        sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, one ? &pm : nullptr, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = g;
     ws->prepared = true;
@@ -826,9 +854,9 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     cudaError_t e = sp::launch_qkv_gemm_2sm(s->head_dim, false, maps, (const uint16_t*)bias, rope, nullptr, nullptr,
                                             (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
-    sp::Buffers buf = ws->buf;
-    if (!s->quant_one_launch) buf.ctl = nullptr;
-    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, buf, ag, s->stream);
+    sp::PrepMaps pm;
+    const bool one = s->quant_one_launch && prep_maps(&pm, s->head_dim, ag, nullptr, k, v);
+    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, ws->buf, one ? &pm : nullptr, ag, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = ag;
     ws->prepared = true;
@@ -919,7 +947,7 @@ int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const sp
     buf.stats = stats;
     buf.kbias = nullptr;  // dense keys: the quantiser never writes kbias
     buf.part = part;      // fully rewritten by every call before it is read
-    e = sp::launch_prepare(head_dim, q.data, k.data, v.data, o.qk_norm_params, buf, g, (cudaStream_t)stream);
+    e = sp::launch_prepare(head_dim, q.data, k.data, v.data, o.qk_norm_params, buf, nullptr, g, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage quantiser");
     return SPL_SAGE_OK;
 }

@@ -55,12 +55,6 @@ constexpr int VST = 3;   // V ring depth
 #define SP_EXP_POLY 4
 #endif
 constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
-#ifndef SP_EXP_F16
-#define SP_EXP_F16 0
-#endif
-#ifndef SP_FOLD_SPLIT
-#define SP_FOLD_SPLIT 0
-#endif
 constexpr int NTHREADS = 384;
 // One service thread per SM sub-partition (warp % 4), so that no pair of
 // softmax warps carries more issue load than another: K loads (and Q),
@@ -393,12 +387,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // needed, so that its latency stays off the softmax warps' path):
         // pv_ready for the fold's PV, s_ready for the next block's S.
         bool pv_ready = false, s_ready = false;
-        // SP_FOLD_SPLIT: the second softmax warp of each SM sub-partition
-        // folds the previous block's PV after its second exponential chunk
-        // instead of after the P arrival, so that the two warps' low-ILP
-        // phases (row maximum, fold) fall at different times
-        const bool late_fold = SP_FOLD_SPLIT && sub == 1;
-        bool fold_ok = true;
         auto correct = [&](int jj, float a) -> bool {
             const int pb = jj & 1;
             if (!__all_sync(0xffffffffu, pv_ready) && !warp_wait(bar(bars.p_free[pb]), (jj >> 1) & 1, err, 31))
@@ -478,36 +466,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const float off = MERGE ? LOG2_448 - mnew : LOG2_448 - mnew - MAGIC_F * sc;
             const uint64_t sc2 = pk2(MERGE ? 1.0f : sc, MERGE ? 1.0f : sc), off2 = pk2(off, off);
             uint64_t sum2a = pk2(0.f, 0.f), sum2b = sum2a;
-#if SP_EXP_F16
-            uint32_t hsum = 0;
-#pragma unroll
-            for (int c16 = 0; c16 < 4; c16++) {
-                uint32_t h[8];
-#pragma unroll
-                for (int e = 0; e < 16; e += 2) {
-                    float y0, y1;
-                    upk2(fma2(pk2(x[c16 * 16 + e], x[c16 * 16 + e + 1]), sc2, off2), y0, y1);
-                    h[e >> 1] = ex2_h2(h2_of(y0, y1));
-                }
-                const uint32_t t = hadd2_u(hadd2_u(hadd2_u(h[0], h[1]), hadd2_u(h[2], h[3])),
-                                           hadd2_u(hadd2_u(h[4], h[5]), hadd2_u(h[6], h[7])));
-                hsum = c16 == 0 ? t : hadd2_u(hsum, t);
-                uint32_t w[4];
-#pragma unroll
-                for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4_h(h[2 * q4], h[2 * q4 + 1]);
-                if (c16 == (late_fold ? 0 : 1) && j >= 1)
-                    pv_ready = mbar_try(bar(bars.p_free[(J - 1) & 1]), ((J - 1) >> 1) & 1);
-                const int chunk = half * 4 + c16;
-                const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
-                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                             "r"(w[3])
-                             : "memory");
-                if (late_fold && c16 == 1 && j >= 1 && fold_ok) fold_ok = correct(J - 1, alpha_prev);
-            }
-            l = fmaf(l, alpha, h2_sum(hsum));
-            (void)sum2a;
-            (void)sum2b;
-#else
 #pragma unroll
             for (int c16 = 0; c16 < 4; c16++) {
                 float p[16];
@@ -530,20 +488,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int q4 = 0; q4 < 4; q4++) w[q4] = e4m3x4(p[4 * q4], p[4 * q4 + 1], p[4 * q4 + 2], p[4 * q4 + 3]);
                 // the fold's PV (block J - 1) is usually done by now
-                if (c16 == (late_fold ? 0 : 1) && j >= 1)
-                    pv_ready = mbar_try(bar(bars.p_free[(J - 1) & 1]), ((J - 1) >> 1) & 1);
+                if (c16 == 1 && j >= 1) pv_ready = mbar_try(bar(bars.p_free[(J - 1) & 1]), ((J - 1) >> 1) & 1);
                 const int chunk = half * 4 + c16;
                 const uint32_t a = prow_addr + (uint32_t)(((chunk ^ (r & 7)) & 7) << 4);
                 asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[0]), "r"(w[1]), "r"(w[2]),
                              "r"(w[3])
                              : "memory");
-                if (late_fold && c16 == 1 && j >= 1 && fold_ok) fold_ok = correct(J - 1, alpha_prev);
             }
             float s0, s1, s2, s3;
             upk2(sum2a, s0, s1);
             upk2(sum2b, s2, s3);
             l = fmaf(l, alpha, (s0 + s1) + (s2 + s3));
-#endif
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
@@ -551,7 +506,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // the next block's S is usually finished during this block
             if (j + 1 < nb) s_ready = mbar_try(bar(bars.s_full[(J + 1) & 1]), ((J + 1) >> 1) & 1);
             // fold the previous block's PV into O while this block's PV runs
-            if (!fold_ok || (!late_fold && j >= 1 && !correct(J - 1, alpha_prev))) {
+            if (j >= 1 && !correct(J - 1, alpha_prev)) {
                 ok = false;
                 break;
             }

@@ -82,49 +82,6 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// ---------------------------------------------------------------- packed f16x2
-
-// Two floats -> f16x2 (RNE), lo in the low half.
-__device__ __forceinline__ uint32_t h2_of(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-// 2^x for both halves (MUFU, one instruction for the pair).
-__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
-    uint32_t r;
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
-    return r;
-}
-__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-// Two f16x2 -> four E4M3 bytes (RNE, saturating), lo's low half in the lowest byte.
-__device__ __forceinline__ uint32_t e4m3x4_h(uint32_t lo, uint32_t hi) {
-    uint32_t r;
-    asm("{\n .reg .b16 a, b;\n"
-        " cvt.rn.satfinite.e4m3x2.f16x2 a, %1;\n"
-        " cvt.rn.satfinite.e4m3x2.f16x2 b, %2;\n"
-        " mov.b32 %0, {a, b};\n}"
-        : "=r"(r)
-        : "r"(lo), "r"(hi));
-    return r;
-}
-// The sum of both halves as a float.
-__device__ __forceinline__ float h2_sum(uint32_t h) {
-    float r;
-    asm("{\n .reg .b16 a, b;\n .reg .f32 fa, fb;\n"
-        " mov.b32 {a, b}, %1;\n"
-        " cvt.f32.f16 fa, a;\n"
-        " cvt.f32.f16 fb, b;\n"
-        " add.rn.f32 %0, fa, fb;\n}"
-        : "=f"(r)
-        : "r"(h));
-    return r;
-}
-
 // ---------------------------------------------------------------- packed f32x2 (sm_100)
 
 __device__ __forceinline__ uint64_t pk2(float a, float b) {
@@ -281,6 +238,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
         ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 

@@ -68,6 +68,13 @@ struct Buffers {
     uint32_t* ctl;
 };
 
+// TMA descriptors of the bf16 inputs of the one-launch quantiser (built per
+// call): Q, K, V as {D, heads, tokens, batch} with the caller's strides, box
+// {D, 1, 64, 1}, zero fill past the last token.
+struct PrepMaps {
+    CUtensorMap q, k, v;
+};
+
 // TMA descriptors for the attention kernel (built once per workspace).
 struct AttnMaps {
     CUtensorMap q;  // q8 as {D, tq_pad, b*h}, box {D, 128, 1}
@@ -123,10 +130,12 @@ size_t noalloc_part_capacity();
 
 // The quantiser without its Q role (Q already quantised by the QKV GEMM's
 // epilogue): K/V statistics, finalize, K/V quantisation.
+// maps (nullptr: the three launches) selects the one-launch quantiser where
+// it applies (dense keys, no QK LayerNorm, buf.ctl set).
 cudaError_t launch_prepare_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
-                              const Geom& g, cudaStream_t st);
+                              const PrepMaps* maps, const Geom& g, cudaStream_t st);
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
-                           const Geom& g, cudaStream_t st);
+                           const PrepMaps* maps, const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);
 // Context parallelism (sage_quant.cu): Q quantised and this rank's raw K/V
 // channel statistics raw [b][g][4][D] = {sum K, sum V, -min V, max V};
