@@ -139,13 +139,6 @@ int spl_sage_reserve_sms(spl_sage* s, int n);
  * 128 x 256 tile. */
 int spl_sage_gemm_pairs(spl_sage* s, int on);
 
-/* No counterpart in the reference (which launches sg_prep, sg_finalize and
- * sg_quant_kv, mod.rs:789-870).  on = 1 (default): spl_sage_prepare and
- * spl_sage_qkv_gemm_quant quantise in one persistent launch that takes each
- * (batch, kv head)'s K/V blocks while its statistics pass has left them in
- * L2; 0: the three launches.  The bytes written are the same either way. */
-int spl_sage_quant_one_launch(spl_sage* s, int on);
-
 /* SageAttention::workspace (mod.rs:649-670) via Plan::new (mod.rs:405-440):
  * allocates the quantised buffers (zeroed, on the engine's stream).  merge
  * NULL = dense.  Causal with merging is rejected. */

@@ -101,7 +101,7 @@ EXPORTS = [
     "spl_sage_quantize_noalloc", "spl_sage_kv_bytes", "spl_sage_kv_create", "spl_sage_kv_destroy",
     "spl_sage_cp_prepare", "spl_sage_cp_quantize_kv", "spl_sage_cp_attend", "spl_sage_cp_finish",
     "spl_sage_reserve_sms", "spl_sage_qkv_gemm_fp8", "spl_sage_layer_norm_fp8", "spl_sage_rows_fp8",
-    "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_quant_one_launch", "spl_sage_ring_create", "spl_sage_ring_destroy",
+    "spl_sage_linear_fp8", "spl_sage_gemm_pairs", "spl_sage_ring_create", "spl_sage_ring_destroy",
     "spl_sage_ring_forward", "spl_sage_plan_new", "spl_sage_wait_selftest", "spl_sage_ring_segment",
     "spl_sage_kv_create_gathered", "spl_sage_cp_attend_gathered", "spl_sage_ring_schedule",
 ]
@@ -131,7 +131,6 @@ def lib() -> ctypes.CDLL:
         L.spl_sage_destroy.argtypes = [P]
         L.spl_sage_reserve_sms.argtypes = [P, I]
         L.spl_sage_gemm_pairs.argtypes = [P, I]
-        L.spl_sage_quant_one_launch.argtypes = [P, I]
         L.spl_sage_ring_create.argtypes = [P, ctypes.POINTER(_Shape), I, I, I, ctypes.POINTER(P)]
         L.spl_sage_ring_destroy.argtypes = [P]
         L.spl_sage_ring_forward.argtypes = [P, P, _Tensor, _Tensor, _Tensor, _Tensor, ctypes.POINTER(_Options), P]
@@ -435,11 +434,6 @@ class SageAttention:
     def gemm_pairs(self, on: bool):
         """Run this engine's GEMMs on SM pairs (tcgen05 cta_group::2)."""
         _check(lib().spl_sage_gemm_pairs(self._h, int(on)))
-
-    def quant_one_launch(self, on: bool):
-        """The quantiser as one persistent launch (default) or as the
-        reference's three (sg_prep, sg_finalize, sg_quant_kv); same bytes."""
-        _check(lib().spl_sage_quant_one_launch(self._h, int(on)))
 
     def close(self):
         if self._h:

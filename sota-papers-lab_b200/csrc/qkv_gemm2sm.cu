@@ -366,6 +366,7 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
 #pragma unroll
                     for (int o = 1; o < 16; o <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, o));
                     const float inv = qmax > 0.f ? 127.0f / qmax : 0.f;
+                    const bool fast = s8_fast(qmax);
                     if (row < g.m) {
                         const long long bhq = (long long)bb * g.hq + head;
                         int8_t* q8row = g.q8 + (bhq * g.tq_pad + tok) * D;
@@ -375,10 +376,10 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                         for (int i = 0; i < D / 16; i++) {
                             const uint32_t* p = qp + 8 * i;
                             const uint4 w = make_uint4(
-                                s8x4(lo(p[0]) * inv, hi(p[0]) * inv, lo(p[1]) * inv, hi(p[1]) * inv),
-                                s8x4(lo(p[2]) * inv, hi(p[2]) * inv, lo(p[3]) * inv, hi(p[3]) * inv),
-                                s8x4(lo(p[4]) * inv, hi(p[4]) * inv, lo(p[5]) * inv, hi(p[5]) * inv),
-                                s8x4(lo(p[6]) * inv, hi(p[6]) * inv, lo(p[7]) * inv, hi(p[7]) * inv));
+                                s8x4(lo(p[0]) * inv, hi(p[0]) * inv, lo(p[1]) * inv, hi(p[1]) * inv, fast),
+                                s8x4(lo(p[2]) * inv, hi(p[2]) * inv, lo(p[3]) * inv, hi(p[3]) * inv, fast),
+                                s8x4(lo(p[4]) * inv, hi(p[4]) * inv, lo(p[5]) * inv, hi(p[5]) * inv, fast),
+                                s8x4(lo(p[6]) * inv, hi(p[6]) * inv, lo(p[7]) * inv, hi(p[7]) * inv, fast));
                             *reinterpret_cast<uint4*>(q8row + 16 * i) = w;
                         }
                         if ((lane & 15) == 0)

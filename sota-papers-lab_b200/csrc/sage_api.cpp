@@ -98,33 +98,6 @@ int make_map_bf16_2d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1,
 
 bool fits_i32(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
 
-// The one-launch quantiser's input maps: Q (when given), K, V as bf16
-// {D, heads, tokens, batch} with the tensors' own strides, box {D, 1, 64, 1},
-// zero fill past the last token.  false when TMA cannot address a tensor
-// (base or a stride not a multiple of 16 bytes); the three launches run then.
-bool prep_maps(sp::PrepMaps* pm, int64_t D, const sp::Geom& g, const void* q, const void* k, const void* v) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    memset(pm, 0, sizeof *pm);
-    auto one = [&](CUtensorMap* m, const void* base, int64_t heads, int64_t sb, int64_t st, int64_t sh) {
-        if ((uintptr_t)base % 16) return false;
-        // a dimension of extent 1 is never stepped over: any valid pitch will do
-        const int64_t pb = g.batch > 1 ? sb * 2 : ((int64_t)g.tokens * st * 2 + 15) / 16 * 16;
-        const int64_t ph = heads > 1 ? sh * 2 : D * 2;
-        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)g.tokens, (cuuint64_t)g.batch};
-        cuuint64_t strides[3] = {(cuuint64_t)ph, (cuuint64_t)(st * 2), (cuuint64_t)pb};
-        for (cuuint64_t x : strides)
-            if (x == 0 || x % 16) return false;
-        cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
-        cuuint32_t elem[4] = {1, 1, 1, 1};
-        return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, elem,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-    };
-    if (q && !one(&pm->q, q, g.heads, g.q_sb, g.q_st, g.q_sh)) return false;
-    return one(&pm->k, k, g.kv_heads, g.k_sb, g.k_st, g.k_sh) && one(&pm->v, v, g.kv_heads, g.v_sb, g.v_st, g.v_sh);
-}
-
 }  // namespace
 
 struct spl_sage {
@@ -135,7 +108,6 @@ struct spl_sage {
     int sm_count;
     int reserved_sms;  // SMs the persistent kernels leave free (spl_sage_reserve_sms)
     int gemm_pairs;    // GEMMs on SM pairs (spl_sage_gemm_pairs)
-    int quant_one_launch;  // the quantiser as one persistent launch (spl_sage_quant_one_launch)
     uint32_t* err;     // device error word of the calls that run without a workspace
 };
 
@@ -234,7 +206,6 @@ int spl_sage_create(void* stream, int head_dim, const spl_sage_config* cfg, spl_
     cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, dev);
     s->reserved_sms = 0;
     s->gemm_pairs = 1;  // measured faster at C4: bf16 1.28 -> 1.20 ms, FP8 0.81 -> 0.78 ms
-    s->quant_one_launch = 1;
     s->err = errw;
     *out = s;
     return SPL_SAGE_OK;
@@ -251,12 +222,6 @@ int spl_sage_reserve_sms(spl_sage* s, int n) {
 int spl_sage_gemm_pairs(spl_sage* s, int on) {
     if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_gemm_pairs: NULL engine");
     s->gemm_pairs = on ? 1 : 0;
-    return SPL_SAGE_OK;
-}
-
-int spl_sage_quant_one_launch(spl_sage* s, int on) {
-    if (!s) return fail(SPL_SAGE_ERR_INVALID, "spl_sage_quant_one_launch: NULL engine");
-    s->quant_one_launch = on ? 1 : 0;
     return SPL_SAGE_OK;
 }
 
@@ -336,7 +301,7 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     const size_t n_k8 = up(B * G * tk_pad * D), n_ks = up(B * G * (tk_pad / KBLOCK) * 4);
     const size_t n_v8 = up(B * G * tk_pad * D), n_st = up(B * G * 4 * D * 4);
     const size_t n_kb = up(tk_pad * 4), n_part = up(B * G * q_tiles * 4 * D * 4), n_err = 256;
-    const size_t n_ctl = up((2 + 2 * B * G) * 4);
+    const size_t n_ctl = up(B * G * 4);
     const size_t total = n_q8 + n_qs + n_k8 + n_ks + n_v8 + n_st + n_kb + n_part + n_err + n_ctl;
 
     int dev = 0;
@@ -372,7 +337,7 @@ int spl_sage_workspace_create(spl_sage* s, const spl_sage_shape* shape, const sp
     ws->buf.kbias = (float*)p; p += n_kb;
     ws->buf.part = (float*)p; p += n_part;
     ws->buf.err = (uint32_t*)p; p += n_err;
-    ws->buf.ctl = (uint32_t*)p;
+    ws->buf.tiles_done = (uint32_t*)p;
 
     const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     int rc = make_map(&ws->maps.q, ws->buf.q8, D, tq_pad, B * H, D, tq_pad * D, (uint32_t)D, 128, swz);
@@ -500,10 +465,7 @@ int spl_sage_prepare(spl_sage* s, spl_sage_ws* ws, spl_sage_tensor q, spl_sage_t
     const float* ln = nullptr;
     int rc = build_geom(s, ws, q, k, v, opts, &g, &ln);
     if (rc) return rc;
-    sp::PrepMaps pm;
-    const bool one = s->quant_one_launch && prep_maps(&pm, s->head_dim, g, q.data, k.data, v.data);
-    cudaError_t e =
-        sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, one ? &pm : nullptr, g, s->stream);
+    cudaError_t e = sp::launch_prepare(s->head_dim, q.data, k.data, v.data, ln, ws->buf, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = g;
     ws->prepared = true;
@@ -854,9 +816,7 @@ int spl_sage_qkv_gemm_quant(spl_sage* s, spl_sage_ws* ws, const spl_sage_qkv_sha
     cudaError_t e = sp::launch_qkv_gemm_2sm(s->head_dim, false, maps, (const uint16_t*)bias, rope, nullptr, nullptr,
                                             (uint16_t*)q, (uint16_t*)k, (uint16_t*)v, s->err, g, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch qkv gemm");
-    sp::PrepMaps pm;
-    const bool one = s->quant_one_launch && prep_maps(&pm, s->head_dim, ag, nullptr, k, v);
-    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, ws->buf, one ? &pm : nullptr, ag, s->stream);
+    e = sp::launch_prepare_kv(s->head_dim, k, v, ln, ws->buf, ag, s->stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage prepare");
     ws->geom = ag;
     ws->prepared = true;
@@ -947,7 +907,7 @@ int spl_sage_quantize_noalloc(void* stream, int head_dim, int pv_accum, const sp
     buf.stats = stats;
     buf.kbias = nullptr;  // dense keys: the quantiser never writes kbias
     buf.part = part;      // fully rewritten by every call before it is read
-    e = sp::launch_prepare(head_dim, q.data, k.data, v.data, o.qk_norm_params, buf, nullptr, g, (cudaStream_t)stream);
+    e = sp::launch_prepare(head_dim, q.data, k.data, v.data, o.qk_norm_params, buf, g, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "launch sage quantiser");
     return SPL_SAGE_OK;
 }

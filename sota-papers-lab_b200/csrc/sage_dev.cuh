@@ -59,9 +59,25 @@ __device__ __forceinline__ uint32_t s8(float x) {
     return (uint32_t)(q & 0xff);
 }
 
-__device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d) {
-    return s8(a) | (s8(b) << 8) | (s8(c) << 16) | (s8(d) << 24);
+// Four values x = v * (127 / amax) of one scale group -> four INT8 bytes, a
+// in the lowest byte, each rounded to nearest even and clamped as s8 does.
+// `fast` (amax zero, or finite and at least 4e-37, so that 127 / amax is
+// finite): then every |x| <= 127 (1 + 2^-23), the clamp never applies, and
+// the integer is read from the low mantissa bits of x + 1.5 * 2^23 (an FMA-
+// pipe add and byte permutes instead of conversions).  The products must
+// be rounded on their own before they come here (a plain or __fmul_rn
+// product: __fadd_rn is never fused with it; a fused multiply-add, as packed
+// f32x2 instructions were measured to become, breaks ties such as 63.5).
+__device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d, bool fast) {
+    if (!fast) return s8(a) | (s8(b) << 8) | (s8(c) << 16) | (s8(d) << 24);
+    constexpr float M = 12582912.0f;
+    const uint32_t ia = __float_as_uint(__fadd_rn(a, M)), ib = __float_as_uint(__fadd_rn(b, M));
+    const uint32_t ic = __float_as_uint(__fadd_rn(c, M)), id = __float_as_uint(__fadd_rn(d, M));
+    return __byte_perm(__byte_perm(ia, ib, 0x0040), __byte_perm(ic, id, 0x0040), 0x5410);
 }
+
+// Whether s8x4's fast path applies to a group with maximum magnitude amax.
+__device__ __forceinline__ bool s8_fast(float amax) { return amax == 0.f || (amax >= 4.0e-37f && amax <= 3.0e38f); }
 
 // Four floats -> four E4M3 bytes in one register, a in the lowest byte; the
 // two halves are joined by register pairing rather than shifts.
@@ -102,11 +118,28 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// Element-wise max / min of two bf16x2 words; a NaN element yields the other
+// element, as fmaxf / fminf do.  Exact (no rounding), so the maximum of bf16
+// values taken here equals the maximum of the same values as floats.
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t bmin2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// The two bf16 halves of a word as floats (exact), lo = the low half.
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) { return pk2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }
+
 __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+
 
 // 2^y for two arguments on the FMA pipe instead of the MUFU unit (which
 // delivers only 16 results per clock per SM).  Cody-Waite style split
@@ -238,14 +271,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
         ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1, int c2,
-                                            int c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-        ::"r"(dst), "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 

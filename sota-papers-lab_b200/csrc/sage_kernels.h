@@ -61,18 +61,11 @@ struct Buffers {
     float* kbias;
     float* part;
     uint32_t* err;
-    // control words of the one-launch quantiser (sp_prep_all): a work
-    // ticket, a finished-CTA count, then per (batch, kv head) the finished
-    // statistics tiles and a ready flag; all zero between launches (the last
-    // CTA of every launch clears them).  nullptr: the three-launch path.
-    uint32_t* ctl;
-};
-
-// TMA descriptors of the bf16 inputs of the one-launch quantiser (built per
-// call): Q, K, V as {D, heads, tokens, batch} with the caller's strides, box
-// {D, 1, 64, 1}, zero fill past the last token.
-struct PrepMaps {
-    CUtensorMap q, k, v;
+    // per (batch, kv head), the statistics tiles sp_prep has finished in the
+    // current launch (zero between launches: the CTA that finishes a slice's
+    // last tile reduces the slice's statistics and clears its count);
+    // nullptr: sp_finalize reduces them in a launch of its own.
+    uint32_t* tiles_done;
 };
 
 // TMA descriptors for the attention kernel (built once per workspace).
@@ -130,12 +123,10 @@ size_t noalloc_part_capacity();
 
 // The quantiser without its Q role (Q already quantised by the QKV GEMM's
 // epilogue): K/V statistics, finalize, K/V quantisation.
-// maps (nullptr: the three launches) selects the one-launch quantiser where
-// it applies (dense keys, no QK LayerNorm, buf.ctl set).
 cudaError_t launch_prepare_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
-                              const PrepMaps* maps, const Geom& g, cudaStream_t st);
+                              const Geom& g, cudaStream_t st);
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
-                           const PrepMaps* maps, const Geom& g, cudaStream_t st);
+                           const Geom& g, cudaStream_t st);
 cudaError_t launch_export_v(int d, const Buffers& buf, const Geom& g, uint8_t* v8_ref, cudaStream_t st);
 // Context parallelism (sage_quant.cu): Q quantised and this rank's raw K/V
 // channel statistics raw [b][g][4][D] = {sum K, sum V, -min V, max V};

@@ -13,14 +13,12 @@
 // gate) and the separate KV head count (GQA: Q and the K/V statistics run
 // as two roles of one launch).
 //
-// The reference's three launches, all HBM-bound:
+// Three launches, all HBM-bound:
 //   sp_prep      grid (q_tiles, heads + kv_heads, batch); without its Q
 //                role (Q quantised in the QKV GEMM's epilogue) (q_tiles,
 //                kv_heads, batch)
 //   sp_finalize  grid (kv_heads, batch)
 //   sp_quant_kv  grid (tk_pad / 64, kv_heads, batch)
-// or, for dense keys without QK LayerNorm (the default), sp_prep_tma: the
-// same arithmetic as one persistent TMA-fed launch (see its comment).
 #include <mutex>
 
 #include "sage_dev.cuh"
@@ -57,182 +55,12 @@ __device__ __forceinline__ void layernorm8(float* x, const float* w, const float
     for (int e = 0; e < 8; e++) x[e] = (x[e] - mean) * rstd * w[ch * 8 + e] + bias[ch * 8 + e];
 }
 
-// Q role: one 128-query tile of one q head.
-template <int D>
-__device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const float* __restrict__ ln,
-                                       int8_t* __restrict__ q8, float* __restrict__ q_scale, const Geom& g, int tile,
-                                       int h, int b) {
-    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
-    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
-    const long long bh = (long long)b * g.heads + h;
-    __shared__ unsigned gmax[QTILE / QGROUP];
-    if (tid < QTILE / QGROUP) gmax[tid] = 0u;
-    __syncthreads();
-    // every load of the tile first; the values are unpacked (and normalised)
-    // again for the quantisation pass rather than kept as floats
-    uint4 raw[NI];
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tok = tile * QTILE + tid / CH + i * TPI;
-        raw[i] = load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, tok < g.tokens);
-    }
-    auto values = [&](int i, float (&f)[8]) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        unpack_bf16x8(raw[i], f);
-        if (g.flags & LN_Q) layernorm8<D>(f, ln, ln + D, ch, g.ln_eps);
-#pragma unroll
-        for (int e = 0; e < 8; e++)
-            if (!ok) f[e] = 0.f;
-    };
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tl = tid / CH + i * TPI;
-        float qv[8];
-        values(i, qv);
-        float amax = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(qv[e]));
-        // The rows of one warp lie in one 16-row group (32 / CH <= 16 rows).
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0) atomicMax(&gmax[tl / QGROUP], __float_as_uint(amax));
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tl = tid / CH + i * TPI;
-        const float amax = __uint_as_float(gmax[tl / QGROUP]);
-        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-        float f[8];
-        values(i, f);
-        uint2 w;
-        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
-        *reinterpret_cast<uint2*>(q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + ch * 8) = w;
-    }
-    if (tid < QTILE / QGROUP) {
-        const float t = __uint_as_float(gmax[tid]) * (1.0f / 127.0f);
-        q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + tid] = t * g.q_mul;
-    }
-}
-
-// Statistics role: per-channel sum of K, sum / min / max of V over one
-// 128-token tile of one kv head, with the reference's reduction tree.
-template <int D>
-__device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
-                                           const float* __restrict__ ln, float* __restrict__ part, const Geom& g,
-                                           int tile, int h, int b) {
-    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ch = tid % CH;
-    const long long bh = (long long)b * g.kv_heads + h;
-    __shared__ float red[8][4][D];
-    float ks[8], vs[8], vmn[8], vmx[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-        ks[e] = 0.f;
-        vs[e] = 0.f;
-        vmn[e] = 3.0e38f;
-        vmx[e] = -3.0e38f;
-    }
-    // K, then V: each a pass of loads issued first, then summed in token
-    // order (the K and V statistics are independent accumulations)
-    uint4 raw[NI];
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tok = tile * QTILE + tid / CH + i * TPI;
-        raw[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, tok < g.tokens);
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        float fk[8];
-        unpack_bf16x8(raw[i], fk);
-        if (g.flags & LN_K) layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
-        if (ok) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) ks[e] += fk[e];
-        }
-    }
-    // the K sums through the lane butterfly now, so they need no registers
-    // during the V pass
-#pragma unroll
-    for (int o = CH; o < 32; o <<= 1) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
-    }
-    if (lane < CH) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) red[warp][0][ch * 8 + e] = ks[e];
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tok = tile * QTILE + tid / CH + i * TPI;
-        raw[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, tok < g.tokens);
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        float fv[8];
-        unpack_bf16x8(raw[i], fv);
-        if (ok) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                vs[e] += fv[e];
-                vmn[e] = fminf(vmn[e], fv[e]);
-                vmx[e] = fmaxf(vmx[e], fv[e]);
-            }
-        }
-    }
-#pragma unroll
-    for (int o = CH; o < 32; o <<= 1) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
-            vmn[e] = fminf(vmn[e], __shfl_xor_sync(0xffffffffu, vmn[e], o));
-            vmx[e] = fmaxf(vmx[e], __shfl_xor_sync(0xffffffffu, vmx[e], o));
-        }
-    }
-    if (lane < CH) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            red[warp][1][ch * 8 + e] = vs[e];
-            red[warp][2][ch * 8 + e] = vmn[e];
-            red[warp][3][ch * 8 + e] = vmx[e];
-        }
-    }
-    __syncthreads();
-    for (int c = tid; c < 4 * D; c += 256) {
-        const int stat = c / D, d = c % D;
-        float r = red[0][stat][d];
-#pragma unroll
-        for (int w = 1; w < 8; w++) {
-            const float x = red[w][stat][d];
-            r = stat < 2 ? r + x : (stat == 2 ? fminf(r, x) : fmaxf(r, x));
-        }
-        part[((bh * g.q_tiles + tile) * 4 + stat) * D + d] = r;
-    }
-}
-
-template <int D>
-__global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
-                                               const uint16_t* __restrict__ v, const float* __restrict__ ln,
-                                               int8_t* __restrict__ q8, float* __restrict__ q_scale,
-                                               float* __restrict__ part, const Geom g, int q_role) {
-    // grid y: the q heads (Q role, when q_role) and then the kv heads
-    const int tile = blockIdx.x, y = blockIdx.y, b = blockIdx.z;
-    const int nq = q_role ? g.heads : 0;
-    if (y < nq)
-        prep_q<D>(q, ln, q8, q_scale, g, tile, y, b);
-    else
-        prep_stats<D>(k, v, ln, part, g, tile, y - nq, b);
-}
-
 // One statistic of one channel over a (batch, kv head)'s tile partials
 // (p = the first tile's value, tiles 4 * D floats apart): the tiles summed
 // (or min / max-ed) in order as two interleaved accumulators, 16 tiles'
 // values loaded before they are combined so that the loads' latency is paid
-// once per 16 tiles.  Loads bypass L1: in the one-launch quantiser other CTAs
-// of the same launch wrote the partials.
+// once per 16 tiles.  Loads bypass L1: when sp_prep reduces them, other CTAs of
+// the same launch wrote the partials.
 template <int D>
 __device__ __forceinline__ float fin_reduce(const float* p, int stat, int q_tiles) {
     float r0 = stat < 2 ? 0.f : (stat == 2 ? 3.0e38f : -3.0e38f);
@@ -279,6 +107,281 @@ __device__ __forceinline__ void fin_store(float* o, int d, float ksum, float vsu
     o[D + d] = mv;
     o[2 * D + d] = scale;
     o[3 * D + d] = 1.0f / scale;
+}
+
+// Q role without QK LayerNorm: one 128-query tile of one q head, warp w
+// taking the 16-row scale group w (lane l: row 16 w + l / 2, channels
+// (l % 2) * D / 2 onwards), so that the group's maximum is a warp reduction.
+// The group maximum of |x| is taken on the bf16 values (exact, NaN-ignoring
+// like fmaxf): the same values and roundings as prep_q below, in fewer
+// instructions.
+template <int D>
+__device__ __forceinline__ void prep_q16(const uint16_t* __restrict__ q, int8_t* __restrict__ q8,
+                                         float* __restrict__ q_scale, const Geom& g, int tile, int h, int b) {
+    constexpr int HALF = D / 2, NV = HALF / 8;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tl = warp * QGROUP + (lane >> 1), c0 = (lane & 1) * HALF;
+    const int tok = tile * QTILE + tl;
+    const long long bh = (long long)b * g.heads + h;
+    const uint16_t* src = q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + c0;
+    uint4 raw[NV];
+#pragma unroll
+    for (int j = 0; j < NV; j++) raw[j] = load8(src + j * 8, tok < g.tokens);
+    uint32_t m2 = 0u;
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        m2 = bmax2(m2, raw[j].x & 0x7fff7fffu);
+        m2 = bmax2(m2, raw[j].y & 0x7fff7fffu);
+        m2 = bmax2(m2, raw[j].z & 0x7fff7fffu);
+        m2 = bmax2(m2, raw[j].w & 0x7fff7fffu);
+    }
+    float amax = fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xffff0000u));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    int8_t* dst = q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + c0;
+    const bool fast = s8_fast(amax);
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        float f[8];
+        unpack_bf16x8(raw[j], f);
+        // __fmul_rn: the product keeps its own rounding (never fused with
+        // s8x4's rounding add; an FMA would break ties such as 63.5)
+        uint2 w;
+        w.x = s8x4(__fmul_rn(f[0], inv), __fmul_rn(f[1], inv), __fmul_rn(f[2], inv), __fmul_rn(f[3], inv), fast);
+        w.y = s8x4(__fmul_rn(f[4], inv), __fmul_rn(f[5], inv), __fmul_rn(f[6], inv), __fmul_rn(f[7], inv), fast);
+        *reinterpret_cast<uint2*>(dst + j * 8) = w;
+    }
+    if (lane == 0)
+        q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + warp] = (amax * (1.0f / 127.0f)) * g.q_mul;
+}
+
+// Q role: one 128-query tile of one q head (any options; QK LayerNorm
+// needs a row's channels on consecutive lanes).
+template <int D>
+__device__ __forceinline__ void prep_q(const uint16_t* __restrict__ q, const float* __restrict__ ln,
+                                       int8_t* __restrict__ q8, float* __restrict__ q_scale, const Geom& g, int tile,
+                                       int h, int b) {
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
+    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
+    const long long bh = (long long)b * g.heads + h;
+    __shared__ unsigned gmax[QTILE / QGROUP];
+    if (tid < QTILE / QGROUP) gmax[tid] = 0u;
+    __syncthreads();
+    // every load of the tile first; the values are unpacked (and normalised)
+    // again for the quantisation pass rather than kept as floats
+    uint4 raw[NI];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        raw[i] = load8(q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + ch * 8, tok < g.tokens);
+    }
+    auto values = [&](int i, float (&f)[8]) {
+        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
+        unpack_bf16x8(raw[i], f);
+        if (g.flags & LN_Q) layernorm8<D>(f, ln, ln + D, ch, g.ln_eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (!ok) f[e] = 0.f;
+    };
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tl = tid / CH + i * TPI;
+        float qv[8];
+        values(i, qv);
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(qv[e]));
+        // The rows of one warp lie in one 16-row group (32 / CH <= 16 rows).
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0) atomicMax(&gmax[tl / QGROUP], __float_as_uint(amax));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tl = tid / CH + i * TPI;
+        const float amax = __uint_as_float(gmax[tl / QGROUP]);
+        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+        const bool fast = s8_fast(amax);
+        float f[8];
+        values(i, f);
+        uint2 w;
+        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
+        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv, fast);
+        *reinterpret_cast<uint2*>(q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + ch * 8) = w;
+    }
+    if (tid < QTILE / QGROUP) {
+        const float t = __uint_as_float(gmax[tid]) * (1.0f / 127.0f);
+        q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + tid] = t * g.q_mul;
+    }
+}
+
+// Statistics role: per-channel sum of K, sum / min / max of V over one
+// 128-token tile of one kv head, with the reference's reduction tree.
+template <int D>
+__device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                           const float* __restrict__ ln, float* __restrict__ part,
+                                           float* __restrict__ stats, uint32_t* __restrict__ tiles_done,
+                                           const Geom& g, int tile, int h, int b) {
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ch = tid % CH;
+    const long long bh = (long long)b * g.kv_heads + h;
+    __shared__ float red[8][4][D];
+    float ks[8], vs[8], vmn[8], vmx[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        ks[e] = 0.f;
+        vs[e] = 0.f;
+        vmn[e] = 3.0e38f;
+        vmx[e] = -3.0e38f;
+    }
+    // K, then V: each a pass of loads issued first, then summed in token
+    // order (the K and V statistics are independent accumulations)
+    uint4 raw[NI];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        raw[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, tok < g.tokens);
+    }
+    if (g.flags & LN_K) {
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
+            float fk[8];
+            unpack_bf16x8(raw[i], fk);
+            layernorm8<D>(fk, ln + 2 * D, ln + 3 * D, ch, g.ln_eps);
+            if (ok) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) ks[e] += fk[e];
+            }
+        }
+    } else {
+        // the same sums, in the same order, as packed pairs
+        uint64_t k2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            if (tile * QTILE + tid / CH + i * TPI < g.tokens) {
+                k2[0] = add2(k2[0], bf2_to_f2(raw[i].x));
+                k2[1] = add2(k2[1], bf2_to_f2(raw[i].y));
+                k2[2] = add2(k2[2], bf2_to_f2(raw[i].z));
+                k2[3] = add2(k2[3], bf2_to_f2(raw[i].w));
+            }
+        }
+#pragma unroll
+        for (int p2 = 0; p2 < 4; p2++) upk2(k2[p2], ks[2 * p2], ks[2 * p2 + 1]);
+    }
+    // the K sums through the lane butterfly now, so they need no registers
+    // during the V pass
+#pragma unroll
+    for (int o = CH; o < 32; o <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
+    }
+    if (lane < CH) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) red[warp][0][ch * 8 + e] = ks[e];
+    }
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        raw[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, tok < g.tokens);
+    }
+    {
+        // sums as packed pairs (the same order and roundings); minimum and
+        // maximum on the bf16 values (exact), starting from +-infinity and
+        // clamped to the +-3e38 starting values afterwards
+        uint64_t v2[4] = {0ull, 0ull, 0ull, 0ull};
+        uint32_t mn[4] = {0x7f807f80u, 0x7f807f80u, 0x7f807f80u, 0x7f807f80u};
+        uint32_t mx[4] = {0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u};
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            if (tile * QTILE + tid / CH + i * TPI < g.tokens) {
+                const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+                for (int p2 = 0; p2 < 4; p2++) {
+                    v2[p2] = add2(v2[p2], bf2_to_f2(w[p2]));
+                    mn[p2] = bmin2(mn[p2], w[p2]);
+                    mx[p2] = bmax2(mx[p2], w[p2]);
+                }
+            }
+        }
+#pragma unroll
+        for (int p2 = 0; p2 < 4; p2++) {
+            upk2(v2[p2], vs[2 * p2], vs[2 * p2 + 1]);
+            vmn[2 * p2] = fminf(vmn[2 * p2], __uint_as_float(mn[p2] << 16));
+            vmn[2 * p2 + 1] = fminf(vmn[2 * p2 + 1], __uint_as_float(mn[p2] & 0xffff0000u));
+            vmx[2 * p2] = fmaxf(vmx[2 * p2], __uint_as_float(mx[p2] << 16));
+            vmx[2 * p2 + 1] = fmaxf(vmx[2 * p2 + 1], __uint_as_float(mx[p2] & 0xffff0000u));
+        }
+    }
+#pragma unroll
+    for (int o = CH; o < 32; o <<= 1) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
+            vmn[e] = fminf(vmn[e], __shfl_xor_sync(0xffffffffu, vmn[e], o));
+            vmx[e] = fmaxf(vmx[e], __shfl_xor_sync(0xffffffffu, vmx[e], o));
+        }
+    }
+    if (lane < CH) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            red[warp][1][ch * 8 + e] = vs[e];
+            red[warp][2][ch * 8 + e] = vmn[e];
+            red[warp][3][ch * 8 + e] = vmx[e];
+        }
+    }
+    __syncthreads();
+    for (int c = tid; c < 4 * D; c += 256) {
+        const int stat = c / D, d = c % D;
+        float r = red[0][stat][d];
+#pragma unroll
+        for (int w = 1; w < 8; w++) {
+            const float x = red[w][stat][d];
+            r = stat < 2 ? r + x : (stat == 2 ? fminf(r, x) : fmaxf(r, x));
+        }
+        part[((bh * g.q_tiles + tile) * 4 + stat) * D + d] = r;
+    }
+    if (!tiles_done) return;
+    // The CTA that finishes the slice's last tile reduces the slice's
+    // partials (the tree of sp_finalize) and clears its count for the next
+    // launch; sp_finalize then does not run.
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(tiles_done + bh, 1u) == (uint32_t)(g.q_tiles - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    float* fr = &red[0][0][0];  // the four reduced statistics, [4][D]
+    for (int c = tid; c < 4 * D; c += 256)
+        fr[c] = fin_reduce<D>(part + bh * g.q_tiles * 4 * D + (c / D) * D + c % D, c / D, g.q_tiles);
+    __syncthreads();
+    for (int d = tid; d < D; d += 256) fin_store<D>(stats + bh * 4 * D, d, fr[d], fr[D + d], fr[2 * D + d], fr[3 * D + d], g);
+    if (tid == 0) tiles_done[bh] = 0u;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                                               const uint16_t* __restrict__ v, const float* __restrict__ ln,
+                                               int8_t* __restrict__ q8, float* __restrict__ q_scale,
+                                               float* __restrict__ part, float* __restrict__ stats,
+                                               uint32_t* __restrict__ tiles_done, const Geom g, int q_role) {
+    // grid y: the Q role of every (batch, q head) (when q_role), then the
+    // statistics role of every (batch, kv head), so that the K and V tiles
+    // are the last inputs read (sp_quant_kv reads them again, newest first,
+    // while they are still in L2)
+    const int tile = blockIdx.x, y = blockIdx.y + blockIdx.z * gridDim.y;
+    const int nq = q_role ? g.batch * g.heads : 0;
+    if (y >= nq + g.batch * g.kv_heads) return;  // past the roles (grid y split over z)
+    if (y < nq)
+        if (g.flags & LN_Q)
+            prep_q<D>(q, ln, q8, q_scale, g, tile, y % g.heads, y / g.heads);
+        else
+            prep_q16<D>(q, q8, q_scale, g, tile, y % g.heads, y / g.heads);
+    else
+        prep_stats<D>(k, v, ln, part, stats, tiles_done, g, tile, (y - nq) % g.kv_heads, (y - nq) / g.kv_heads);
 }
 
 // Per (kv head, batch, 32 channels): K mean, V mean, V scale and its
@@ -406,12 +509,13 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
         __syncthreads();
         const float km = __uint_as_float(kmax);
         const float inv = km > 0.f ? 127.0f / km : 0.f;
+        const bool fast = s8_fast(km);
 #pragma unroll
         for (int i = 0; i < NI; i++) {
             const float* f = kq[i];
             uint2 w;
-            w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-            w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+            w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
+            w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv, fast);
             *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + 4 * m + i) * D + ch * 8) = w;
         }
         if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
@@ -506,13 +610,14 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
 
     const float km = __uint_as_float(kmax);
     const float inv = km > 0.f ? 127.0f / km : 0.f;
+    const bool fast = s8_fast(km);
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int kl = tid / CH + i * TPI;
         const float* f = kv[i];
         uint2 w;
-        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
+        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
+        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv, fast);
         *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + kl) * D + ch * 8) = w;
     }
     if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
@@ -529,490 +634,22 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
     }
 }
 
+// Resident sp_quant_kv CTAs per SM the register allocation must allow: the
+// kernel waits on its loads (one 64-key K and V block per CTA), so more CTAs
+// keep more bytes in flight.
+#ifndef SP_QUANT_KV_CTAS
+#define SP_QUANT_KV_CTAS 3
+#endif
 template <int D>
-__global__ void __launch_bounds__(256) sp_quant_kv(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+__global__ void __launch_bounds__(256, SP_QUANT_KV_CTAS) sp_quant_kv(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                                                    const float* __restrict__ ln, const float* __restrict__ stats,
                                                    int8_t* __restrict__ k8, float* __restrict__ k_scale,
                                                    uint8_t* __restrict__ v8, float* __restrict__ kbias,
                                                    const Geom g) {
-    quant_kv_block<D>(k, v, ln, stats, k8, k_scale, v8, kbias, g, blockIdx.x, blockIdx.y, blockIdx.z);
-}
-
-// ---------------------------------------------------------------- one launch
-// The three passes above as one persistent launch fed by TMA, for dense keys
-// without QK LayerNorm (the other cases keep the three launches).  One CTA
-// per SM: a producer warp streams each work item's bf16 input tiles into a
-// ring of shared-memory slots (cp.async.bulk.tensor, up to 192 KB in
-// flight per SM), eight consumer warps turn them into the outputs with the
-// arithmetic of sp_prep / sp_finalize / sp_quant_kv (the same thread-to-
-// value mapping, reduction trees and roundings, so the bytes are the same).
-// Work items, taken in order from a ticket counter, are laid out in rounds
-// r = 0 .. slices + lag - 1 of equal width
-//   [ statistics tiles of slice r | a share of the Q tiles | K/V blocks of slice r - lag ]
-// (slice = one (batch, kv head); out-of-range items are skipped), so that a
-// slice's K and V (2 MB at D = 128, N = 8192) are read again for
-// quantisation while its statistics pass has left them in L2.  The CTA that
-// finishes a slice's last statistics tile reduces the slice's partials (the
-// tree of sp_finalize) and sets the slice's ready flag; a K/V block waits
-// for that flag.  No wait can close a cycle: an item only ever waits on
-// items with smaller tickets (a K/V block on its slice's statistics tiles,
-// which precede it; a ring slot on the items ahead of it in the same ring).
-// Every wait is bounded (ERR_TIMEOUT; sites 60-63).
-struct PrepSchedule {
-    int slices;   // batch * kv_heads
-    int ns;       // statistics tiles per slice (q_tiles)
-    int nq;       // Q tiles per round
-    int nk;       // K/V blocks per slice (tk_pad / 64)
-    int lag;      // rounds between a slice's statistics and its K/V blocks
-    int q_total;  // Q tiles in all (0: no Q role)
-    int width;    // items per round
-    int total;    // items in all
-};
-
-template <int D>
-struct PrepRing {
-    static constexpr int TILE = QTILE * D * 2;  // 128 tokens of one head, bf16
-    static constexpr int SLOT = 2 * TILE;       // a statistics item: K and V tiles
-    static constexpr int NSLOT = 192 * 1024 / SLOT;
-    static constexpr int DYN = NSLOT * SLOT + 1024;
-    static constexpr int THREADS = 256 + 32;    // eight consumer warps, one producer warp
-};
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// the eight consumer warps only
-__device__ __forceinline__ void csync() { named_bar(1, 256); }
-
-__device__ __forceinline__ uint4 lds16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-
-// prep_q on a tile in shared memory (rows of D bf16; rows past the last
-// token were zero-filled by TMA and are zeroed again here, as load8 does).
-template <int D>
-__device__ __forceinline__ void tile_q(const uint8_t* t, int8_t* __restrict__ q8, float* __restrict__ q_scale,
-                                       const Geom& g, int tile, int h, int b, unsigned* gmax) {
-    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
-    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
-    const long long bh = (long long)b * g.heads + h;
-    if (tid < QTILE / QGROUP) gmax[tid] = 0u;
-    csync();
-    uint4 raw[NI];
-#pragma unroll
-    for (int i = 0; i < NI; i++) raw[i] = lds16(t + ((tid / CH + i * TPI) * D + ch * 8) * 2);
-    auto values = [&](int i, float (&f)[8]) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        unpack_bf16x8(raw[i], f);
-#pragma unroll
-        for (int e = 0; e < 8; e++)
-            if (!ok) f[e] = 0.f;
-    };
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tl = tid / CH + i * TPI;
-        float qv[8];
-        values(i, qv);
-        float amax = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(qv[e]));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0) atomicMax(&gmax[tl / QGROUP], __float_as_uint(amax));
-    }
-    csync();
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tl = tid / CH + i * TPI;
-        const float amax = __uint_as_float(gmax[tl / QGROUP]);
-        const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-        float f[8];
-        values(i, f);
-        uint2 w;
-        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
-        *reinterpret_cast<uint2*>(q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + ch * 8) = w;
-    }
-    if (tid < QTILE / QGROUP) {
-        const float tq = __uint_as_float(gmax[tid]) * (1.0f / 127.0f);
-        q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + tid] = tq * g.q_mul;
-    }
-}
-
-// prep_stats on K and V tiles in shared memory; red: [8][4][D] floats.
-template <int D>
-__device__ __forceinline__ void tile_stats(const uint8_t* kt, const uint8_t* vt, float* __restrict__ part,
-                                           const Geom& g, int tile, int h, int b, float* red) {
-    constexpr int CH = D / 8, TPI = 256 / CH, NI = QTILE / TPI;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ch = tid % CH;
-    const long long bh = (long long)b * g.kv_heads + h;
-    float ks[8], vs[8], vmn[8], vmx[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-        ks[e] = 0.f;
-        vs[e] = 0.f;
-        vmn[e] = 3.0e38f;
-        vmx[e] = -3.0e38f;
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        float fk[8];
-        unpack_bf16x8(lds16(kt + ((tid / CH + i * TPI) * D + ch * 8) * 2), fk);
-        if (ok) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) ks[e] += fk[e];
-        }
-    }
-#pragma unroll
-    for (int o = CH; o < 32; o <<= 1) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) ks[e] += __shfl_xor_sync(0xffffffffu, ks[e], o);
-    }
-    if (lane < CH) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) red[(warp * 4 + 0) * D + ch * 8 + e] = ks[e];
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const bool ok = tile * QTILE + tid / CH + i * TPI < g.tokens;
-        float fv[8];
-        unpack_bf16x8(lds16(vt + ((tid / CH + i * TPI) * D + ch * 8) * 2), fv);
-        if (ok) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                vs[e] += fv[e];
-                vmn[e] = fminf(vmn[e], fv[e]);
-                vmx[e] = fmaxf(vmx[e], fv[e]);
-            }
-        }
-    }
-#pragma unroll
-    for (int o = CH; o < 32; o <<= 1) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            vs[e] += __shfl_xor_sync(0xffffffffu, vs[e], o);
-            vmn[e] = fminf(vmn[e], __shfl_xor_sync(0xffffffffu, vmn[e], o));
-            vmx[e] = fmaxf(vmx[e], __shfl_xor_sync(0xffffffffu, vmx[e], o));
-        }
-    }
-    if (lane < CH) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            red[(warp * 4 + 1) * D + ch * 8 + e] = vs[e];
-            red[(warp * 4 + 2) * D + ch * 8 + e] = vmn[e];
-            red[(warp * 4 + 3) * D + ch * 8 + e] = vmx[e];
-        }
-    }
-    csync();
-    for (int c = tid; c < 4 * D; c += 256) {
-        const int stat = c / D, d = c % D;
-        float r = red[stat * D + d];
-#pragma unroll
-        for (int w = 1; w < 8; w++) {
-            const float x = red[(w * 4 + stat) * D + d];
-            r = stat < 2 ? r + x : (stat == 2 ? fminf(r, x) : fmaxf(r, x));
-        }
-        part[((bh * g.q_tiles + tile) * 4 + stat) * D + d] = r;
-    }
-}
-
-// quant_kv_block's dense paths (one member per key) on 64-key K and V tiles
-// in shared memory; scratch: at least D * 17 words.
-template <int D>
-__device__ __forceinline__ void tile_quant_kv(const uint8_t* kt, const uint8_t* vt, const float* __restrict__ stats,
-                                              int8_t* __restrict__ k8, float* __restrict__ k_scale,
-                                              uint8_t* __restrict__ v8, const Geom& g, int blk, int h, int b,
-                                              uint32_t* scratch, unsigned* kmax) {
-    constexpr int CH = D / 8, TPI = 256 / CH, NI = KBLOCK / TPI;
-    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
-    const long long bh = (long long)b * g.kv_heads + h;
-    const int nblk = g.tk_pad / KBLOCK;
-    if (tid == 0) *kmax = 0u;
-    float mk[8], mv[8], rv[8];
-    {
-        const float* st = stats + bh * 4 * D + ch * 8;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            mk[e] = __ldcg(st + e);
-            mv[e] = __ldcg(st + D + e);
-            rv[e] = __ldcg(st + 3 * D + e);
-        }
-    }
-    csync();
-    if (NI == 4) {
-        // thread (m, ch): keys 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7, each
-        // channel's 4 E4M3 bytes one word of the transposed tile
-        uint32_t (*vw)[17] = reinterpret_cast<uint32_t (*)[17]>(scratch);
-        const int m = tid / CH;
-        float kq[NI][8];
-        float amx = 0.f;
-        uint32_t word[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int i = 0; i < NI; i++) {
-            const bool ok = blk * KBLOCK + 4 * m + i < g.tk;
-            float fk[8], fv[8];
-            unpack_bf16x8(lds16(kt + ((4 * m + i) * D + ch * 8) * 2), fk);
-            unpack_bf16x8(lds16(vt + ((4 * m + i) * D + ch * 8) * 2), fv);
-            float vq[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
-                amx = fmaxf(amx, fabsf(kq[i][e]));
-                vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
-                word[e] |= (two & 0xffu) << (8 * i);
-                word[e + 1] |= (two >> 8) << (8 * i);
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
-        if (lane == 0) atomicMax(kmax, __float_as_uint(amx));
-        csync();
-        const float km = __uint_as_float(*kmax);
-        const float inv = km > 0.f ? 127.0f / km : 0.f;
-#pragma unroll
-        for (int i = 0; i < NI; i++) {
-            const float* f = kq[i];
-            uint2 w;
-            w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-            w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
-            *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + 4 * m + i) * D + ch * 8) = w;
-        }
-        if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
-        for (int c = tid; c < D * 16; c += 256) {
-            const int d = c >> 4, w = c & 15;
-            *reinterpret_cast<uint32_t*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) = vw[d][w];
-        }
-        return;
-    }
-    uint8_t (*vtr)[KBLOCK] = reinterpret_cast<uint8_t (*)[KBLOCK]>(scratch);
-    float kv[NI][8];
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int kl = tid / CH + i * TPI;
-        const bool ok = blk * KBLOCK + kl < g.tk;
-        float fk[8], fv[8], vq[8];
-        unpack_bf16x8(lds16(kt + (kl * D + ch * 8) * 2), fk);
-        unpack_bf16x8(lds16(vt + (kl * D + ch * 8) * 2), fv);
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
-            amax = fmaxf(amax, fabsf(kv[i][e]));
-            vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
-            vtr[ch * 8 + e][kl] = (uint8_t)(two & 0xff);
-            vtr[ch * 8 + e + 1][kl] = (uint8_t)(two >> 8);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) atomicMax(kmax, __float_as_uint(amax));
-    csync();
-    const float km = __uint_as_float(*kmax);
-    const float inv = km > 0.f ? 127.0f / km : 0.f;
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int kl = tid / CH + i * TPI;
-        const float* f = kv[i];
-        uint2 w;
-        w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv);
-        w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv);
-        *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + kl) * D + ch * 8) = w;
-    }
-    if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
-    for (int c = tid; c < D * (KBLOCK / 16); c += 256) {
-        const int d = c / (KBLOCK / 16), part16 = c % (KBLOCK / 16);
-        *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + part16 * 16) =
-            *reinterpret_cast<const uint4*>(&vtr[d][part16 * 16]);
-    }
-}
-
-// Item kinds of the one-launch schedule.
-enum : int { ITEM_NONE = 0, ITEM_STATS = 1, ITEM_Q = 2, ITEM_KV = 3 };
-
-__device__ __forceinline__ int item_kind(const PrepSchedule& ps, int item, int& r, int& o) {
-    r = item / ps.width;
-    o = item % ps.width;
-    if (o < ps.ns) return r < ps.slices ? ITEM_STATS : ITEM_NONE;
-    if (o < ps.ns + ps.nq) return r * ps.nq + (o - ps.ns) < ps.q_total ? ITEM_Q : ITEM_NONE;
-    const int sl = r - ps.lag;
-    return sl >= 0 && sl < ps.slices ? ITEM_KV : ITEM_NONE;
-}
-
-template <int D>
-__global__ void __launch_bounds__(PrepRing<D>::THREADS, 1)
-    sp_prep_tma(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                const __grid_constant__ CUtensorMap map_v, const Buffers buf, const Geom g, const PrepSchedule ps) {
-    using R = PrepRing<D>;
-    extern __shared__ uint8_t dyn_smem[];
-    __shared__ __align__(8) uint64_t full[R::NSLOT], empty[R::NSLOT];
-    __shared__ int slot_item[R::NSLOT];
-    __shared__ __align__(16) float scratch[8 * 4 * D];  // statistics tree or the V transpose
-    __shared__ float s_red[4][D];
-    __shared__ unsigned s_small[QTILE / QGROUP + 1];
-    __shared__ int s_flag;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-    const uint8_t* ring = dyn_smem + (base - smem_u32(dyn_smem));
-    uint32_t* ticket = buf.ctl;
-    uint32_t* done = buf.ctl + 1;
-    uint32_t* tiles_done = buf.ctl + 2;
-    uint32_t* ready = buf.ctl + 2 + ps.slices;
-    auto bar = [](uint64_t& x) { return smem_u32(&x); };
-    if (tid == 0) {
-        for (int i = 0; i < R::NSLOT; i++) {
-            mbar_init(bar(full[i]), 1);
-            mbar_init(bar(empty[i]), 8);  // one arrival per consumer warp
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    if (warp == 8) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            tma_prefetch_desc(&map_k);
-            tma_prefetch_desc(&map_v);
-            if (ps.q_total) tma_prefetch_desc(&map_q);
-            int n = 0;  // slots filled
-            bool ok = true;
-            for (;;) {
-                int item = (int)atomicAdd(ticket, 1u), r = 0, o = 0;
-                int kind = ITEM_NONE;
-                if (item < ps.total) {
-                    kind = item_kind(ps, item, r, o);
-                    if (kind == ITEM_NONE) continue;
-                } else {
-                    item = -1;  // the end
-                }
-                const int s = n % R::NSLOT;
-                if (n >= R::NSLOT && !(ok = mbar_wait(bar(empty[s]), ((n / R::NSLOT) - 1) & 1, buf.err, 61))) break;
-                slot_item[s] = item;
-                const uint32_t dst = base + s * R::SLOT, fb = bar(full[s]);
-                if (kind == ITEM_STATS) {
-                    const int h = r % g.kv_heads, b = r / g.kv_heads, t0 = o * QTILE;
-                    mbar_expect_tx(fb, 2 * R::TILE);
-                    tma_load_4d(dst, &map_k, fb, 0, h, t0, b);
-                    tma_load_4d(dst + R::TILE / 2, &map_k, fb, 0, h, t0 + 64, b);
-                    tma_load_4d(dst + R::TILE, &map_v, fb, 0, h, t0, b);
-                    tma_load_4d(dst + R::TILE + R::TILE / 2, &map_v, fb, 0, h, t0 + 64, b);
-                } else if (kind == ITEM_Q) {
-                    const int qi = r * ps.nq + (o - ps.ns);
-                    const int tile = qi % g.q_tiles, rest = qi / g.q_tiles;
-                    const int h = rest % g.heads, b = rest / g.heads, t0 = tile * QTILE;
-                    mbar_expect_tx(fb, R::TILE);
-                    tma_load_4d(dst, &map_q, fb, 0, h, t0, b);
-                    tma_load_4d(dst + R::TILE / 2, &map_q, fb, 0, h, t0 + 64, b);
-                } else if (kind == ITEM_KV) {
-                    const int sl = r - ps.lag, blk = o - ps.ns - ps.nq;
-                    const int h = sl % g.kv_heads, b = sl / g.kv_heads;
-                    mbar_expect_tx(fb, R::TILE);
-                    tma_load_4d(dst, &map_k, fb, 0, h, blk * KBLOCK, b);
-                    tma_load_4d(dst + R::TILE / 2, &map_v, fb, 0, h, blk * KBLOCK, b);
-                } else {
-                    mbar_arrive(fb);  // the end marker: no bytes
-                }
-                n++;
-                if (item < 0) break;
-            }
-            // every load this warp issued has landed before it leaves
-            for (int s = 0; s < R::NSLOT && s < n; s++) {
-                const int last = s + ((n - 1 - s) / R::NSLOT) * R::NSLOT;
-                mbar_wait(bar(full[s]), (last / R::NSLOT) & 1, buf.err, 62, false);
-            }
-            (void)ok;
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------------- consumers
-    for (int n = 0;; n++) {
-        const int s = n % R::NSLOT;
-        if (!warp_all_wait(bar(full[s]), (n / R::NSLOT) & 1, buf.err, 60)) break;
-        const int item = slot_item[s];
-        if (item < 0) break;
-        const uint8_t* slot = ring + s * R::SLOT;
-        int r = 0, o = 0;
-        const int kind = item_kind(ps, item, r, o);
-        csync();  // the previous item's shared scratch is free
-        if (kind == ITEM_STATS) {
-            const int h = r % g.kv_heads, b = r / g.kv_heads;
-            tile_stats<D>(slot, slot + R::TILE, buf.part, g, o, h, b, scratch);
-            __threadfence();
-            csync();
-            if (tid == 0) s_flag = atomicAdd(tiles_done + r, 1u) == (uint32_t)(ps.ns - 1);
-            csync();
-            if (s_flag) {
-                // the slice's last tile: its statistics, as sp_finalize computes them
-                __threadfence();
-                const long long bh = (long long)b * g.kv_heads + h;
-                for (int c = tid; c < 4 * D; c += 256) {
-                    const int stat = c / D, d = c % D;
-                    s_red[stat][d] = fin_reduce<D>(buf.part + bh * g.q_tiles * 4 * D + stat * D + d, stat, g.q_tiles);
-                }
-                csync();
-                for (int d = tid; d < D; d += 256)
-                    fin_store<D>(buf.stats + bh * 4 * D, d, s_red[0][d], s_red[1][d], s_red[2][d], s_red[3][d], g);
-                __threadfence();
-                csync();
-                if (tid == 0) st_release_gpu(ready + r, 1u);
-            }
-        } else if (kind == ITEM_Q) {
-            const int qi = r * ps.nq + (o - ps.ns);
-            const int tile = qi % g.q_tiles, rest = qi / g.q_tiles;
-            tile_q<D>(slot, buf.q8, buf.q_scale, g, tile, rest % g.heads, rest / g.heads, s_small);
-        } else {
-            const int sl = r - ps.lag, blk = o - ps.ns - ps.nq;
-            if (tid == 0) {
-                int ok = 1;
-                if (ld_acquire_gpu(ready + sl) == 0u) {
-                    const unsigned long long t0 = globaltimer();
-                    for (uint32_t i = 1;; ++i) {
-                        __nanosleep(128);
-                        if (ld_acquire_gpu(ready + sl) != 0u) break;
-                        if ((i & 63u) == 0 &&
-                            (globaltimer() - t0 > WAIT_LIMIT_NS || i >= WAIT_MAX_TRIES || ld_volatile(buf.err) != 0)) {
-                            atomicOr(buf.err, ERR_TIMEOUT | (63u << ERR_SITE_SHIFT));
-                            ok = 0;
-                            break;
-                        }
-                    }
-                }
-                s_flag = ok;
-            }
-            csync();
-            if (s_flag)
-                tile_quant_kv<D>(slot, slot + R::TILE / 2, buf.stats, buf.k8, buf.k_scale, buf.v8, g, blk,
-                                 sl % g.kv_heads, sl / g.kv_heads, reinterpret_cast<uint32_t*>(scratch),
-                                 &s_small[QTILE / QGROUP]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(empty[s]));
-    }
-    // the last CTA out clears the control words for the next launch
-    csync();
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(done, 1u) == gridDim.x - 1) {
-            for (int i = 0; i < 2 * ps.slices; i++) tiles_done[i] = 0u;
-            *ticket = 0u;
-            *done = 0u;
-            __threadfence();
-        }
-    }
+    // newest statistics tiles first (reverse of sp_prep's order): their K
+    // and V are the likeliest to be in L2 still
+    quant_kv_block<D>(k, v, ln, stats, k8, k_scale, v8, kbias, g, gridDim.x - 1 - blockIdx.x,
+                      gridDim.y - 1 - blockIdx.y, gridDim.z - 1 - blockIdx.z);
 }
 
 // The reference's V layout for the bit gate: [b][g][tk_pad/64][D][64], keys
@@ -1034,58 +671,36 @@ __global__ void __launch_bounds__(256) sp_export_v(const uint8_t* __restrict__ v
     }
 }
 
+// sp_prep's grid: x the 128-token tiles, y (split over z past 65535) the
+// roles of every batch item.
+static dim3 prep_grid(const Geom& g, int q_role) {
+    const int roles = g.batch * ((q_role ? g.heads : 0) + g.kv_heads);
+    const int y = roles < 65535 ? roles : 65535;
+    return dim3(g.q_tiles, y, (roles + y - 1) / y);
+}
+
 template <int D>
 static cudaError_t prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
-                             const PrepMaps* maps, const Geom& g, cudaStream_t st) {
+                             const Geom& g, cudaStream_t st) {
     const int q_role = q != nullptr;
-    if (maps && buf.ctl && g.merge == 1 && !(g.flags & (LN_Q | LN_K))) {
-        using R = PrepRing<D>;
-        static int sms = 0;
-        static std::once_flag once;
-        std::call_once(once, [] {
-            int dev = 0;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            cudaFuncSetAttribute(sp_prep_tma<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, R::DYN);
-        });
-        PrepSchedule ps;
-        ps.slices = g.batch * g.kv_heads;
-        ps.ns = g.q_tiles;
-        ps.nk = g.tk_pad / KBLOCK;
-        ps.q_total = q_role ? g.batch * g.heads * g.q_tiles : 0;
-        // lag: enough rounds that a slice's statistics tiles were all taken
-        // well before its first K/V block is (two rings' worth of items per SM)
-        const long long need = 2LL * sms * R::NSLOT;
-        ps.lag = 1;
-        for (;;) {
-            const int rounds = ps.slices + ps.lag;
-            ps.nq = (ps.q_total + rounds - 1) / rounds;
-            ps.width = ps.ns + ps.nq + ps.nk;
-            if (ps.lag >= ps.slices || (long long)ps.lag * ps.width + ps.nq >= need) break;
-            ps.lag++;
-        }
-        ps.total = (ps.slices + ps.lag) * ps.width;
-        sp_prep_tma<D><<<sms, R::THREADS, R::DYN, st>>>(maps->q, maps->k, maps->v, buf, g, ps);
-        return cudaGetLastError();
-    }
-    sp_prep<D><<<dim3(g.q_tiles, (q_role ? g.heads : 0) + g.kv_heads, g.batch), 256, 0, st>>>(
-        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g, q_role);
-    sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
+    sp_prep<D><<<prep_grid(g, q_role), 256, 0, st>>>(
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, buf.stats,
+        buf.tiles_done, g, q_role);
+    if (!buf.tiles_done) sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
     sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
     return cudaGetLastError();
 }
 
 cudaError_t launch_prepare(int d, const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
-                           const PrepMaps* maps, const Geom& g, cudaStream_t st) {
+                           const Geom& g, cudaStream_t st) {
     if (!q) return cudaErrorInvalidValue;
-    return d == 64 ? prepare_d<64>(q, k, v, ln, buf, maps, g, st) : prepare_d<128>(q, k, v, ln, buf, maps, g, st);
+    return d == 64 ? prepare_d<64>(q, k, v, ln, buf, g, st) : prepare_d<128>(q, k, v, ln, buf, g, st);
 }
 
 cudaError_t launch_prepare_kv(int d, const void* k, const void* v, const float* ln, const Buffers& buf,
-                              const PrepMaps* maps, const Geom& g, cudaStream_t st) {
-    return d == 64 ? prepare_d<64>(nullptr, k, v, ln, buf, maps, g, st)
-                   : prepare_d<128>(nullptr, k, v, ln, buf, maps, g, st);
+                              const Geom& g, cudaStream_t st) {
+    return d == 64 ? prepare_d<64>(nullptr, k, v, ln, buf, g, st) : prepare_d<128>(nullptr, k, v, ln, buf, g, st);
 }
 
 // ---------------------------------------------------------------- context parallelism
@@ -1156,8 +771,10 @@ __global__ void __launch_bounds__(256) sp_cp_finish(const float* __restrict__ ac
 template <int D>
 static cudaError_t cp_prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                                 const Geom& g, float* raw, cudaStream_t st) {
-    sp_prep<D><<<dim3(g.q_tiles, g.heads + g.kv_heads, g.batch), 256, 0, st>>>(
-        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, g, 1);
+    // (the partials are reduced across ranks: sp_prep does not finish them)
+    sp_prep<D><<<prep_grid(g, 1), 256, 0, st>>>(
+        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, nullptr,
+        nullptr, g, 1);
     sp_cp_partial<D><<<dim3(g.kv_heads, g.batch), 256, 0, st>>>(buf.part, raw, g);
     return cudaGetLastError();
 }

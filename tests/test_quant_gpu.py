@@ -80,58 +80,3 @@ def test_long_ragged_sequence_quantiser():
     want = O.prepare(x.q, x.k, x.v, st.geom(c), None)
     st.assert_quant_equal(ours, want, what="T3001")
 
-
-ONE_LAUNCH_CASES = {
-    # the C4 bench shape (bench.py's generator): 32 kv slices, lag of 2 rounds
-    "c4": dict(bench="C4"),
-    # the C2 shape: 128 slices of 11 tiles, D = 64, a lag of many rounds
-    "c2": dict(bench="C2"),
-    "gqa_t3001": dict(batch=2, heads=8, kv_heads=2, tokens=3001, d=128),
-    "merge2": dict(merge=2),
-    "merge4_ln": dict(merge=4, ln=True),
-}
-
-
-@pytest.mark.parametrize("name", list(ONE_LAUNCH_CASES))
-def test_one_launch_quantiser_equals_three_launches(name):
-    """The persistent one-launch quantiser (sp_prep_all, the default) writes
-    the same bytes as the reference's three launches, on consecutive calls
-    (its control words are cleared by each launch's last CTA)."""
-    import torch
-
-    import bench
-    import sagetest as st
-    spec = ONE_LAUNCH_CASES[name]
-    if "bench" in spec:
-        w = bench.WORKLOADS[spec["bench"]]
-        q, k, v = bench.make_inputs(w, w["batch"], 5, "cuda")
-        bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
-        c = st.Case(batch=w["batch"], heads=w["heads"], kv_heads=w["kv_heads"], tokens=w["tokens"], d=w["d"],
-                    causal=w["causal"], packed=False)
-        x = st.Inputs(bits(q), bits(k), bits(v), None)
-        del q, k, v
-    elif "merge" in spec:
-        c = _case(st, 128, "merge2" if spec["merge"] == 2 else "merge4_ln")
-        x = st.make_inputs(c)
-    else:
-        c = st.Case(**spec, packed=False)
-        x = st.make_inputs(c)
-    runs = []
-    for one in (False, True, True):
-        eng = st.engine(c)
-        eng.quant_one_launch(one)
-        ws = eng.workspace(st.sage.Shape(c.batch, c.heads, c.tokens, c.kv_heads, c.causal), st.merge_of(c))
-        keep, (tq, tk, tv) = st.to_device(c, x)
-        opts = st.sage.Options(smooth_k=c.smooth, smooth_v=c.smooth)
-        ln_dev = None
-        if c.ln:
-            ln_dev = torch.from_numpy(x.ln).cuda()
-            opts.qk_norm = st.sage.QkNorm(ln_dev, 1e-5)
-        eng.prepare(ws, tq, tk, tv, opts)
-        if one:
-            eng.prepare(ws, tq, tk, tv, opts)  # a second call on the same workspace
-        assert eng.status(ws) == 0
-        runs.append(st.export_quant(eng, ws, c))
-        del keep
-    for other in runs[1:]:
-        st.assert_quant_equal(other, runs[0], what=f"one launch vs three, {name}")

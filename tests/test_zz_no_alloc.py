@@ -110,3 +110,37 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     with pytest.raises(sage.SageError) as e:
         sage.quantize_noalloc(d, sage.Shape(b, h, t, h), tv, tv, tv, small, small, small, small, small, small)
     assert "scratch" in str(e.value)
+
+
+@pytest.mark.parametrize("name", ["C4", "C2"])
+def test_noalloc_matches_workspace_prepare_at_benchmark_shapes(name):
+    """At the benchmark shapes (bench.py's generator): with a workspace the
+    slice statistics are reduced by the CTA that finishes a slice's last
+    statistics tile, without one by sp_finalize in a launch of its own; the
+    bytes are the same (many tiles per slice, every slice's count reset for
+    the next call: the workspace path runs twice)."""
+    import bench
+    w = bench.WORKLOADS[name]
+    q, k, v = bench.make_inputs(w, w["batch"], 4, "cuda")
+    c = Case(batch=w["batch"], heads=w["heads"], kv_heads=w["kv_heads"], tokens=w["tokens"], d=w["d"],
+             packed=False)
+    st_q, st_kv = sage.Strides.bthd(c.tokens, c.heads, c.d), sage.Strides.bthd(c.tokens, c.kv_heads, c.d)
+    tensors = (sage.Tensor(q.reshape(-1), st_q), sage.Tensor(k.reshape(-1), st_kv), sage.Tensor(v.reshape(-1), st_kv))
+    outs = _outputs(c)
+    _call(c, None, tensors, outs)
+    torch.cuda.synchronize()
+    got = _host(c, outs)
+    del outs
+    eng = engine(c)
+    ws = eng.workspace(sage.Shape(c.batch, c.heads, c.tokens, c.kv_heads))
+    opts = sage.Options(smooth_k=c.smooth, smooth_v=c.smooth)
+    for _ in range(2):
+        eng.prepare(ws, *tensors, opts)
+    assert eng.status(ws) == 0
+    from sagetest import export_quant
+    want = export_quant(eng, ws, c)
+    for name_, arr in got.items():
+        ref = getattr(want, name_)
+        assert arr.shape == ref.shape, name_
+        np.testing.assert_array_equal(arr.view(np.uint8), np.ascontiguousarray(ref).view(np.uint8),
+                                      err_msg=f"{name}: {name_}")
