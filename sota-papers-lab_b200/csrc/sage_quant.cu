@@ -110,23 +110,27 @@ __device__ __forceinline__ void fin_store(float* o, int d, float ksum, float vsu
 }
 
 // Q role without QK LayerNorm: one 128-query tile of one q head, warp w
-// taking the 16-row scale group w (lane l: row 16 w + l / 2, channels
-// (l % 2) * D / 2 onwards), so that the group's maximum is a warp reduction.
-// The group maximum of |x| is taken on the bf16 values (exact, NaN-ignoring
-// like fmaxf): the same values and roundings as prep_q below, in fewer
-// instructions.
+// taking the 16-row scale group w, so that the group's maximum is a warp
+// reduction (no shared memory, atomics or block barrier).  Lane l holds
+// channels (l % CH) * 8 .. + 7 (CH = D / 8 chunks per row) of rows
+// 16 w + (32 / CH) i + l / CH: each load and store instruction of the warp
+// covers 32 / CH whole rows.  The group maximum of |x| is taken on the bf16
+// values (exact, NaN-ignoring like fmaxf): the same values and roundings as
+// prep_q below, in fewer instructions.
 template <int D>
 __device__ __forceinline__ void prep_q16(const uint16_t* __restrict__ q, int8_t* __restrict__ q8,
                                          float* __restrict__ q_scale, const Geom& g, int tile, int h, int b) {
-    constexpr int HALF = D / 2, NV = HALF / 8;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tl = warp * QGROUP + (lane >> 1), c0 = (lane & 1) * HALF;
-    const int tok = tile * QTILE + tl;
+    constexpr int CH = D / 8, RPI = 32 / CH, NV = QGROUP / RPI;  // rows per instruction, rows per lane
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, ch = lane % CH;
+    const int r0 = warp * QGROUP + lane / CH;  // the lane's first row in the tile
     const long long bh = (long long)b * g.heads + h;
-    const uint16_t* src = q + b * g.q_sb + (long long)tok * g.q_st + h * g.q_sh + c0;
+    const uint16_t* src = q + b * g.q_sb + h * g.q_sh + ch * 8;
     uint4 raw[NV];
 #pragma unroll
-    for (int j = 0; j < NV; j++) raw[j] = load8(src + j * 8, tok < g.tokens);
+    for (int j = 0; j < NV; j++) {
+        const int tok = tile * QTILE + r0 + j * RPI;
+        raw[j] = load8(src + (long long)tok * g.q_st, tok < g.tokens);
+    }
     uint32_t m2 = 0u;
 #pragma unroll
     for (int j = 0; j < NV; j++) {
@@ -139,8 +143,8 @@ __device__ __forceinline__ void prep_q16(const uint16_t* __restrict__ q, int8_t*
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-    int8_t* dst = q8 + (bh * g.tq_pad + tile * QTILE + tl) * D + c0;
     const bool fast = s8_fast(amax);
+    int8_t* dst = q8 + (bh * g.tq_pad + tile * QTILE + r0) * D + ch * 8;
 #pragma unroll
     for (int j = 0; j < NV; j++) {
         float f[8];
@@ -150,7 +154,7 @@ __device__ __forceinline__ void prep_q16(const uint16_t* __restrict__ q, int8_t*
         uint2 w;
         w.x = s8x4(__fmul_rn(f[0], inv), __fmul_rn(f[1], inv), __fmul_rn(f[2], inv), __fmul_rn(f[3], inv), fast);
         w.y = s8x4(__fmul_rn(f[4], inv), __fmul_rn(f[5], inv), __fmul_rn(f[6], inv), __fmul_rn(f[7], inv), fast);
-        *reinterpret_cast<uint2*>(dst + j * 8) = w;
+        *reinterpret_cast<uint2*>(dst + (long long)j * RPI * D) = w;
     }
     if (lane == 0)
         q_scale[bh * (g.tq_pad / QGROUP) + tile * (QTILE / QGROUP) + warp] = (amax * (1.0f / 127.0f)) * g.q_mul;
@@ -519,10 +523,12 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
             *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + 4 * m + i) * D + ch * 8) = w;
         }
         if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
-        // V: channel d's 64 keys are the 16 words of row d
-        for (int c = tid; c < D * 16; c += 256) {
-            const int d = c >> 4, w = c & 15;
-            *reinterpret_cast<uint32_t*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) = vw[d][w];
+        // V: channel d's 64 keys are the 16 words of row d, stored 16 keys
+        // (four words) at a time
+        for (int c = tid; c < D * 4; c += 256) {
+            const int d = c >> 2, w = 4 * (c & 3);
+            *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) =
+                make_uint4(vw[d][w], vw[d][w + 1], vw[d][w + 2], vw[d][w + 3]);
         }
         return;
     }
