@@ -658,6 +658,188 @@ __global__ void __launch_bounds__(256, SP_QUANT_KV_CTAS) sp_quant_kv(const uint1
                       gridDim.y - 1 - blockIdx.y, gridDim.z - 1 - blockIdx.z);
 }
 
+// ---------------------------------------------------------------- streaming K/V quantisation
+// sp_quant_kv for dense keys without QK LayerNorm (the common case) as a
+// persistent kernel: each CTA takes every gridDim.x-th 64-key block (newest
+// statistics tiles first, as sp_quant_kv) and copies the next block's K and
+// V rows into shared memory with cp.async while it quantises the current
+// one, so that loads stay in flight across blocks.  The arithmetic is
+// quant_kv_block's dense paths (one member per key), value for value.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int D>
+struct KvStream {
+    static constexpr int ROW = D * 2;                // bytes of one key row of one head
+    static constexpr int TILE = KBLOCK * ROW;        // one tensor's 64 keys
+    static constexpr int STAGE = 2 * TILE;           // K and V
+    static constexpr int DYN = 2 * STAGE + D * 17 * 4 + 16;  // two stages, the V transpose, kmax
+};
+
+template <int D>
+__global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __restrict__ k,
+                                                             const uint16_t* __restrict__ v,
+                                                             const float* __restrict__ stats, int8_t* __restrict__ k8,
+                                                             float* __restrict__ k_scale, uint8_t* __restrict__ v8,
+                                                             const Geom g) {
+    using S = KvStream<D>;
+    constexpr int CH = D / 8, TPI = 256 / CH, NI = KBLOCK / TPI;
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    uint32_t* scratch = reinterpret_cast<uint32_t*>(dyn_smem + 2 * S::STAGE);
+    unsigned* kmax = reinterpret_cast<unsigned*>(dyn_smem + 2 * S::STAGE + D * 17 * 4);
+    const int tid = threadIdx.x, lane = tid & 31, ch = tid % CH;
+    const int nblk = g.tk_pad / KBLOCK, total = g.batch * g.kv_heads * nblk;
+    auto decode = [&](int item, int& blk, int& h, int& b) {
+        const int idx = total - 1 - item;  // newest first
+        blk = idx % nblk;
+        h = (idx / nblk) % g.kv_heads;
+        b = idx / nblk / g.kv_heads;
+    };
+    auto issue = [&](int item, int stage) {
+        int blk, h, b;
+        decode(item, blk, h, b);
+        const uint32_t base = smem_u32(dyn_smem) + stage * S::STAGE;
+        for (int c = tid; c < KBLOCK * CH; c += 256) {
+            const int key = c / CH, cc = c % CH, j = blk * KBLOCK + key;
+            if (j < g.tk) {  // rows past the end are masked in the arithmetic
+                cp_async16(base + key * S::ROW + cc * 16, k + b * g.k_sb + (long long)j * g.k_st + h * g.k_sh + cc * 8);
+                cp_async16(base + S::TILE + key * S::ROW + cc * 16,
+                           v + b * g.v_sb + (long long)j * g.v_st + h * g.v_sh + cc * 8);
+            }
+        }
+        cp_async_commit();
+    };
+    int item = blockIdx.x;
+    if (item < total) issue(item, 0);
+    for (int n = 0; item < total; item += gridDim.x, n++) {
+        if (item + (int)gridDim.x < total) {
+            issue(item + gridDim.x, (n + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        if (tid == 0) *kmax = 0u;
+        __syncthreads();  // this stage's rows (all threads' copies) have landed
+        int blk, h, b;
+        decode(item, blk, h, b);
+        const long long bh = (long long)b * g.kv_heads + h;
+        const uint8_t* kt = dyn_smem + (n & 1) * S::STAGE;
+        const uint8_t* vt = kt + S::TILE;
+        float mk[8], mv[8], rv[8];
+        {
+            const float4* st = reinterpret_cast<const float4*>(stats + bh * 4 * D + ch * 8);
+            const float4 a0 = __ldg(st), a1 = __ldg(st + 1), b0 = __ldg(st + D / 4), b1 = __ldg(st + D / 4 + 1);
+            const float4 c0 = __ldg(st + 3 * D / 4), c1 = __ldg(st + 3 * D / 4 + 1);
+            mk[0] = a0.x; mk[1] = a0.y; mk[2] = a0.z; mk[3] = a0.w; mk[4] = a1.x; mk[5] = a1.y; mk[6] = a1.z; mk[7] = a1.w;
+            mv[0] = b0.x; mv[1] = b0.y; mv[2] = b0.z; mv[3] = b0.w; mv[4] = b1.x; mv[5] = b1.y; mv[6] = b1.z; mv[7] = b1.w;
+            rv[0] = c0.x; rv[1] = c0.y; rv[2] = c0.z; rv[3] = c0.w; rv[4] = c1.x; rv[5] = c1.y; rv[6] = c1.z; rv[7] = c1.w;
+        }
+        if (NI == 4) {
+            // thread (m, ch): keys 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7,
+            // each channel's 4 E4M3 bytes one word of the transposed tile
+            uint32_t (*vw)[17] = reinterpret_cast<uint32_t (*)[17]>(scratch);
+            const int m = tid / CH;
+            float kq[NI][8];
+            float amx = 0.f;
+            uint32_t word[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int i = 0; i < NI; i++) {
+                const bool ok = blk * KBLOCK + 4 * m + i < g.tk;
+                float fk[8], fv[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(kt + (4 * m + i) * S::ROW + ch * 16), fk);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(vt + (4 * m + i) * S::ROW + ch * 16), fv);
+                float vq[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
+                    amx = fmaxf(amx, fabsf(kq[i][e]));
+                    vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
+                    word[e] |= (two & 0xffu) << (8 * i);
+                    word[e + 1] |= (two >> 8) << (8 * i);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
+            if (lane == 0) atomicMax(kmax, __float_as_uint(amx));
+            __syncthreads();
+            const float km = __uint_as_float(*kmax);
+            const float inv = km > 0.f ? 127.0f / km : 0.f;
+            const bool fast = s8_fast(km);
+#pragma unroll
+            for (int i = 0; i < NI; i++) {
+                const float* f = kq[i];
+                uint2 w;
+                w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
+                w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv, fast);
+                *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + 4 * m + i) * D + ch * 8) = w;
+            }
+            if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
+            for (int c = tid; c < D * 4; c += 256) {
+                const int d = c >> 2, w = 4 * (c & 3);
+                *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) =
+                    make_uint4(vw[d][w], vw[d][w + 1], vw[d][w + 2], vw[d][w + 3]);
+            }
+        } else {
+            uint8_t (*vtr)[KBLOCK] = reinterpret_cast<uint8_t (*)[KBLOCK]>(scratch);
+            float kv[NI][8];
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < NI; i++) {
+                const int kl = tid / CH + i * TPI;
+                const bool ok = blk * KBLOCK + kl < g.tk;
+                float fk[8], fv[8], vq[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(kt + kl * S::ROW + ch * 16), fk);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(vt + kl * S::ROW + ch * 16), fv);
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
+                    amax = fmaxf(amax, fabsf(kv[i][e]));
+                    vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
+                    vtr[ch * 8 + e][kl] = (uint8_t)(two & 0xff);
+                    vtr[ch * 8 + e + 1][kl] = (uint8_t)(two >> 8);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            if (lane == 0) atomicMax(kmax, __float_as_uint(amax));
+            __syncthreads();
+            const float km = __uint_as_float(*kmax);
+            const float inv = km > 0.f ? 127.0f / km : 0.f;
+            const bool fast = s8_fast(km);
+#pragma unroll
+            for (int i = 0; i < NI; i++) {
+                const int kl = tid / CH + i * TPI;
+                const float* f = kv[i];
+                uint2 w;
+                w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
+                w.y = s8x4(f[4] * inv, f[5] * inv, f[6] * inv, f[7] * inv, fast);
+                *reinterpret_cast<uint2*>(k8 + (bh * g.tk_pad + blk * KBLOCK + kl) * D + ch * 8) = w;
+            }
+            if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
+            for (int c = tid; c < D * (KBLOCK / 16); c += 256) {
+                const int d = c / (KBLOCK / 16), part16 = c % (KBLOCK / 16);
+                *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + part16 * 16) =
+                    *reinterpret_cast<const uint4*>(&vtr[d][part16 * 16]);
+            }
+        }
+        __syncthreads();  // this stage and the transpose are free for the next blocks
+    }
+}
+
 // The reference's V layout for the bit gate: [b][g][tk_pad/64][D][64], keys
 // permuted within each 16 by vpos (sage_common.cu:151-155).
 __device__ __forceinline__ int vpos(int k) { return ((k >> 1) & 3) * 4 + ((k >> 3) << 1) + (k & 1); }
@@ -693,6 +875,23 @@ static cudaError_t prepare_d(const void* q, const void* k, const void* v, const 
         (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, buf.stats,
         buf.tiles_done, g, q_role);
     if (!buf.tiles_done) sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
+    if (g.merge == 1 && !(g.flags & LN_K)) {
+        using S = KvStream<D>;
+        static int ctas = 0;
+        static std::once_flag once;
+        std::call_once(once, [] {
+            int dev = 0, sms = 0, per = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaFuncSetAttribute(sp_quant_kv_stream<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::DYN);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, sp_quant_kv_stream<D>, 256, S::DYN);
+            ctas = sms * (per > 0 ? per : 1);
+        });
+        const int total = g.batch * g.kv_heads * (g.tk_pad / KBLOCK);
+        sp_quant_kv_stream<D><<<total < ctas ? total : ctas, 256, S::DYN, st>>>(
+            (const uint16_t*)k, (const uint16_t*)v, buf.stats, buf.k8, buf.k_scale, buf.v8, g);
+        return cudaGetLastError();
+    }
     sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
     return cudaGetLastError();
