@@ -152,16 +152,19 @@ class ClockSampler:
             self.nv = None
             self.err = str(e)
 
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
     def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for name, bit in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            self._sample()
             time.sleep(0.002)
 
     def __enter__(self):
@@ -171,7 +174,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        # the caller synchronises before leaving the region: one last sample
+        # taken here still falls inside it, so short regions get two or more
         if self.nv is not None:
+            self._sample()
             self._stop.set()
             self.t.join()
 
