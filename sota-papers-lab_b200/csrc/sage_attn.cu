@@ -76,7 +76,11 @@ struct AttnSmem {
     static constexpr int V_OFF = K_OFF + KST * K_BYTES;
     static constexpr int P_OFF = V_OFF + VST * V_BYTES;
     static constexpr int M_OFF = P_OFF + 2 * P_BYTES;  // 4 KB of 1.5 * 2^23 for the S refill
-    static constexpr int END = M_OFF + 4096;
+    // (D = 64) each softmax warp's 16 output rows (bf16), padded by 16 bytes
+    // per row, so that the epilogue's global stores cover whole rows
+    static constexpr int STAGE_ROW = 2 * D + 16;
+    static constexpr int STAGE_OFF = M_OFF + 4096;
+    static constexpr int END = STAGE_OFF + (D == 64 ? NSOFTMAX_WARPS * 16 * STAGE_ROW : 0);
     static constexpr int DYN = END + 1024;  // slack to align the base to 1024
 };
 
@@ -515,7 +519,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (ok) ok = correct(J - 1, alpha_prev);  // the tile's last block
         if (PREFETCH) first_scales(tile_at(it + 1), qs_next, ks_next);  // (latency covered by the epilogue)
-        if (ok && !PARTIAL) {
+        if (ok && !PARTIAL && D == 64) {
+            // out = O / l * v_scale + v_mean for this lane's D/2 columns,
+            // written (bf16) into the warp's staging rows, then stored to
+            // the output four whole rows per warp instruction (D = 64: a
+            // tile's epilogue is a larger share of its few key blocks; at
+            // D = 128 the direct stores below measured faster)
+            const float inv = 1.0f / (l + __shfl_xor_sync(0xffffffffu, l, 16));
+            const float4* vmean4 = reinterpret_cast<const float4*>(stats + (long long)bh_kv * 4 * D + D + half * DH);
+            const float4* vscale4 = vmean4 + D / 4;
+            uint8_t* stage = dyn_smem + (sbase - smem_u32(dyn_smem)) + L::STAGE_OFF + (warp * 16) * L::STAGE_ROW;
+#pragma unroll
+            for (int c = 0; c < DH; c += 8) {
+                const float4 s0 = __ldg(vscale4 + c / 4), s1 = __ldg(vscale4 + c / 4 + 1);
+                const float4 m0 = __ldg(vmean4 + c / 4), m1 = __ldg(vmean4 + c / 4 + 1);
+                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+                uint32_t w[4];
+#pragma unroll
+                for (int e2 = 0; e2 < 4; e2++) {
+                    const int d = c + 2 * e2;
+                    const float y0 = fmaf(o[d] * inv, sv[2 * e2], mv[2 * e2]);
+                    const float y1 = fmaf(o[d + 1] * inv, sv[2 * e2 + 1], mv[2 * e2 + 1]);
+                    w[e2] = pack_bf16x2(y0, y1);
+                }
+                *reinterpret_cast<uint4*>(stage + (lane & 15) * L::STAGE_ROW + (half * DH + c) * 2) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            __syncwarp();
+            constexpr int CPR = 2 * D / 16, RPI = 32 / CPR;  // 16-byte chunks per row, rows per instruction
+            const int row0_ws = qrow_ws - (lane & 15);       // the warp's first row
+            uint16_t* obase = out + (long long)(bh_q / g.heads) * g.o_sb + (long long)(bh_q % g.heads) * g.o_sh;
+#pragma unroll
+            for (int i = 0; i < 16; i += RPI) {
+                const int rr = i + lane / CPR, cc = lane % CPR;
+                if (row0_ws + rr < g.tokens)
+                    *reinterpret_cast<uint4*>(obase + (long long)(row0_ws + rr) * g.o_st + cc * 8) =
+                        *reinterpret_cast<const uint4*>(stage + rr * L::STAGE_ROW + cc * 16);
+            }
+            __syncwarp();  // the staging rows are free for the next tile
+        }
+        if (ok && !PARTIAL && D == 128) {
             // out = O / l * v_scale + v_mean for this lane's D/2 columns
             const float inv = 1.0f / (l + __shfl_xor_sync(0xffffffffu, l, 16));
             const float* vmean = stats + (long long)bh_kv * 4 * D + D + half * DH;
