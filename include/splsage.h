@@ -196,9 +196,10 @@ int spl_sage_attn_resources(spl_sage* s, int* registers, int* spill_bytes);
  * [frame_len][head_dim/2][2] (cos, sin; RopeTable, qkv.rs:65-131) applied to
  * q and k with pairs (d, d ^ rope_half) (16 or 32 at head dim 64, 64 at 128),
  * table row = token % frame_len.  Writes q bf16 [batch][tokens][heads][D],
- * k and v bf16 [batch][tokens][kv_heads][D].  The q, k and v widths must be
- * multiples of 256 channels; every buffer, bias and RoPE table included,
- * 16-byte aligned. */
+ * k and v bf16 [batch][tokens][kv_heads][D].  The q + k + v width,
+ * (heads + 2*kv_heads)*head_dim, must be a multiple of 256 channels (one
+ * GEMM tile may hold heads of q, k and v); every buffer, bias and RoPE table
+ * included, 16-byte aligned. */
 typedef struct {
     int64_t batch;
     int64_t tokens;

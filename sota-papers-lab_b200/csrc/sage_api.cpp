@@ -613,10 +613,12 @@ static int qkv_setup(spl_sage* s, const spl_sage_qkv_shape* shape, const void* x
     const int64_t m = sh.batch * sh.tokens, n = (sh.heads + 2 * G) * D, kd = sh.hidden;
     if (sh.batch <= 0 || sh.tokens <= 0 || sh.heads <= 0 || kd <= 0)
         return fail(SPL_SAGE_ERR_INVALID, "qkv: empty shape");
-    if (n % 256 != 0 || (sh.heads * D) % 256 != 0 || (G * D) % 256 != 0)
+    // the epilogues route every head of a 256-channel tile to Q, K or V on
+    // its own, so only the whole width must fill whole tiles
+    if (n % 256 != 0)
         return fail(SPL_SAGE_ERR_INVALID,
-                    "qkv: q and k/v widths (%lld, %lld channels) must be multiples of 256 (the GEMM tile)",
-                    (long long)(sh.heads * D), (long long)(G * D));
+                    "qkv: the q + k + v width (%lld channels) must be a multiple of 256 (the GEMM tile)",
+                    (long long)n);
     if (kd % kmul != 0)
         return fail(SPL_SAGE_ERR_INVALID, "qkv: hidden size %lld must be a multiple of %d", (long long)kd, kmul);
     if (!fits_i32(m) || !fits_i32(n) || !fits_i32(kd)) return fail(SPL_SAGE_ERR_INVALID, "qkv: size does not fit i32");

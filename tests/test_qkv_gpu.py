@@ -35,6 +35,10 @@ CASES = {
     "vit_d64_norope": (2, 137, 1024, 16, 16, 64, None),
     "llama_d128_rope1d": (2, 200, 512, 4, 2, 128, "llama"),
     "vggt_d64_rope2d": (1, 3 * 75, 256, 4, 4, 64, "vggt"),
+    # one kv head (C4 sharded over 8 GPUs): a 256-channel tile holds a K and
+    # a V head; at D = 64 one tile holds Q, K and V heads
+    "llama_d128_kv1": (2, 200, 512, 4, 1, 128, "llama"),
+    "d64_q2_kv1": (1, 160, 256, 2, 1, 64, None),
 }
 
 
@@ -78,6 +82,7 @@ QUANT_CASES = {
     "fused_d128_rope1d": (2, 304, 512, 4, 2, 128, "llama", True),      # Q quantised in the epilogue
     "fused_d64_norope": (2, 256, 256, 4, 4, 64, None, True),
     "fused_d64_vggt": (1, 3 * 80, 256, 4, 4, 64, "vggt", True),
+    "fused_d128_kv1": (2, 304, 512, 4, 1, 128, "llama", True),        # the per-rank shape of C4 on 8 GPUs
     "unfused_ragged": (1, 300, 512, 4, 2, 128, "llama", True),         # tokens % 16 != 0: whole quantiser
     "unfused_1sm": (1, 304, 512, 4, 2, 128, "llama", False),
 }
