@@ -745,26 +745,40 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
             const int m = tid / CH;
             float kq[NI][8];
             float amx = 0.f;
-            uint32_t word[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-#pragma unroll
-            for (int i = 0; i < NI; i++) {
-                const bool ok = blk * KBLOCK + 4 * m + i < g.tk;
+            uint32_t two[NI][4];  // E4M3 pairs (channels 2p, 2p + 1) of each key
+            // key i of this thread's four; ok false: a key past the end (zeros)
+            auto key = [&](int i, bool ok) {
                 float fk[8], fv[8];
                 unpack_bf16x8(*reinterpret_cast<const uint4*>(kt + (4 * m + i) * S::ROW + ch * 16), fk);
                 unpack_bf16x8(*reinterpret_cast<const uint4*>(vt + (4 * m + i) * S::ROW + ch * 16), fv);
                 float vq[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    kq[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
+                    // fk - mk is the reference's fma(k, 1, -mean); it differs from
+                    // quant_kv_block's (0 + fk) only in the sign of a zero,
+                    // which no K byte or maximum sees
+                    kq[i][e] = ok ? fk[e] - mk[e] : 0.f;
                     amx = fmaxf(amx, fabsf(kq[i][e]));
                     vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
                 }
 #pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
-                    word[e] |= (two & 0xffu) << (8 * i);
-                    word[e + 1] |= (two >> 8) << (8 * i);
-                }
+                for (int p2 = 0; p2 < 4; p2++) two[i][p2] = e4m3x2(vq[2 * p2], vq[2 * p2 + 1]);
+            };
+            if (blk * KBLOCK + KBLOCK <= g.tk) {
+#pragma unroll
+                for (int i = 0; i < NI; i++) key(i, true);  // a whole block: no key masked
+            } else {
+#pragma unroll
+                for (int i = 0; i < NI; i++) key(i, blk * KBLOCK + 4 * m + i < g.tk);
+            }
+            // each channel's 4 bytes (keys 4m .. 4m + 3) into one word
+            uint32_t word[8];
+#pragma unroll
+            for (int p2 = 0; p2 < 4; p2++) {
+                word[2 * p2] = __byte_perm(__byte_perm(two[0][p2], two[1][p2], 0x0040),
+                                           __byte_perm(two[2][p2], two[3][p2], 0x0040), 0x5410);
+                word[2 * p2 + 1] = __byte_perm(__byte_perm(two[0][p2], two[1][p2], 0x0051),
+                                               __byte_perm(two[2][p2], two[3][p2], 0x0051), 0x5410);
             }
 #pragma unroll
             for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
