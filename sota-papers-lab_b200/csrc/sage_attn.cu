@@ -211,6 +211,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
+    // the set-up above may overlap the end of the quantiser launched before
+    // this kernel; everything below reads what it wrote
+    griddep_wait();
 
     // Every role walks the same tiles; J counts this CTA's 128-key blocks over
     // all its tiles and drives every ring index and phase, so the buffers
@@ -644,9 +647,10 @@ static cudaError_t attend_t(const AttnMaps& maps, const Buffers& buf, const Geom
     if (g.max_ctas > 0 && g.max_ctas < n_sm) n_sm = g.max_ctas;
     const long long ntiles = (long long)g.batch * g.heads * q_tiles;
     dim3 grid((unsigned)(ntiles < n_sm ? ntiles : n_sm));  // persistent: one CTA per SM
-    kern<<<grid, NTHREADS, AttnSmem<D>::DYN, st>>>(maps.q, maps.k, maps.v, buf.q_scale, buf.k_scale, buf.stats,
-                                                   buf.kbias, (uint16_t*)out, acc, lse, buf.err, g);
-    return cudaGetLastError();
+    cudaError_t e = launch_after_previous(kern, grid, dim3(NTHREADS), AttnSmem<D>::DYN, st, maps.q, maps.k, maps.v,
+                                          buf.q_scale, buf.k_scale, buf.stats, buf.kbias, (uint16_t*)out, acc, lse,
+                                          buf.err, g);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_attend(int d, const AttnMaps& maps, const Buffers& buf, const Geom& g, void* out,

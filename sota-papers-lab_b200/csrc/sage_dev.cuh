@@ -404,6 +404,16 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Programmatic dependent launch.  griddep_wait: wait until the kernel this
+// one was launched after (with cudaLaunchAttributeProgrammaticStreamSerialization)
+// has completed and its writes are visible; without such a predecessor it
+// returns at once.  griddep_launch_dependents: this CTA no longer holds back
+// the start of that next kernel (which starts once every CTA of this grid
+// has said so or exited; it still waits for this grid's completion before
+// it reads anything this grid writes).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -51,6 +51,25 @@ struct Geom {
 //   kbias   f32 [tk_pad]                  log2(count) or -inf (merge only)
 //   part    f32 [b][g][q_tiles][4][D]     per-tile channel statistics
 //   err     u32 [1]                       device error word
+// Launches kern with programmatic stream serialization: it may start while
+// the previous kernel on the stream finishes; it must call griddep_wait
+// before it reads anything that kernel writes.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_after_previous(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem,
+                                         cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, ((Params)args)...);
+}
+
 struct Buffers {
     int8_t* q8;
     float* q_scale;

@@ -376,6 +376,10 @@ __global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q
     // statistics role of every (batch, kv head), so that the K and V tiles
     // are the last inputs read (sp_quant_kv reads them again, newest first,
     // while they are still in L2)
+    // the next launch (sp_quant_kv_stream) may start once every CTA of this
+    // grid has started; it waits for this grid's end before it reads the
+    // statistics
+    griddep_launch_dependents();
     const int tile = blockIdx.x, y = blockIdx.y + blockIdx.z * gridDim.y;
     const int nq = q_role ? g.batch * g.heads : 0;
     if (y >= nq + g.batch * g.kv_heads) return;  // past the roles (grid y split over z)
@@ -714,8 +718,10 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
         cp_async_commit();
     };
     int item = blockIdx.x;
-    if (item < total) issue(item, 0);
+    if (item < total) issue(item, 0);  // K and V are inputs of the whole quantiser
+    griddep_wait();                    // the statistics come from sp_prep (or sp_finalize)
     for (int n = 0; item < total; item += gridDim.x, n++) {
+        if (item + (int)gridDim.x >= total) griddep_launch_dependents();  // this CTA's last block
         if (item + (int)gridDim.x < total) {
             issue(item + gridDim.x, (n + 1) & 1);
             cp_async_wait<1>();
@@ -902,9 +908,10 @@ static cudaError_t prepare_d(const void* q, const void* k, const void* v, const 
             ctas = sms * (per > 0 ? per : 1);
         });
         const int total = g.batch * g.kv_heads * (g.tk_pad / KBLOCK);
-        sp_quant_kv_stream<D><<<total < ctas ? total : ctas, 256, S::DYN, st>>>(
-            (const uint16_t*)k, (const uint16_t*)v, buf.stats, buf.k8, buf.k_scale, buf.v8, g);
-        return cudaGetLastError();
+        cudaError_t e = launch_after_previous(sp_quant_kv_stream<D>, dim3(total < ctas ? total : ctas), dim3(256),
+                                              S::DYN, st, (const uint16_t*)k, (const uint16_t*)v, buf.stats, buf.k8,
+                                              buf.k_scale, buf.v8, g);
+        return e != cudaSuccess ? e : cudaGetLastError();
     }
     sp_quant_kv<D><<<dim3(g.tk_pad / KBLOCK, g.kv_heads, g.batch), 256, 0, st>>>(
         (const uint16_t*)k, (const uint16_t*)v, ln, buf.stats, buf.k8, buf.k_scale, buf.v8, buf.kbias, g);
