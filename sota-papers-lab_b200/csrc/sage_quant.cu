@@ -13,12 +13,18 @@
 // gate) and the separate KV head count (GQA: Q and the K/V statistics run
 // as two roles of one launch).
 //
-// Three launches, all HBM-bound:
-//   sp_prep      grid (q_tiles, heads + kv_heads, batch); without its Q
-//                role (Q quantised in the QKV GEMM's epilogue) (q_tiles,
-//                kv_heads, batch)
-//   sp_finalize  grid (kv_heads, batch)
-//   sp_quant_kv  grid (tk_pad / 64, kv_heads, batch)
+// Launches, all HBM-bound:
+//   sp_prep             grid (q_tiles, batch * (heads + kv_heads)): every
+//                       Q role (none when the QKV GEMM's epilogue quantised
+//                       Q), then every K/V statistics role; with a workspace
+//                       the CTA that finishes a (batch, kv head)'s last tile
+//                       also reduces its statistics
+//   sp_finalize         grid (kv_heads, batch, D / 32): that reduction where
+//                       there is no workspace counter (the no-allocation call)
+//   sp_quant_kv_stream  dense keys without QK LayerNorm: persistent, one
+//                       64-key block after another, newest statistics first
+//   sp_quant_kv         grid (tk_pad / 64, kv_heads, batch): merged keys, QK
+//                       LayerNorm, context parallelism
 #include <mutex>
 
 #include "sage_dev.cuh"
