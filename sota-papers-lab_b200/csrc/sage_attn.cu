@@ -33,7 +33,7 @@
 //              tcgen05.mma kind::i8 M128 N128 into a double-buffered S;
 //              11: PV = tcgen05.mma kind::f8f6f4 M128 N=D with P from shared
 //              memory into a double-buffered PV
-// Per 16 keys, SP_EXP_POLY of the exponentials run on the FMA pipe
+// Per 16 keys, exp_poly<D>() of the exponentials run on the FMA pipe
 // (exp2_poly2) to take load off the MUFU unit.
 // Extensions not in the reference: causal masking (blocks past the diagonal
 // are skipped, the diagonal block masked) and GQA (q head h reads kv head
@@ -51,10 +51,18 @@ namespace sp {
 
 constexpr int KST = 3;   // K ring depth
 constexpr int VST = 3;   // V ring depth
-#ifndef SP_EXP_POLY
-#define SP_EXP_POLY 4
+// Of every 16 exponentials, how many run on the FMA pipe (exp2_poly2): 4 at
+// D = 128, 6 at D = 64, whose PV fold leaves the FMA pipe more room
+// (measured: C4 2.052 ms with 4 against 2.108 with 6; C2 0.1235 ms with 6
+// against 0.1271 with 4).
+#ifndef SP_EXP_POLY_128
+#define SP_EXP_POLY_128 4
 #endif
-constexpr int EXP_POLY = SP_EXP_POLY;  // of every 16 exponentials, how many run on the FMA pipe
+#ifndef SP_EXP_POLY_64
+#define SP_EXP_POLY_64 6
+#endif
+template <int D>
+constexpr int exp_poly() { return D == 64 ? SP_EXP_POLY_64 : SP_EXP_POLY_128; }
 constexpr int NTHREADS = 384;
 // One service thread per SM sub-partition (warp % 4), so that no pair of
 // softmax warps carries more issue load than another: K loads (and Q),
@@ -480,7 +488,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 for (int e = 0; e < 16; e += 2) {
                     float y0, y1;
                     upk2(fma2(pk2(x[c16 * 16 + e], x[c16 * 16 + e + 1]), sc2, off2), y0, y1);
-                    if (e < EXP_POLY) {
+                    if (e < exp_poly<D>()) {
                         exp2_poly2(y0, y1, p[e], p[e + 1]);
                     } else {
                         p[e] = ex2(y0);
