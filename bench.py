@@ -688,6 +688,9 @@ def run_ours(args, rank, world, local_rank):
             # the probe's rate is a burst at the maximum clock; the GEMM runs
             # long enough to meet the power cap: its rate at the clock it ran at
             qkv8["frac_of_peak_at_its_clock"] = round(qkv8["frac"] * gc["sm_max_mhz"] / gc["sm_mhz"], 4)
+        lib = qkv8["library_fp8_gemm"]
+        if "ms" in lib:  # > 1: ours (with its RoPE / bf16 scatter epilogue) is faster
+            lib["library_ms_over_ours"] = round(lib["ms"] / qkv8["gemm_ms"], 3)
         line["qkv_fp8"] = qkv8
     if ring_sub is not None:
         line["ring_c5"] = ring_sub
@@ -846,13 +849,50 @@ def qkv_fp8_time(eng, w, dev, stream, iters=30):
         clocks[name] = clk.summary()
     assert eng.engine_status() == 0
     flops = 2.0 * B * N * hidden * n_out
+    lib = library_fp8_gemm_time(x8, xs, w8, w_scale, iters, flops)
     ln_bytes = B * N * hidden * (2 + 1) + B * N * 4  # bf16 in, E4M3 out, scales
     return {"kernels": "sp_ln_fp8 (LN1 -> per-token E4M3) + sp_qkv_gemm_2sm<FP8> (tcgen05 kind::f8f6f4 on SM "
                        "pairs, token/channel scales + RoPE + bf16 epilogue)",
             "shape": f"[{B * N}x{hidden}] x [{n_out}x{hidden}]^T", "ln_ms": round(times["ln"], 4),
             "ln_gbs": round(ln_bytes / (times["ln"] * 1e-3) / 1e9, 1), "gemm_ms": round(times["gemm"], 4),
             "achieved": round(flops / (times["gemm"] * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "bound": "tensor",
-            "gemm_clocks": clocks["gemm"]}
+            "gemm_clocks": clocks["gemm"], "library_fp8_gemm": lib}
+
+
+def library_fp8_gemm_time(x8, xs, w8, w_scale, iters, flops):
+    """The same E4M3 product through torch._scaled_mm (a library FP8 GEMM,
+    cuBLASLt or torch's own kernels) on the same operands, bf16 out: with
+    the token / channel scales when the library takes them, else with one
+    scale per operand (the plain GEMM, no epilogue).  A comparison on the
+    same GPU, not part of the path."""
+    import torch
+    a = x8.view(torch.float8_e4m3fn)
+    b = w8.view(torch.float8_e4m3fn).t()  # [hidden][n_out], column-major
+    one = torch.ones((), dtype=torch.float32, device=x8.device)
+    forms = (("per-token x per-channel scales", lambda: torch._scaled_mm(
+                 a, b, scale_a=xs[:, None].contiguous(), scale_b=w_scale[None, :].contiguous(),
+                 out_dtype=torch.bfloat16)),
+             ("one scale per operand", lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one,
+                                                                 out_dtype=torch.bfloat16)))
+    for form, call in forms:
+        try:
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+        except Exception as e:  # the library lacks this form on this build
+            last = f"{type(e).__name__}: {str(e).splitlines()[0][:120]}"
+            continue
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            e0.record()
+            for _ in range(iters):
+                call()
+            e1.record()
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        return {"call": "torch._scaled_mm", "scales": form, "ms": round(ms, 4),
+                "achieved": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "clocks": clk.summary()}
+    return {"call": "torch._scaled_mm", "unavailable": last}
 
 
 # ---------------------------------------------------------------- CPU arms
