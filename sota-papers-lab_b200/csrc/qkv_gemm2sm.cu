@@ -28,14 +28,16 @@ constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 6;      // per CTA: 1
 constexpr int A_BYTES = BM * BK_BYTES, B_BYTES = (BN / 2) * BK_BYTES;  // each CTA holds half of B's rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
-// warps 0-3 load / MMA / idle, then the epilogue warps: eight for E4M3
-// (whose MMAs are fast enough for a four-warp epilogue to hold them up), four
-// for bf16 (C4: FP8 0.689 ms with eight, 0.722 with four; bf16 1.184 ms
-// with four, 1.200 with eight)
-template <bool FP8>
-constexpr int epilogue_warps() { return FP8 ? 8 : 4; }
-template <bool FP8>
-constexpr int nthreads() { return 128 + 32 * epilogue_warps<FP8>(); }
+// warps 0-3 load / MMA / idle, then EPW epilogue warps: eight where a
+// tile's MMAs are short enough for a four-warp epilogue to hold them up (E4M3,
+// and bf16 with K <= 2048 unless Q is quantised at D = 128, whose registers
+// do not fit 384 threads), else four (C4: FP8 0.689 ms with eight, 0.722
+// with four; bf16 1.184 ms with four, 1.200 with eight; C2, K = 1024: bf16
+// 0.0758 ms with four, 0.0645 with eight)
+constexpr int epilogue_warps(bool fp8, bool qq, int d, int k) {
+    return fp8 || (k <= 2048 && !(qq && d == 128)) ? 8 : 4;  // (Q quantised at D = 128: 64 packed values per thread)
+}
+constexpr int nthreads(int epw) { return 128 + 32 * epw; }
 }  // namespace gemm2
 
 namespace {
@@ -109,8 +111,8 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 
 }  // namespace
 
-template <int D, int HALF, bool FP8, bool QQ>
-__global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
+template <int D, int HALF, bool FP8, bool QQ, int EPW>
+__global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
     sp_qkv_gemm_2sm(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                     const uint16_t* __restrict__ bias, const float2* __restrict__ rope,
                     const float* __restrict__ x_scale, const float* __restrict__ w_scale, uint16_t* __restrict__ q_out,
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(acc_full[i]), 1);
-            mbar_init(bar(acc_empty[i]), 2 * epilogue_warps<FP8>());  // epilogue warps of both CTAs
+            mbar_init(bar(acc_empty[i]), 2 * EPW);  // epilogue warps of both CTAs
         }
         mbar_init(bar(done), 1);
         fence_barrier_init();
@@ -223,7 +225,6 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
         // all); a warp reads its own TMEM lane quarter (warp % 4), one thread
         // per row.  Columns go through 32 at a time, with their RoPE partners
         // (d + HALF) when HALF >= 32, so that only 64 floats are live.
-        constexpr int EPW = epilogue_warps<FP8>();
         constexpr int HEADS = (EPW == 8 ? BN / 2 : BN) / D;  // heads per epilogue warp
         const int quarter = warp & 3, chalf = EPW == 8 ? (warp - 4) >> 2 : 0;
         const int r = quarter * 32 + lane;
@@ -258,6 +259,14 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                                 (long long)head * D;
                 // columns c .. c+31 of the head: GEMM output, scales, bias
                 auto load = [&](int c, float (&x)[32]) {
+                    // the bias first (independent of TMEM), so that its
+                    // latency hides under the TMEM load's (hoisting the E4M3
+                    // channel scales too measured slower)
+                    uint4 braw[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        braw[i] = bias ? __ldg(reinterpret_cast<const uint4*>(bias + c0 + c + 8 * i))
+                                       : make_uint4(0, 0, 0, 0);
                     uint32_t v[32];
                     tmem_ld32(acc + hh * D + c, v);
                     tmem_wait_ld();
@@ -273,8 +282,7 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
 #pragma unroll
                             for (int e = 0; e < 8; e++) ws[e] = 1.0f;
                         }
-                        if (bias)
-                            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(bias + c0 + c + e8)), bs);
+                        unpack_bf16x8(braw[e8 / 8], bs);
 #pragma unroll
                         for (int e = 0; e < 8; e++) {
                             float y = __uint_as_float(v[e8 + e]);
@@ -284,8 +292,10 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
                                 if (bias) y = __fadd_rn(y, bs[e]);
                                 x[e8 + e] = y;
                             } else {
+                                // rounded to bf16 here only ahead of RoPE: the
+                                // stores (and Q's quantisation) round the same way
                                 if (bias) y += bs[e];
-                                x[e8 + e] = __uint_as_float(pack_bf16x2(y, 0.f) << 16);
+                                x[e8 + e] = HALF ? __uint_as_float(pack_bf16x2(y, 0.f) << 16) : y;
                             }
                         }
                     }
@@ -428,11 +438,11 @@ __global__ void __launch_bounds__(gemm2::nthreads<FP8>(), 1)
     if (warp == 1) tmem_dealloc_pair(tmem, 2 * BN);
 }
 
-template <int D, int HALF, bool FP8, bool QQ>
+template <int D, int HALF, bool FP8, bool QQ, int EPW>
 static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float* rope, const float* x_scale,
                           const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v, uint32_t* err,
                           const QkvGeom& g, cudaStream_t st) {
-    auto kern = sp_qkv_gemm_2sm<D, HALF, FP8, QQ>;
+    auto kern = sp_qkv_gemm_2sm<D, HALF, FP8, QQ, EPW>;
     static std::atomic<unsigned> attr_set{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
@@ -455,7 +465,7 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     if (pairs < 1) pairs = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs));
-    cfg.blockDim = dim3(gemm2::nthreads<FP8>());
+    cfg.blockDim = dim3(gemm2::nthreads(EPW));
     cfg.dynamicSmemBytes = gemm2::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1] = {};
@@ -468,20 +478,38 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     return cudaLaunchKernelEx(&cfg, kern, maps.x, maps.w, bias, (const float2*)rope, x_scale, w_scale, q, k, v, err, g);
 }
 
+template <bool FP8, bool QQ, int EPW>
+static cudaError_t qkv2_dispatch_epw(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
+                                     const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k,
+                                     uint16_t* v, uint32_t* err, const QkvGeom& g, cudaStream_t st) {
+    const int half = rope ? g.rope_half : 0;
+    if (d == 64) {
+        if (half == 0) return qkv2_t<64, 0, FP8, QQ, EPW>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 16) return qkv2_t<64, 16, FP8, QQ, EPW>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 32) return qkv2_t<64, 32, FP8, QQ, EPW>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        return cudaErrorInvalidValue;
+    }
+    if constexpr (QQ && EPW == 8) {
+        return cudaErrorInvalidValue;  // never chosen (epilogue_warps)
+    } else {
+        if (half == 0) return qkv2_t<128, 0, FP8, QQ, EPW>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        if (half == 64)
+            return qkv2_t<128, 64, FP8, QQ, EPW>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        return cudaErrorInvalidValue;
+    }
+}
+
 template <bool FP8, bool QQ>
 static cudaError_t qkv2_dispatch(int d, const QkvMaps& maps, const uint16_t* bias, const float* rope,
                                  const float* x_scale, const float* w_scale, uint16_t* q, uint16_t* k, uint16_t* v,
                                  uint32_t* err, const QkvGeom& g, cudaStream_t st) {
-    const int half = rope ? g.rope_half : 0;
-    if (d == 64) {
-        if (half == 0) return qkv2_t<64, 0, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-        if (half == 16) return qkv2_t<64, 16, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-        if (half == 32) return qkv2_t<64, 32, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-        return cudaErrorInvalidValue;
+    if constexpr (FP8) {
+        return qkv2_dispatch_epw<FP8, QQ, 8>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+    } else {
+        if (gemm2::epilogue_warps(FP8, QQ, d, g.k) == 8)
+            return qkv2_dispatch_epw<FP8, QQ, 8>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
+        return qkv2_dispatch_epw<FP8, QQ, 4>(d, maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
     }
-    if (half == 0) return qkv2_t<128, 0, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-    if (half == 64) return qkv2_t<128, 64, FP8, QQ>(maps, bias, rope, x_scale, w_scale, q, k, v, err, g, st);
-    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_qkv_gemm_2sm(int d, bool fp8, const QkvMaps& maps, const uint16_t* bias, const float* rope,
