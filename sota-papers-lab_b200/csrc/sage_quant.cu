@@ -246,14 +246,22 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
         vmn[e] = 3.0e38f;
         vmx[e] = -3.0e38f;
     }
-    // K, then V: each a pass of loads issued first, then summed in token
-    // order (the K and V statistics are independent accumulations)
-    uint4 raw[NI];
+    // the K loads and the first NV0 V loads issued together (the rest of V
+    // once K's registers are free: all of it would spill at D = 128), then
+    // K and V each summed in token order (independent accumulations)
+    constexpr int NV0 = NI <= 4 ? NI : NI / 2;
+    uint4 raw[NI], rawv[NI];
+    auto load_v = [&](int i) {
+        const int tok = tile * QTILE + tid / CH + i * TPI;
+        rawv[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, tok < g.tokens);
+    };
 #pragma unroll
     for (int i = 0; i < NI; i++) {
         const int tok = tile * QTILE + tid / CH + i * TPI;
         raw[i] = load8(k + b * g.k_sb + (long long)tok * g.k_st + h * g.k_sh + ch * 8, tok < g.tokens);
     }
+#pragma unroll
+    for (int i = 0; i < NV0; i++) load_v(i);
     if (g.flags & LN_K) {
 #pragma unroll
         for (int i = 0; i < NI; i++) {
@@ -281,8 +289,10 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
 #pragma unroll
         for (int p2 = 0; p2 < 4; p2++) upk2(k2[p2], ks[2 * p2], ks[2 * p2 + 1]);
     }
+#pragma unroll
+    for (int i = NV0; i < NI; i++) load_v(i);
     // the K sums through the lane butterfly now, so they need no registers
-    // during the V pass
+    // during the V sums
 #pragma unroll
     for (int o = CH; o < 32; o <<= 1) {
 #pragma unroll
@@ -291,11 +301,6 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
     if (lane < CH) {
 #pragma unroll
         for (int e = 0; e < 8; e++) red[warp][0][ch * 8 + e] = ks[e];
-    }
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int tok = tile * QTILE + tid / CH + i * TPI;
-        raw[i] = load8(v + b * g.v_sb + (long long)tok * g.v_st + h * g.v_sh + ch * 8, tok < g.tokens);
     }
     {
         // sums as packed pairs (the same order and roundings); minimum and
@@ -307,7 +312,7 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
 #pragma unroll
         for (int i = 0; i < NI; i++) {
             if (tile * QTILE + tid / CH + i * TPI < g.tokens) {
-                const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+                const uint32_t w[4] = {rawv[i].x, rawv[i].y, rawv[i].z, rawv[i].w};
 #pragma unroll
                 for (int p2 = 0; p2 < 4; p2++) {
                     v2[p2] = add2(v2[p2], bf2_to_f2(w[p2]));
@@ -728,6 +733,14 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
     griddep_wait();                    // the statistics come from sp_prep (or sp_finalize)
     for (int n = 0; item < total; item += gridDim.x, n++) {
         if (item + (int)gridDim.x >= total) griddep_launch_dependents();  // this CTA's last block
+        int blk, h, b;
+        decode(item, blk, h, b);
+        const long long bh = (long long)b * g.kv_heads + h;
+        // the slice's statistics requested before the wait for its rows, so
+        // that the two latencies overlap
+        const float4* st = reinterpret_cast<const float4*>(stats + bh * 4 * D + ch * 8);
+        const float4 a0 = __ldg(st), a1 = __ldg(st + 1), b0 = __ldg(st + D / 4), b1 = __ldg(st + D / 4 + 1);
+        const float4 c0 = __ldg(st + 3 * D / 4), c1 = __ldg(st + 3 * D / 4 + 1);
         if (item + (int)gridDim.x < total) {
             issue(item + gridDim.x, (n + 1) & 1);
             cp_async_wait<1>();
@@ -736,16 +749,10 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
         }
         if (tid == 0) *kmax = 0u;
         __syncthreads();  // this stage's rows (all threads' copies) have landed
-        int blk, h, b;
-        decode(item, blk, h, b);
-        const long long bh = (long long)b * g.kv_heads + h;
         const uint8_t* kt = dyn_smem + (n & 1) * S::STAGE;
         const uint8_t* vt = kt + S::TILE;
         float mk[8], mv[8], rv[8];
         {
-            const float4* st = reinterpret_cast<const float4*>(stats + bh * 4 * D + ch * 8);
-            const float4 a0 = __ldg(st), a1 = __ldg(st + 1), b0 = __ldg(st + D / 4), b1 = __ldg(st + D / 4 + 1);
-            const float4 c0 = __ldg(st + 3 * D / 4), c1 = __ldg(st + 3 * D / 4 + 1);
             mk[0] = a0.x; mk[1] = a0.y; mk[2] = a0.z; mk[3] = a0.w; mk[4] = a1.x; mk[5] = a1.y; mk[6] = a1.z; mk[7] = a1.w;
             mv[0] = b0.x; mv[1] = b0.y; mv[2] = b0.z; mv[3] = b0.w; mv[4] = b1.x; mv[5] = b1.y; mv[6] = b1.z; mv[7] = b1.w;
             rv[0] = c0.x; rv[1] = c0.y; rv[2] = c0.z; rv[3] = c0.w; rv[4] = c1.x; rv[5] = c1.y; rv[6] = c1.z; rv[7] = c1.w;
