@@ -446,12 +446,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float x[64];
             const int key0 = j * BLK + half * 64;
             if (MERGE) {
+                // this lane's 64 key biases as 16-byte loads (key0 and
+                // tk_pad are multiples of 64, the workspace 256-byte aligned)
                 const float c0 = -MAGIC_F * sc;
+                const bool in = key0 < g.tk_pad;
+                const float4* kb4 = reinterpret_cast<const float4*>(kbias + (in ? key0 : 0));
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const int key = key0 + c;
-                    const float kb = key < g.tk_pad ? __ldg(kbias + key) : __int_as_float(0xff800000);
-                    x[c] = fmaf(__uint_as_float(sr[c]), sc, kb + c0);
+                for (int c = 0; c < 64; c += 4) {
+                    const float ninf = __int_as_float(0xff800000);
+                    const float4 kb = in ? __ldg(kb4 + c / 4) : make_float4(ninf, ninf, ninf, ninf);
+                    x[c] = fmaf(__uint_as_float(sr[c]), sc, kb.x + c0);
+                    x[c + 1] = fmaf(__uint_as_float(sr[c + 1]), sc, kb.y + c0);
+                    x[c + 2] = fmaf(__uint_as_float(sr[c + 2]), sc, kb.z + c0);
+                    x[c + 3] = fmaf(__uint_as_float(sr[c + 3]), sc, kb.w + c0);
                 }
             } else {
 #pragma unroll
