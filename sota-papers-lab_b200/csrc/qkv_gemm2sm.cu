@@ -27,7 +27,11 @@ namespace gemm2 {
 constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 6;      // per CTA: 128 rows of the 256-row tile
 constexpr int A_BYTES = BM * BK_BYTES, B_BYTES = (BN / 2) * BK_BYTES;  // each CTA holds half of B's rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+// each epilogue warp stages its 32 rows x 32 channels (bf16) in rows of 80
+// bytes (64 + 16 of padding: conflict-free 16-byte writes), so that the
+// global stores cover 64 contiguous bytes per row, 8 rows per instruction
+constexpr int STG_ROW = 80, STG_WARP = 32 * STG_ROW;
+constexpr int smem_bytes(int epw) { return STAGES * STAGE_BYTES + 1024 + epw * STG_WARP; }
 // warps 0-3 load / MMA / idle, then EPW epilogue warps: eight where a
 // tile's MMAs are short enough for a four-warp epilogue to hold them up (E4M3,
 // and bf16 with K <= 2048 unless Q is quantised at D = 128, whose registers
@@ -229,6 +233,7 @@ __global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
         const int quarter = warp & 3, chalf = EPW == 8 ? (warp - 4) >> 2 : 0;
         const int r = quarter * 32 + lane;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        uint8_t* stg = dyn_smem + (sbase - smem_u32(dyn_smem)) + STAGES * STAGE_BYTES + (warp - 4) * STG_WARP;
         bool ok = true;
         for (int t = pair, it = 0; t < ntiles && ok; t += npairs, it++) {
             const int ab = it & 1;
@@ -254,9 +259,10 @@ __global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
                     part = 2;
                     head = (c0 - (g.hq + g.hkv) * D) / D;
                 }
-                uint16_t* dst = (part == 0 ? q_out : part == 1 ? k_out : v_out) +
-                                ((long long)bb * g.tokens + tok) * (long long)(part == 0 ? g.hq : g.hkv) * D +
-                                (long long)head * D;
+                // row r of q / k / v starts at r * (heads of the part) * D: the
+                // flattened row index is batch * tokens + token
+                const long long rstride = (long long)(part == 0 ? g.hq : g.hkv) * D;
+                uint16_t* dst_head = (part == 0 ? q_out : part == 1 ? k_out : v_out) + (long long)head * D;
                 // columns c .. c+31 of the head: GEMM output, scales, bias
                 auto load = [&](int c, float (&x)[32]) {
                     // the bias first (independent of TMEM), so that its
@@ -300,8 +306,9 @@ __global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
                         }
                     }
                 };
+                // columns c .. c+31 of the warp's 32 rows: each lane's row into
+                // the staging rows, then 16 bytes per lane, 4 lanes per row
                 auto store = [&](int c, const float (&x)[32]) {
-                    if (row >= g.m) return;
 #pragma unroll
                     for (int e = 0; e < 32; e += 8) {
                         uint4 w;
@@ -309,8 +316,18 @@ __global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
                         w.y = pack_bf16x2(x[e + 2], x[e + 3]);
                         w.z = pack_bf16x2(x[e + 4], x[e + 5]);
                         w.w = pack_bf16x2(x[e + 6], x[e + 7]);
-                        *reinterpret_cast<uint4*>(dst + c + e) = w;
+                        *reinterpret_cast<uint4*>(stg + lane * STG_ROW + e * 2) = w;
                     }
+                    __syncwarp();
+                    const int row0 = row - lane, q16 = lane & 3;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        const int rr = i + (lane >> 2);
+                        if (row0 + rr < g.m)
+                            *reinterpret_cast<uint4*>(dst_head + (long long)(row0 + rr) * rstride + c + q16 * 8) =
+                                *reinterpret_cast<const uint4*>(stg + rr * STG_ROW + q16 * 16);
+                    }
+                    __syncwarp();
                 };
                 // RoPE on (a, b) with the table entries of channels d, d + 1
                 auto rot2 = [&](int d, float& a0, float& b0, float& a1, float& b1) {
@@ -447,7 +464,7 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 32 || !(attr_set.load(std::memory_order_acquire) & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::smem_bytes(EPW));
         if (e != cudaSuccess) return e;
         if (dev < 32) attr_set.fetch_or(1u << dev, std::memory_order_release);
     }
@@ -466,7 +483,7 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs));
     cfg.blockDim = dim3(gemm2::nthreads(EPW));
-    cfg.dynamicSmemBytes = gemm2::SMEM;
+    cfg.dynamicSmemBytes = gemm2::smem_bytes(EPW);
     cfg.stream = st;
     cudaLaunchAttribute attr[1] = {};
     attr[0].id = cudaLaunchAttributeClusterDimension;
