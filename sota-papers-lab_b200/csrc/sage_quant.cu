@@ -377,8 +377,9 @@ __device__ __forceinline__ void prep_stats(const uint16_t* __restrict__ k, const
     if (tid == 0) tiles_done[bh] = 0u;
 }
 
+// four CTAs per SM at D = 64 (64 registers suffice there), three at D = 128
 template <int D>
-__global__ void __launch_bounds__(256, 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+__global__ void __launch_bounds__(256, D == 64 ? 4 : 3) sp_prep(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
                                                const uint16_t* __restrict__ v, const float* __restrict__ ln,
                                                int8_t* __restrict__ q8, float* __restrict__ q_scale,
                                                float* __restrict__ part, float* __restrict__ stats,
