@@ -109,8 +109,12 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, 
         : "memory");
 }
 
+// Relaxed: the epilogue's accumulator reads have completed (tcgen05.wait::ld,
+// then tcgen05.fence::before_thread_sync) before the arrival, and the MMA
+// thread that waits on it reads nothing the epilogue writes, so no release
+// of the epilogue's global stores (a wait for them to drain) is needed.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
 }  // namespace
