@@ -9,12 +9,14 @@
 // stage barrier, which the leader arms for both halves), warp 1 owns TMEM
 // (allocated for the pair) and, in the leader (cluster rank 0), issues the
 // MMAs, whose commits arrive on the stage and accumulator barriers of both
-// CTAs; the epilogue warps (4-11 for E4M3, 4-7 for bf16) read their own
-// CTA's accumulator (rows rank * 128 + quarter * 32 + lane; with eight,
-// warps 4-7 take channels 0-127 of the tile and warps 8-11 channels 128-255)
-// and run the epilogue of qkv_gemm.cu (for spl_sage_qkv_gemm_quant also
-// quantising Q to INT8 with its 16-row scales, so that the quantiser only
-// reads K and V), then tell the leader the accumulator is free.  Every mbarrier wait is bounded; both CTAs always
+// CTAs; the epilogue warps (4-11, or 4-7 for bf16 with K > 2048 or Q
+// quantised at D = 128) read their own CTA's accumulator (rows rank * 128 +
+// quarter * 32 + lane; with eight, warps 4-7 take channels 0-127 of the tile
+// and warps 8-11 channels 128-255) and run the arithmetic of qkv_gemm.cu's
+// epilogue (for spl_sage_qkv_gemm_quant also quantising Q to INT8 with its
+// 16-row scales, so that the quantiser only reads K and V), storing through
+// shared memory 64 contiguous bytes per row, then tell the leader the
+// accumulator is free.  Every mbarrier wait is bounded; both CTAs always
 // reach the closing cluster barrier, after which TMEM is freed.
 #include <atomic>
 
