@@ -697,7 +697,7 @@ struct KvStream {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __restrict__ k,
+__global__ void __launch_bounds__(256, D == 64 ? 4 : 3) sp_quant_kv_stream(const uint16_t* __restrict__ k,
                                                              const uint16_t* __restrict__ v,
                                                              const float* __restrict__ stats, int8_t* __restrict__ k8,
                                                              float* __restrict__ k_scale, uint8_t* __restrict__ v8,
@@ -758,7 +758,7 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
             mv[0] = b0.x; mv[1] = b0.y; mv[2] = b0.z; mv[3] = b0.w; mv[4] = b1.x; mv[5] = b1.y; mv[6] = b1.z; mv[7] = b1.w;
             rv[0] = c0.x; rv[1] = c0.y; rv[2] = c0.z; rv[3] = c0.w; rv[4] = c1.x; rv[5] = c1.y; rv[6] = c1.z; rv[7] = c1.w;
         }
-        if (NI == 4) {
+        if constexpr (NI == 4) {
             // thread (m, ch): keys 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7,
             // each channel's 4 E4M3 bytes one word of the transposed tile
             uint32_t (*vw)[17] = reinterpret_cast<uint32_t (*)[17]>(scratch);
@@ -824,29 +824,33 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
                     make_uint4(vw[d][w], vw[d][w + 1], vw[d][w + 2], vw[d][w + 3]);
             }
         } else {
-            uint8_t (*vtr)[KBLOCK] = reinterpret_cast<uint8_t (*)[KBLOCK]>(scratch);
+            static_assert(NI == 2, "D = 64: two keys per thread");
+            // thread (m, ch): keys 2m and 2m + 1 of channels ch*8 .. ch*8 + 7;
+            // each channel's two E4M3 bytes one 16-bit element of the
+            // transposed tile, whose rows of 33 elements (66 bytes) put the
+            // eight channel chunks of a warp's store in different banks
+            constexpr int TROW = KBLOCK / 2 + 1;
+            uint16_t (*vt16)[TROW] = reinterpret_cast<uint16_t (*)[TROW]>(scratch);
+            const int m = tid / CH;
             float kv[NI][8];
             float amax = 0.f;
+            float vq[NI][8];
 #pragma unroll
             for (int i = 0; i < NI; i++) {
-                const int kl = tid / CH + i * TPI;
+                const int kl = 2 * m + i;
                 const bool ok = blk * KBLOCK + kl < g.tk;
-                float fk[8], fv[8], vq[8];
+                float fk[8], fv[8];
                 unpack_bf16x8(*reinterpret_cast<const uint4*>(kt + kl * S::ROW + ch * 16), fk);
                 unpack_bf16x8(*reinterpret_cast<const uint4*>(vt + kl * S::ROW + ch * 16), fv);
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
                     kv[i][e] = ok ? fmaf(0.f + fk[e], 1.0f, -mk[e]) : 0.f;
                     amax = fmaxf(amax, fabsf(kv[i][e]));
-                    vq[e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
-                }
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    const uint32_t two = e4m3x2(vq[e], vq[e + 1]);
-                    vtr[ch * 8 + e][kl] = (uint8_t)(two & 0xff);
-                    vtr[ch * 8 + e + 1][kl] = (uint8_t)(two >> 8);
+                    vq[i][e] = ok ? fmaf(0.f + fv[e], 1.0f, -mv[e]) * rv[e] : 0.f;
                 }
             }
+#pragma unroll
+            for (int e = 0; e < 8; e++) vt16[ch * 8 + e][m] = (uint16_t)e4m3x2(vq[0][e], vq[1][e]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             if (lane == 0) atomicMax(kmax, __float_as_uint(amax));
@@ -856,7 +860,7 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
             const bool fast = s8_fast(km);
 #pragma unroll
             for (int i = 0; i < NI; i++) {
-                const int kl = tid / CH + i * TPI;
+                const int kl = 2 * m + i;
                 const float* f = kv[i];
                 uint2 w;
                 w.x = s8x4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv, fast);
@@ -866,8 +870,13 @@ __global__ void __launch_bounds__(256, 3) sp_quant_kv_stream(const uint16_t* __r
             if (tid == 0) k_scale[bh * nblk + blk] = km * (1.0f / 127.0f);
             for (int c = tid; c < D * (KBLOCK / 16); c += 256) {
                 const int d = c / (KBLOCK / 16), part16 = c % (KBLOCK / 16);
-                *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + part16 * 16) =
-                    *reinterpret_cast<const uint4*>(&vtr[d][part16 * 16]);
+                const uint16_t* src = &vt16[d][part16 * 8];
+                uint4 w;
+                w.x = (uint32_t)src[0] | ((uint32_t)src[1] << 16);
+                w.y = (uint32_t)src[2] | ((uint32_t)src[3] << 16);
+                w.z = (uint32_t)src[4] | ((uint32_t)src[5] << 16);
+                w.w = (uint32_t)src[6] | ((uint32_t)src[7] << 16);
+                *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + part16 * 16) = w;
             }
         }
         __syncthreads();  // this stage and the transpose are free for the next blocks
