@@ -32,6 +32,13 @@
 
 namespace sp {
 
+// The transposed V tile at D = 128 (vw[D][17]: per channel, 16 words of four
+// keys' E4M3 bytes): key group w of channel d is kept in column
+// (w + 2 * (d / 32)) mod 16, so that the 32 lanes of a warp (16 channel
+// chunks x 2 key groups) store to 32 different banks (unswizzled, channel
+// chunks ch, ch + 4, ch + 8, ch + 12 met in one bank).
+__device__ __forceinline__ int vw_col(int w, int d) { return (w + 2 * (d >> 5)) & 15; }
+
 __device__ __forceinline__ uint4 load8(const uint16_t* p, bool ok) {
     return ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
 }
@@ -485,7 +492,7 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
         // Dense keys, D = 128: thread (m, ch) takes the 4 consecutive keys
         // 4m .. 4m + 3 of channels ch*8 .. ch*8 + 7, so that each channel's
         // 4 E4M3 bytes form one 32-bit word of the transposed tile (rows of
-        // 17 words: at most 4-way bank conflicts).  Every load first; one
+        // 17 words, key groups in swizzled columns: vw_col).  Every load first; one
         // member per key, so ksum = 0 + k and rc = 1 exactly: the same
         // arithmetic as the general path.
         __shared__ uint32_t vw[D][17];
@@ -522,7 +529,7 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
             }
         }
 #pragma unroll
-        for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
+        for (int e = 0; e < 8; e++) vw[ch * 8 + e][vw_col(m, ch * 8)] = word[e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
         if (lane == 0) atomicMax(&kmax, __float_as_uint(amx));
@@ -544,7 +551,8 @@ __device__ __forceinline__ void quant_kv_block(const uint16_t* __restrict__ k, c
         for (int c = tid; c < D * 4; c += 256) {
             const int d = c >> 2, w = 4 * (c & 3);
             *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) =
-                make_uint4(vw[d][w], vw[d][w + 1], vw[d][w + 2], vw[d][w + 3]);
+                make_uint4(vw[d][vw_col(w, d)], vw[d][vw_col(w + 1, d)], vw[d][vw_col(w + 2, d)],
+                           vw[d][vw_col(w + 3, d)]);
         }
         return;
     }
@@ -801,7 +809,7 @@ __global__ void __launch_bounds__(256, D == 64 ? 4 : 3) sp_quant_kv_stream(const
                                                __byte_perm(two[2][p2], two[3][p2], 0x0051), 0x5410);
             }
 #pragma unroll
-            for (int e = 0; e < 8; e++) vw[ch * 8 + e][m] = word[e];
+            for (int e = 0; e < 8; e++) vw[ch * 8 + e][vw_col(m, ch * 8)] = word[e];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
             if (lane == 0) atomicMax(kmax, __float_as_uint(amx));
@@ -821,7 +829,8 @@ __global__ void __launch_bounds__(256, D == 64 ? 4 : 3) sp_quant_kv_stream(const
             for (int c = tid; c < D * 4; c += 256) {
                 const int d = c >> 2, w = 4 * (c & 3);
                 *reinterpret_cast<uint4*>(v8 + (bh * D + d) * (long long)g.tk_pad + blk * KBLOCK + 4 * w) =
-                    make_uint4(vw[d][w], vw[d][w + 1], vw[d][w + 2], vw[d][w + 3]);
+                    make_uint4(vw[d][vw_col(w, d)], vw[d][vw_col(w + 1, d)], vw[d][vw_col(w + 2, d)],
+                           vw[d][vw_col(w + 3, d)]);
             }
         } else {
             static_assert(NI == 2, "D = 64: two keys per thread");
