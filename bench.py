@@ -281,6 +281,27 @@ def run_layers(args, rank, world, local_rank):
     ms_max = float(t.item())
     attn_ms = a0.elapsed_time(a1) / (args.steps * Lr)
 
+    # the projection alone (bf16 q/k/v out, no quantiser) against the
+    # library's linear on the same operands (bias, one [B*N][3072] output, no
+    # head scatter), each over the 24 layers' weights
+    def per_layer(call):
+        for i in range(Lr):
+            call(i)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            for i in range(Lr):
+                call(i)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        return g0.elapsed_time(g1) / (args.steps * Lr)
+
+    gemm_ms = per_layer(lambda i: eng.qkv_gemm(x, ws_w[i], ws_b[i], None, q, k, v, batch=B, tokens=N, heads=H))
+    y_lib = torch.empty(B * N, 3 * H * D, dtype=torch.bfloat16, device=dev)
+    lib_ms = per_layer(lambda i: torch.addmm(ws_b[i], x, ws_w[i].t(), out=y_lib))
+    del y_lib
+
     # end to end: each step's activations up from pinned host memory, the 24
     # layers, the last layer's attention output back to the host
     xh = x.cpu().pin_memory()
@@ -323,11 +344,17 @@ def run_layers(args, rank, world, local_rank):
                      "traffic": None, "attn_ms_per_layer": round(attn_ms, 4),
                      "layer_ms": round(step_ms / Lr, 4),
                      "peak_source": "measured in this run by the tcgen05 probe (lower of INT8, FP8 E4M3)"},
+        "qkv_gemm": {"kernel": "sp_qkv_gemm_2sm (bias, bf16 q/k/v scattered per head)",
+                     "shape": f"[{B * N}x{Hd}] x [{3 * H * D}x{Hd}]^T", "ms": round(gemm_ms, 4),
+                     "achieved": round(2.0 * B * N * Hd * 3 * H * D / (gemm_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                     "library_addmm_ms": round(lib_ms, 4),
+                     "library": "torch.addmm(bias, x, W^T) into one [B*N][3*H*D] bf16 output (cuBLASLt)",
+                     "library_ms_over_ours": round(lib_ms / gemm_ms, 3)},
         "e2e": {"value": round(eff / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS", "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
                 "api": "qkv_gemm_quant + attend via libsplsage C ABI, 24 layers per step, pinned host buffers"},
-        "gpu_launches": 3 * Lr * args.steps,  # per layer: GEMM, one-launch K/V quantiser, attention
+        "gpu_launches": 4 * Lr * args.steps,  # per layer: GEMM, quantiser (sp_prep, sp_quant_kv_stream), attention
         "clocks": clk.summary(),
         "device_error_word": word,
     }
@@ -668,7 +695,7 @@ def run_ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": d2h,
                 "api": "SageAttention.forward via libsplsage C ABI, pinned host buffers; uploads, compute and "
                        "downloads of consecutive steps overlapped on three streams (every rank its own share)"},
-        "gpu_launches": 2 * args.steps,  # per step: the one-launch quantiser, the attention
+        "gpu_launches": 3 * args.steps,  # per step: the quantiser (sp_prep, sp_quant_kv_stream), the attention
         "clocks": clk.summary(),
         "device_error_word": word,
     }
@@ -763,7 +790,7 @@ def c4_block_time(eng, wr, B, dev, stream, rank, world, max_over_ranks, iters=5)
             "tflops_gemm_plus_attention": round((gemm_flops + attn_flops) / (t_block * 1e-3) / 1e12, 1),
             "gemm_quant_ms": round(t_fused, 4), "unfused_gemm_then_quantiser_ms": round(t_unfused, 4),
             "q_round_trip_bytes_removed": B * N * full["heads"] * D * 2 // world * 2,
-            "gpu_launches_per_block": 3, "device_error_word": word}
+            "gpu_launches_per_block": 4, "device_error_word": word}  # GEMM, sp_prep, sp_quant_kv_stream, attention
 
 
 def qkv_gemm_time(eng, w, dev, stream, iters=30):
