@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(gemm2::nthreads(EPW), 1)
     cluster_sync();  // both CTAs' barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
+    // the set-up above may overlap the end of the kernel launched before this
+    // one (programmatic dependent launch); everything below reads or writes
+    // memory that kernel may use
+    griddep_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -491,13 +495,17 @@ static cudaError_t qkv2_t(const QkvMaps& maps, const uint16_t* bias, const float
     cfg.blockDim = dim3(gemm2::nthreads(EPW));
     cfg.dynamicSmemBytes = gemm2::smem_bytes(EPW);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1] = {};
+    cudaLaunchAttribute attr[2] = {};
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // may start while the previous kernel on the stream finishes (griddep_wait
+    // above keeps every memory access after that kernel's end)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, maps.x, maps.w, bias, (const float2*)rope, x_scale, w_scale, q, k, v, err, g);
 }
 

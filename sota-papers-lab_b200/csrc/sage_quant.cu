@@ -399,6 +399,9 @@ __global__ void __launch_bounds__(256, D == 64 ? 4 : 3) sp_prep(const uint16_t* 
     // grid has started; it waits for this grid's end before it reads the
     // statistics
     griddep_launch_dependents();
+    // this grid may itself start while the kernel before it (the QKV GEMM, the
+    // previous attention) finishes: nothing is read or written before its end
+    griddep_wait();
     const int tile = blockIdx.x, y = blockIdx.y + blockIdx.z * gridDim.y;
     const int nq = q_role ? g.batch * g.heads : 0;
     if (y >= nq + g.batch * g.kv_heads) return;  // past the roles (grid y split over z)
@@ -923,9 +926,10 @@ template <int D>
 static cudaError_t prepare_d(const void* q, const void* k, const void* v, const float* ln, const Buffers& buf,
                              const Geom& g, cudaStream_t st) {
     const int q_role = q != nullptr;
-    sp_prep<D><<<prep_grid(g, q_role), 256, 0, st>>>(
-        (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part, buf.stats,
-        buf.tiles_done, g, q_role);
+    cudaError_t e0 = launch_after_previous(sp_prep<D>, prep_grid(g, q_role), dim3(256), 0, st, (const uint16_t*)q,
+                                           (const uint16_t*)k, (const uint16_t*)v, ln, buf.q8, buf.q_scale, buf.part,
+                                           buf.stats, buf.tiles_done, g, q_role);
+    if (e0 != cudaSuccess) return e0;
     if (!buf.tiles_done) sp_finalize<D><<<dim3(g.kv_heads, g.batch, D / 32), 128, 0, st>>>(buf.part, buf.stats, g);
     if (g.merge == 1 && !(g.flags & LN_K)) {
         using S = KvStream<D>;
