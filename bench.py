@@ -303,18 +303,52 @@ def run_layers(args, rank, world, local_rank):
     del y_lib
 
     # end to end: each step's activations up from pinned host memory, the 24
-    # layers, the last layer's attention output back to the host
+    # layers, the last layer's attention output back to the host.  As a
+    # serving loop runs it: uploads on one stream into two alternating
+    # device buffers, the layers on the engine's stream, downloads of each
+    # step's last attention output (its own buffer per step parity) on a
+    # third, so one step's copies overlap its neighbours' layers; events
+    # order every reuse of a buffer.
     xh = x.cpu().pin_memory()
-    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    e_steps = max(1, min(args.steps, 3))
+    oh = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    xs = [torch.empty_like(x) for _ in range(2)]
+    lasts = [torch.empty_like(out) for _ in range(2)]
+    to_last = [sage.Tensor(t_, sage.Strides.bthd(N, H, D)) for t_ in lasts]
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev = lambda: torch.cuda.Event()  # noqa: E731 (ordering only)
+    e_steps = max(1, args.steps)
     barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(e_steps):
-        x.copy_(xh, non_blocking=True)
-        for i in range(Lr):
-            layer(i)
-        oh.copy_(out, non_blocking=True)
+    up.wait_event(e0)
+    down.wait_event(e0)
+    done_x, done_dl = [None, None], [None, None]
+    for s_ in range(e_steps):
+        p_ = s_ & 1
+        with torch.cuda.stream(up):
+            if done_x[p_] is not None:
+                up.wait_event(done_x[p_])  # step s - 2 has finished reading xs[p]
+            xs[p_].copy_(xh, non_blocking=True)
+            up_done = ev()
+            up_done.record(up)
+        stream.wait_event(up_done)
+        for i in range(Lr - 1):
+            eng.qkv_gemm_quant(ws, xs[p_], ws_w[i], ws_b[i], None, q, k, v)
+            eng.attend(ws, to)
+        eng.qkv_gemm_quant(ws, xs[p_], ws_w[Lr - 1], ws_b[Lr - 1], None, q, k, v)
+        if done_dl[p_] is not None:
+            stream.wait_event(done_dl[p_])  # step s - 2's output is on the host
+        eng.attend(ws, to_last[p_])
+        done_x[p_] = ev()
+        done_x[p_].record(stream)
+        with torch.cuda.stream(down):
+            down.wait_event(done_x[p_])
+            oh[p_].copy_(lasts[p_], non_blocking=True)
+            done_dl[p_] = ev()
+            done_dl[p_].record(down)
+    for d_ in done_dl:
+        if d_ is not None:
+            stream.wait_event(d_)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -353,7 +387,8 @@ def run_layers(args, rank, world, local_rank):
         "e2e": {"value": round(eff / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS", "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size(),
-                "api": "qkv_gemm_quant + attend via libsplsage C ABI, 24 layers per step, pinned host buffers"},
+                "api": "qkv_gemm_quant + attend via libsplsage C ABI, 24 layers per step, pinned host buffers; "
+                       "uploads, layers and downloads of consecutive steps overlapped on three streams"},
         "gpu_launches": 4 * Lr * args.steps,  # per layer: GEMM, quantiser (sp_prep, sp_quant_kv_stream), attention
         "clocks": clk.summary(),
         "device_error_word": word,
